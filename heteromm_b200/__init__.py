@@ -1,0 +1,11 @@
+"""heteromm_b200 — B200-native (sm_100a) kernels for the HeteroMM
+score -> select -> apply path, behind the C ABI in include/heteromm_cuda.h.
+
+Python is plumbing here (device memory, streams, torch.distributed); every
+operation runs in libheteromm_cuda.so.
+"""
+from ._abi import HmmError, last_error, load, lib_path  # noqa: F401
+from .flat import (ip_score_f32, ip_topk_bf16, ip_topk_f32, shard_merge_topk,  # noqa: F401
+                   threshold_bitmap_f32, topk_f32)
+
+__version__ = "0.1.0"

@@ -1,0 +1,82 @@
+"""ctypes binding of the C ABI in include/heteromm_cuda.h.
+
+The library is built in-tree (heteromm_b200/lib/libheteromm_cuda.so) by
+heteromm_b200.build.  Loading fails loudly when it is missing: there is no
+fallback implementation behind these entry points.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+from . import build as _build
+
+HMM_OK = 0
+STATUS_NAMES = {
+    0: "HMM_OK", 1: "HMM_ERR_INVALID", 2: "HMM_ERR_CUDA", 3: "HMM_ERR_OOM",
+    4: "HMM_ERR_BOUNDS", 5: "HMM_ERR_TIMEOUT", 6: "HMM_ERR_UNSUPPORTED",
+}
+
+_P = C.c_void_p
+_I = C.c_int64
+_F = C.c_float
+_S = C.c_size_t
+
+# name -> (restype, argtypes); mirrors include/heteromm_cuda.h
+SIGNATURES = {
+    "hmm_last_error": (C.c_char_p, []),
+    "hmm_version": (C.c_char_p, []),
+    "hmm_ip_score_f32": (C.c_int, [_P, _I, _I, _P, _I, _P, _P]),
+    "hmm_topk_f32_workspace_size": (_S, [_I, _I, _I]),
+    "hmm_topk_f32": (C.c_int, [_P, _I, _I, _I, _P, _P, _P, _S, _P]),
+    "hmm_threshold_bitmap_f32": (C.c_int, [_P, _I, _I, _F, _P, _P]),
+    "hmm_ip_topk_f32_workspace_size": (_S, [_I, _I, _I, _I]),
+    "hmm_ip_topk_f32": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _F, _P, _P, _S, _P]),
+    "hmm_ip_topk_bf16_workspace_size": (_S, [_I, _I, _I, _I]),
+    "hmm_ip_topk_bf16": (C.c_int, [_P, _I, _I, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
+    "hmm_shard_merge_topk_workspace_size": (_S, [_I, _I, _I]),
+    "hmm_shard_merge_topk": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
+}
+
+
+class HmmError(RuntimeError):
+    def __init__(self, status: int, where: str, msg: str):
+        super().__init__(f"{where}: {STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib_path() -> str:
+    return _build.CUDA_LIB
+
+
+def load(build_if_missing: bool = True) -> C.CDLL:
+    """Loads libheteromm_cuda.so (building it first if it is absent)."""
+    global _lib
+    if _lib is None:
+        path = lib_path()
+        if not os.path.exists(path):
+            if not build_if_missing:
+                raise FileNotFoundError(f"{path} is not built")
+            _build.build_cuda()
+        lib = C.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def call(name: str, *args) -> int:
+    lib = load()
+    st = getattr(lib, name)(*args)
+    if st != HMM_OK:
+        raise HmmError(st, name, lib.hmm_last_error().decode())
+    return st
+
+
+def last_error() -> str:
+    return load().hmm_last_error().decode()

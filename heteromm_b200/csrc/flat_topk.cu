@@ -1,0 +1,565 @@
+// flat_topk.cu — exact inner-product scoring fused with top-k and threshold
+// selection on CUDA cores (reference steps/example_kernel/
+// inner_product_compute.cpp:11-31, topk_retrieval.cpp:13-31,
+// threshold_retrieval.cpp:11-32), plus the stand-alone top-k / threshold
+// kernels on device-resident scores and the candidate merges.
+//
+// Layout in HBM: memory rows [n][dim] row-major (fp32 or bf16), queries
+// [nq][dim].  One CTA owns QG=16 queries and a contiguous range of rows,
+// which it streams through shared memory in tiles of RT=256 rows x KC=64
+// columns.  Each thread keeps a 4-row x 4-query register tile; a dot product
+// accumulates column-ascending exactly as the reference (fp32: separate
+// multiply and add, both round-to-nearest; bf16: the product is exact in fp32
+// so a fused multiply-add rounds identically).  After each row tile the CTA
+// writes the threshold-bitmap words straight from warp ballots, and appends
+// the (score, row) composites that beat its running per-query threshold to a
+// shared-memory candidate buffer.  A full buffer is cut back to its top k with
+// a warp radix select, which also raises the threshold.  Scores never leave
+// the SM; each CTA emits k candidates per query, and one CTA per query
+// merges them (block radix select + bitonic sort).
+#include <algorithm>
+
+#include "hmm_common.cuh"
+
+namespace hmm {
+namespace {
+
+constexpr int NT = 256;     // threads per CTA
+constexpr int QG = 16;      // queries per CTA
+constexpr int RT = 256;     // rows per tile
+constexpr int KC = 64;      // columns per shared-memory chunk
+constexpr int SROW = KC + 4;  // padded row stride (floats): conflict-free float4 reads
+constexpr int CAP = 512;    // candidate slots per query
+constexpr int KMAX_FUSED = CAP - RT;  // largest k the fused kernel keeps
+constexpr int NWARPS = NT / 32;
+
+struct F32In {
+    using T = float;
+    static constexpr int VEC = 4;   // elements per 16-byte load
+    __device__ static float widen1(const float* p) { return *p; }
+    __device__ static float mac(float acc, float a, float b) { return __fadd_rn(acc, __fmul_rn(a, b)); }
+};
+
+struct BF16In {
+    using T = uint16_t;
+    static constexpr int VEC = 8;
+    __device__ static float widen1(const uint16_t* p) { return bf16_bits_to_f32(*p); }
+    // bf16 x bf16 products are exact in fp32: fma rounds exactly as mul+add.
+    __device__ static float mac(float acc, float a, float b) { return fmaf(a, b, acc); }
+};
+
+size_t fused_smem_bytes(int dim) {
+    const int dimp = (dim + 3) & ~3;
+    return sizeof(float) * (size_t)(RT * SROW + QG * dimp) + sizeof(uint64_t) * (QG * CAP + QG) +
+           sizeof(int) * QG + sizeof(unsigned) * NWARPS * 256;
+}
+
+struct Plan {
+    int64_t rows_per_part;
+    int n_parts;
+    int n_qgroups;
+};
+
+Plan plan_fused(int64_t n, int64_t nq) {
+    Plan p;
+    p.n_qgroups = (int)((nq + QG - 1) / QG);
+    const int64_t tiles = std::max<int64_t>(1, (n + RT - 1) / RT);
+    const int64_t target = std::max<int64_t>(1, (int64_t)device_sm_count() * 2 / p.n_qgroups);
+    const int64_t tiles_per_part = (tiles + target - 1) / target;
+    p.rows_per_part = tiles_per_part * RT;
+    p.n_parts = (int)((tiles + tiles_per_part - 1) / tiles_per_part);
+    return p;
+}
+
+// Loads chunk [c0, c0+w) of rows [t0, t0+RT) into srow, widened to fp32 and
+// zero padded to a multiple of 4 columns.  Zero padding leaves every sum
+// unchanged: s + (+-0) == s for the +0-initialised accumulations used here.
+template <typename In>
+__device__ __forceinline__ void load_rows(float* srow, const typename In::T* __restrict__ mem,
+                                          int64_t t0, int64_t r_end, int dim, int c0, int w,
+                                          bool vec_ok) {
+    const int wp = (w + 3) & ~3;
+    if (vec_ok && (w % In::VEC) == 0) {
+        const int per_row = w / In::VEC;
+        for (int idx = threadIdx.x; idx < RT * per_row; idx += NT) {
+            const int r = idx / per_row, j = (idx % per_row) * In::VEC;
+            const int64_t row = t0 + r;
+            float* dst = srow + r * SROW + j;
+            if (row < r_end) {
+                const typename In::T* src = mem + row * dim + c0 + j;
+                if constexpr (In::VEC == 4) {
+                    *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
+                } else {
+                    const uint4 v = *reinterpret_cast<const uint4*>(src);
+                    float4 lo, hi;
+                    lo.x = __uint_as_float(v.x << 16); lo.y = __uint_as_float(v.x & 0xffff0000u);
+                    lo.z = __uint_as_float(v.y << 16); lo.w = __uint_as_float(v.y & 0xffff0000u);
+                    hi.x = __uint_as_float(v.z << 16); hi.y = __uint_as_float(v.z & 0xffff0000u);
+                    hi.z = __uint_as_float(v.w << 16); hi.w = __uint_as_float(v.w & 0xffff0000u);
+                    *reinterpret_cast<float4*>(dst) = lo;
+                    *reinterpret_cast<float4*>(dst + 4) = hi;
+                }
+            } else {
+                for (int e = 0; e < In::VEC; ++e) dst[e] = 0.0f;
+            }
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < RT * wp; idx += NT) {
+            const int r = idx / wp, j = idx % wp;
+            const int64_t row = t0 + r;
+            srow[r * SROW + j] = (row < r_end && j < w) ? In::widen1(mem + row * dim + c0 + j) : 0.0f;
+        }
+    }
+}
+
+// Cuts query ql's candidate buffer back to its best k and raises its threshold.
+__device__ __forceinline__ void compact_query(uint64_t* cbuf, int* scnt, uint64_t* sthr, int ql,
+                                              int k, unsigned* hist) {
+    const int m = scnt[ql];
+    const uint64_t T = warp_select_threshold(cbuf + ql * CAP, m, k, hist);
+    const int kept = warp_compact_ge(cbuf + ql * CAP, m, T);
+    if ((threadIdx.x & 31) == 0) {
+        scnt[ql] = kept;
+        if (kept >= k) sthr[ql] = T;
+    }
+    __syncwarp();
+}
+
+// grid (n_parts, n_qgroups), NT threads.  cand [nq][n_parts][k] composites.
+template <typename In>
+__global__ void __launch_bounds__(NT, 1)
+fused_ip_topk_kernel(const typename In::T* __restrict__ mem, int64_t n, int dim,
+                     const typename In::T* __restrict__ qry, int nq, int k,
+                     int64_t rows_per_part, float thr, uint32_t* __restrict__ bitmap32,
+                     float* __restrict__ scores_out, uint64_t* __restrict__ cand, bool vec_ok) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int dimp = (dim + 3) & ~3;
+    float* srow = reinterpret_cast<float*>(smem_raw);
+    float* sq = srow + RT * SROW;
+    uint64_t* cbuf = reinterpret_cast<uint64_t*>(sq + QG * dimp);
+    uint64_t* sthr = cbuf + QG * CAP;
+    int* scnt = reinterpret_cast<int*>(sthr + QG);
+    unsigned* shist = reinterpret_cast<unsigned*>(scnt + QG);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rg = tid & 63;          // rows rg + 64*i
+    const int qg = tid >> 6;          // queries 4*qg .. 4*qg+3
+    const int part = blockIdx.x;
+    const int q0 = blockIdx.y * QG;
+    const int64_t r_begin = (int64_t)part * rows_per_part;
+    const int64_t r_end = min(n, r_begin + rows_per_part);
+    const int64_t words32 = 2 * ((n + 63) / 64);
+
+    for (int i = tid; i < QG * dimp; i += NT) {
+        const int q = i / dimp, j = i % dimp;
+        sq[i] = (q0 + q < nq && j < dim) ? In::widen1(qry + (int64_t)(q0 + q) * dim + j) : 0.0f;
+    }
+    if (tid < QG) { scnt[tid] = 0; sthr[tid] = 0ull; }
+
+    for (int64_t t0 = r_begin; t0 < r_end; t0 += RT) {
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+
+        for (int c0 = 0; c0 < dim; c0 += KC) {
+            const int w = min(KC, dim - c0);
+            __syncthreads();
+            load_rows<In>(srow, mem, t0, r_end, dim, c0, w, vec_ok);
+            __syncthreads();
+            const int wp = (w + 3) & ~3;
+            for (int kk = 0; kk < wp; kk += 4) {
+                float4 a[4], b[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    a[i] = *reinterpret_cast<const float4*>(srow + (rg + 64 * i) * SROW + kk);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    b[j] = *reinterpret_cast<const float4*>(sq + (4 * qg + j) * dimp + c0 + kk);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc[i][j] = In::mac(acc[i][j], a[i].x, b[j].x);
+                        acc[i][j] = In::mac(acc[i][j], a[i].y, b[j].y);
+                        acc[i][j] = In::mac(acc[i][j], a[i].z, b[j].z);
+                        acc[i][j] = In::mac(acc[i][j], a[i].w, b[j].w);
+                    }
+            }
+        }
+
+        // ---- tile epilogue: scores, threshold bitmap, candidates
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int64_t row = t0 + rg + 64 * i;
+            const bool rv = row < r_end;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int ql = 4 * qg + j;
+                const int q = q0 + ql;
+                const bool v = rv && q < nq;
+                const float s = acc[i][j];
+                if (scores_out && v) scores_out[(int64_t)q * n + row] = s;
+                if (bitmap32) {
+                    const unsigned bits = __ballot_sync(0xffffffffu, v && s >= thr);
+                    const int64_t w32 = ((t0 + 64 * i) >> 5) + (rg >> 5);
+                    if (lane == 0 && q < nq && w32 < words32)
+                        bitmap32[(int64_t)q * words32 + w32] = bits;
+                }
+                if (v && cand) {
+                    const uint64_t c = make_cand(f32_key(s), (uint32_t)row);
+                    if (c > sthr[ql]) {
+                        const int pos = atomicAdd(&scnt[ql], 1);
+                        cbuf[ql * CAP + pos] = c;
+                    }
+                }
+            }
+        }
+        if (cand) {
+            __syncthreads();
+            for (int ql = warp; ql < QG; ql += NWARPS)
+                if (scnt[ql] > CAP - RT) compact_query(cbuf, scnt, sthr, ql, k, shist + warp * 256);
+            __syncthreads();
+        }
+    }
+    if (!cand) return;
+
+    // ---- final: top-k of each query's buffer -> cand
+    const int n_parts = gridDim.x;
+    for (int ql = warp; ql < QG; ql += NWARPS) {
+        const int q = q0 + ql;
+        if (q >= nq) continue;
+        compact_query(cbuf, scnt, sthr, ql, k, shist + warp * 256);
+        const int m = scnt[ql];
+        uint64_t* dst = cand + ((int64_t)q * n_parts + part) * k;
+        for (int i = lane; i < k; i += 32) dst[i] = i < m ? cbuf[ql * CAP + i] : 0ull;
+    }
+}
+
+// Top-k over device scores: CTA (part, q) turns scores[q][part*P .. +P) into
+// composites and keeps its best k.  cand [nq][n_parts][k].
+constexpr int TOPK_P = 4096;
+constexpr int TOPK_KMAX = 4096;
+
+__global__ void __launch_bounds__(256)
+scores_topk_partition_kernel(const float* __restrict__ scores, int64_t n, int k,
+                             uint64_t* __restrict__ cand) {
+    __shared__ uint64_t keys[TOPK_P];
+    __shared__ unsigned sm[300];
+    __shared__ int cnt;
+    const int part = blockIdx.x, q = blockIdx.y;
+    const int64_t r0 = (int64_t)part * TOPK_P;
+    const int m = (int)(n - r0 < TOPK_P ? n - r0 : TOPK_P);
+    const float* src = scores + (int64_t)q * n + r0;
+    for (int i = threadIdx.x; i < m; i += 256) keys[i] = make_cand(f32_key(src[i]), (uint32_t)(r0 + i));
+    if (threadIdx.x == 0) cnt = 0;
+    __syncthreads();
+    const int kk = min(k, m);
+    const uint64_t T = block_select_threshold(keys, m, kk, sm);
+    __syncthreads();
+    uint64_t* dst = cand + ((int64_t)q * gridDim.x + part) * k;
+    // keys are unique and nonzero: exactly kk of them are >= T
+    for (int i = threadIdx.x; i < m; i += 256) {
+        if (keys[i] >= T) dst[atomicAdd(&cnt, 1)] = keys[i];
+    }
+    for (int i = kk + threadIdx.x; i < k; i += 256) dst[i] = 0ull;
+}
+
+// One CTA per query: best k of cand[q][0..M) -> sorted outputs.
+template <typename IdxT>
+__global__ void __launch_bounds__(256)
+merge_candidates_kernel(const uint64_t* __restrict__ cand, int64_t M, int k, int64_t row_offset,
+                        IdxT* __restrict__ out_idx, float* __restrict__ out_scores) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint64_t* best = reinterpret_cast<uint64_t*>(smem_raw);
+    __shared__ unsigned sm[300];
+    __shared__ int cnt;
+    const int q = blockIdx.x;
+    const uint64_t* src = cand + (int64_t)q * M;
+    const int kp = next_pow2(k);
+    const uint64_t T = block_select_threshold(src, M, k, sm);
+    if (threadIdx.x == 0) cnt = 0;
+    for (int i = threadIdx.x; i < kp; i += 256) best[i] = 0ull;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < M; i += 256) {
+        const uint64_t c = src[i];
+        if (c > T) best[atomicAdd(&cnt, 1)] = c;
+    }
+    __syncthreads();
+    // keys equal to T: one real key (T > 0) or any number of empty slots (T == 0)
+    if (threadIdx.x == 0 && T != 0ull && cnt < k) best[cnt++] = T;
+    __syncthreads();
+    block_bitonic_sort_desc(best, kp);
+    for (int i = threadIdx.x; i < k; i += 256) {
+        const uint64_t c = best[i];
+        const bool ok = c != 0ull;
+        out_idx[(int64_t)q * k + i] = ok ? (IdxT)((int64_t)cand_row(c) + row_offset) : (IdxT)-1;
+        if (out_scores) out_scores[(int64_t)q * k + i] = ok ? cand_score(c) : -INFINITY;
+    }
+}
+
+// bit i%64 of word i/64 = scores[i] >= thr.  One warp per 64-score word.
+__global__ void threshold_bitmap_kernel(const float* __restrict__ scores, int64_t n, int nq,
+                                        float thr, uint64_t* __restrict__ bitmap) {
+    const int64_t words = (n + 63) / 64;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= words * nq) return;
+    const int64_t q = gw / words, w = gw % words;
+    const float* s = scores + q * n;
+    const int64_t i0 = w * 64 + lane, i1 = i0 + 32;
+    const unsigned lo = __ballot_sync(0xffffffffu, i0 < n && s[i0] >= thr);
+    const unsigned hi = __ballot_sync(0xffffffffu, i1 < n && s[i1] >= thr);
+    if (lane == 0) bitmap[q * words + w] = ((uint64_t)hi << 32) | lo;
+}
+
+// Shard merge: one CTA per query sorts the n_shards*k gathered (score,
+// global index) candidates by (score desc, index asc) in shared memory and
+// keeps the first k.  Empty slots (index -1) sort last.
+constexpr int MERGE_MAX = 8192;
+
+__device__ __forceinline__ bool pair_better(uint32_t ka, int64_t ia, uint32_t kb, int64_t ib) {
+    return ka > kb || (ka == kb && ia < ib);
+}
+
+__global__ void __launch_bounds__(256)
+shard_merge_kernel(const float* __restrict__ cand_scores, const int64_t* __restrict__ cand_idx,
+                   int n_shards, int nq, int k, float* __restrict__ out_scores,
+                   int64_t* __restrict__ out_idx) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int M = n_shards * k;
+    const int n = next_pow2(M);
+    int64_t* sidx = reinterpret_cast<int64_t*>(smem_raw);
+    uint32_t* skey = reinterpret_cast<uint32_t*>(sidx + n);
+    const int q = blockIdx.x;
+    for (int r = threadIdx.x; r < n; r += blockDim.x) {
+        if (r < M) {
+            const int s = r / k, i = r % k;
+            const int64_t o = ((int64_t)s * nq + q) * k + i;
+            const int64_t id = cand_idx[o];
+            skey[r] = id < 0 ? 0u : f32_key(cand_scores[o]);
+            sidx[r] = id < 0 ? INT64_MAX : id;
+        } else {
+            skey[r] = 0u;
+            sidx[r] = INT64_MAX;
+        }
+    }
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool desc = ((lo & size) == 0);
+                const bool hi_better = pair_better(skey[hi], sidx[hi], skey[lo], sidx[lo]);
+                if (hi_better == desc) {
+                    const uint32_t tk = skey[lo]; skey[lo] = skey[hi]; skey[hi] = tk;
+                    const int64_t ti = sidx[lo]; sidx[lo] = sidx[hi]; sidx[hi] = ti;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const bool ok = sidx[i] != INT64_MAX;
+        out_idx[(int64_t)q * k + i] = ok ? sidx[i] : -1;
+        out_scores[(int64_t)q * k + i] = ok ? key_to_f32(skey[i]) : -INFINITY;
+    }
+}
+
+hmm_status_t check_common(const void* mem, int64_t n, int64_t dim, const void* qry, int64_t nq,
+                          int64_t k) {
+    HMM_REQUIRE(n >= 0 && n < (int64_t(1) << 31), "n_rows must be in [0, 2^31), got %lld",
+                (long long)n);
+    HMM_REQUIRE(nq >= 0 && nq <= 65535 * QG, "n_queries out of range: %lld", (long long)nq);
+    HMM_REQUIRE(dim >= 1 && dim <= 1024, "dim must be in [1, 1024], got %lld", (long long)dim);
+    HMM_REQUIRE(k >= 1, "k must be >= 1, got %lld", (long long)k);
+    HMM_REQUIRE(n == 0 || mem, "memory pointer is null");
+    HMM_REQUIRE(nq == 0 || qry, "queries pointer is null");
+    return HMM_OK;
+}
+
+template <typename In, typename IdxT>
+hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const typename In::T* qry,
+                       int64_t nq, int64_t k, int64_t row_offset, IdxT* out_idx,
+                       float* out_scores, float thr, uint64_t* out_bitmap, float* full_scores,
+                       void* ws, size_t ws_bytes, cudaStream_t st, size_t need) {
+    HMM_REQUIRE(k <= KMAX_FUSED, "fused score+top-k supports k <= %d, got %lld", KMAX_FUSED,
+                (long long)k);
+    HMM_REQUIRE(out_idx, "out_idx is null");
+    if (nq == 0) return HMM_OK;
+    if (ws_bytes < need || !ws)
+        return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu bytes", ws_bytes, need);
+    const Plan p = plan_fused(n, nq);
+    uint64_t* cand = static_cast<uint64_t*>(ws);
+    const size_t smem = fused_smem_bytes((int)dim);
+    auto kern = fused_ip_topk_kernel<In>;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const bool vec_ok = (dim % In::VEC) == 0 &&
+                        (reinterpret_cast<uintptr_t>(mem) % 16) == 0;
+    dim3 grid(p.n_parts, p.n_qgroups);
+    if (n > 0) {
+        kern<<<grid, NT, smem, st>>>(mem, n, (int)dim, qry, (int)nq, (int)k, p.rows_per_part, thr,
+                                     reinterpret_cast<uint32_t*>(out_bitmap), full_scores, cand,
+                                     vec_ok);
+        hmm_status_t s = check_launch("fused_ip_topk_kernel");
+        if (s != HMM_OK) return s;
+    } else {
+        HMM_CUDA_TRY(cudaMemsetAsync(cand, 0, sizeof(uint64_t) * nq * p.n_parts * k, st));
+    }
+    const size_t msmem = sizeof(uint64_t) * next_pow2((int)k);
+    merge_candidates_kernel<IdxT><<<(unsigned)nq, 256, msmem, st>>>(
+        cand, (int64_t)p.n_parts * k, (int)k, row_offset, out_idx, out_scores);
+    return check_launch("merge_candidates_kernel");
+}
+
+size_t fused_ws_bytes(int64_t n, int64_t nq, int64_t k) {
+    const Plan p = plan_fused(n, nq);
+    return sizeof(uint64_t) * (size_t)nq * (size_t)p.n_parts * (size_t)k + 256;
+}
+
+}  // namespace
+}  // namespace hmm
+
+using namespace hmm;
+
+extern "C" {
+
+hmm_status_t hmm_ip_score_f32(const float* mem, int64_t n_rows, int64_t dim,
+                              const float* queries, int64_t n_queries, float* scores,
+                              void* stream) {
+    hmm_status_t s = check_common(mem, n_rows, dim, queries, n_queries, 1);
+    if (s != HMM_OK) return s;
+    HMM_REQUIRE(n_rows == 0 || n_queries == 0 || scores, "scores pointer is null");
+    if (n_rows == 0 || n_queries == 0) return HMM_OK;
+    // The fused kernel with no candidate output writes every score.
+    const Plan p = plan_fused(n_rows, n_queries);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t smem = fused_smem_bytes((int)dim);
+    auto kern = fused_ip_topk_kernel<F32In>;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const bool vec_ok = (dim % 4) == 0 && (reinterpret_cast<uintptr_t>(mem) % 16) == 0;
+    kern<<<dim3(p.n_parts, p.n_qgroups), NT, smem, st>>>(mem, n_rows, (int)dim, queries,
+                                                         (int)n_queries, 1, p.rows_per_part, 0.0f,
+                                                         nullptr, scores, nullptr, vec_ok);
+    return check_launch("fused_ip_topk_kernel(scores)");
+}
+
+size_t hmm_topk_f32_workspace_size(int64_t n, int64_t n_queries, int64_t k) {
+    if (n < 0 || n_queries < 0 || k < 1) return 0;
+    const int64_t parts = std::max<int64_t>(1, (n + TOPK_P - 1) / TOPK_P);
+    return sizeof(uint64_t) * (size_t)(parts * n_queries * k) + 256;
+}
+
+hmm_status_t hmm_topk_f32(const float* scores, int64_t n, int64_t n_queries, int64_t k,
+                          int32_t* out_idx, float* out_scores, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    HMM_REQUIRE(n >= 0 && n < (int64_t(1) << 31), "n must be in [0, 2^31)");
+    HMM_REQUIRE(n_queries >= 0 && n_queries <= 65535, "n_queries out of range");
+    HMM_REQUIRE(k >= 1 && k <= TOPK_KMAX, "k must be in [1, %d], got %lld", TOPK_KMAX,
+                (long long)k);
+    HMM_REQUIRE(n == 0 || n_queries == 0 || scores, "scores pointer is null");
+    HMM_REQUIRE(n_queries == 0 || out_idx, "out_idx is null");
+    if (n_queries == 0) return HMM_OK;
+    const size_t need = hmm_topk_f32_workspace_size(n, n_queries, k);
+    if (!workspace || workspace_bytes < need)
+        return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu bytes", workspace_bytes, need);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint64_t* cand = static_cast<uint64_t*>(workspace);
+    const int64_t parts = std::max<int64_t>(1, (n + TOPK_P - 1) / TOPK_P);
+    HMM_REQUIRE(parts <= 2147483647, "too many partitions");
+    if (n > 0) {
+        scores_topk_partition_kernel<<<dim3((unsigned)parts, (unsigned)n_queries), 256, 0, st>>>(
+            scores, n, (int)k, cand);
+        hmm_status_t s = check_launch("scores_topk_partition_kernel");
+        if (s != HMM_OK) return s;
+    } else {
+        HMM_CUDA_TRY(cudaMemsetAsync(cand, 0, sizeof(uint64_t) * n_queries * k, st));
+    }
+    const size_t msmem = sizeof(uint64_t) * next_pow2((int)k);
+    auto mk = merge_candidates_kernel<int32_t>;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(mk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
+    mk<<<(unsigned)n_queries, 256, msmem, st>>>(cand, parts * k, (int)k, 0, out_idx, out_scores);
+    return check_launch("merge_candidates_kernel");
+}
+
+hmm_status_t hmm_threshold_bitmap_f32(const float* scores, int64_t n, int64_t n_queries,
+                                      float threshold, uint64_t* bitmap, void* stream) {
+    HMM_REQUIRE(n >= 0 && n_queries >= 0, "negative size");
+    HMM_REQUIRE(n == 0 || n_queries == 0 || (scores && bitmap), "null pointer");
+    const int64_t words = (n + 63) / 64;
+    if (words == 0 || n_queries == 0) return HMM_OK;
+    const int64_t threads = words * n_queries * 32;
+    const int64_t blocks = (threads + 255) / 256;
+    HMM_REQUIRE(blocks <= 2147483647, "problem too large");
+    threshold_bitmap_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        scores, n, (int)n_queries, threshold, bitmap);
+    return check_launch("threshold_bitmap_kernel");
+}
+
+size_t hmm_ip_topk_f32_workspace_size(int64_t n_rows, int64_t dim, int64_t n_queries, int64_t k) {
+    (void)dim;
+    if (n_rows < 0 || n_queries < 0 || k < 1) return 0;
+    return fused_ws_bytes(n_rows, n_queries, k);
+}
+
+hmm_status_t hmm_ip_topk_f32(const float* mem, int64_t n_rows, int64_t dim,
+                             const float* queries, int64_t n_queries, int64_t k,
+                             int32_t* out_idx, float* out_scores, float threshold,
+                             uint64_t* out_bitmap, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+    hmm_status_t s = check_common(mem, n_rows, dim, queries, n_queries, k);
+    if (s != HMM_OK) return s;
+    return run_fused<F32In, int32_t>(mem, n_rows, dim, queries, n_queries, k, 0, out_idx,
+                                     out_scores, threshold, out_bitmap, nullptr, workspace,
+                                     workspace_bytes, static_cast<cudaStream_t>(stream),
+                                     fused_ws_bytes(n_rows, n_queries, k));
+}
+
+size_t hmm_ip_topk_bf16_workspace_size(int64_t n_rows, int64_t dim, int64_t n_queries,
+                                       int64_t k) {
+    (void)dim;
+    if (n_rows < 0 || n_queries < 0 || k < 1) return 0;
+    return fused_ws_bytes(n_rows, n_queries, k);
+}
+
+hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
+                              const uint16_t* queries, int64_t n_queries, int64_t k,
+                              int64_t row_offset, int64_t* out_idx, float* out_scores,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    hmm_status_t s = check_common(mem, n_rows, dim, queries, n_queries, k);
+    if (s != HMM_OK) return s;
+    HMM_REQUIRE(row_offset >= 0, "row_offset must be >= 0");
+    HMM_REQUIRE(n_queries == 0 || out_scores, "out_scores is null");
+    return run_fused<BF16In, int64_t>(mem, n_rows, dim, queries, n_queries, k, row_offset,
+                                      out_idx, out_scores, 0.0f, nullptr, nullptr, workspace,
+                                      workspace_bytes, static_cast<cudaStream_t>(stream),
+                                      fused_ws_bytes(n_rows, n_queries, k));
+}
+
+size_t hmm_shard_merge_topk_workspace_size(int64_t n_shards, int64_t n_queries, int64_t k) {
+    (void)n_shards; (void)n_queries; (void)k;
+    return 0;
+}
+
+hmm_status_t hmm_shard_merge_topk(const float* cand_scores, const int64_t* cand_idx,
+                                  int64_t n_shards, int64_t n_queries, int64_t k,
+                                  float* out_scores, int64_t* out_idx, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    (void)workspace; (void)workspace_bytes;
+    HMM_REQUIRE(n_shards >= 1 && k >= 1 && n_queries >= 0, "bad sizes");
+    HMM_REQUIRE(n_shards * k <= MERGE_MAX, "n_shards * k must be <= %d", MERGE_MAX);
+    HMM_REQUIRE(n_queries <= 2147483647, "n_queries out of range");
+    if (n_queries == 0) return HMM_OK;
+    HMM_REQUIRE(cand_scores && cand_idx && out_scores && out_idx, "null pointer");
+    const int n = next_pow2((int)(n_shards * k));
+    const size_t smem = (sizeof(int64_t) + sizeof(uint32_t)) * (size_t)n;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(shard_merge_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    shard_merge_kernel<<<(unsigned)n_queries, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+        cand_scores, cand_idx, (int)n_shards, (int)n_queries, (int)k, out_scores, out_idx);
+    return check_launch("shard_merge_kernel");
+}
+
+}  // extern "C"

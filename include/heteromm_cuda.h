@@ -1,0 +1,122 @@
+/*
+ * heteromm_cuda.h — C ABI of the B200 (sm_100a) kernels behind the HeteroMM
+ * score -> select -> apply steps.
+ *
+ * This is the drop-in boundary: the `KernelType::GPU` arm of every step
+ * (steps/compute_score.h:104-112, steps/memory_retrieval.h:96-104,
+ * steps/build_memory.h:94-102, steps/apply_memory.h:103-111,
+ * steps/fused_steps/template.h:75-83 in the reference) calls these entry
+ * points, and so can any FFI (ctypes, cgo, JNI) directly.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, status codes.  No exceptions cross the ABI.
+ *   - Every data pointer is a DEVICE pointer on the current CUDA device;
+ *     `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *   - Outputs are caller-owned.  Entry points that need scratch memory take a
+ *     caller-provided `workspace` of at least `*_workspace_size(...)` bytes
+ *     (sized for the current device); they never allocate.
+ *   - Calls are asynchronous on `stream`; argument errors are reported
+ *     synchronously, device-side errors through the CUDA error state.
+ *   - Top-k outputs are ordered best first; ties are broken by the lowest
+ *     row index; NaN ranks below every number and -0.0 ties with +0.0.
+ *     Slots beyond min(k, n) hold index -1 and score -inf.
+ *   - fp32 dot products are computed exactly as the reference CPU code does:
+ *     fl(fl(a*b) + s) with j ascending (no FMA contraction), so fp32 scores
+ *     are bit-identical to the reference's.
+ *   - hmm_last_error() returns the message of the calling thread's last
+ *     failed call.
+ */
+#ifndef HETEROMM_CUDA_H_
+#define HETEROMM_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    HMM_OK = 0,
+    HMM_ERR_INVALID = 1,      /* bad argument (null pointer, negative size, k out of range) */
+    HMM_ERR_CUDA = 2,         /* a CUDA runtime call or kernel launch failed */
+    HMM_ERR_OOM = 3,          /* workspace too small */
+    HMM_ERR_BOUNDS = 4,       /* an index / page-table entry outside its extent */
+    HMM_ERR_TIMEOUT = 5,      /* a bounded wait (device or collective) gave up */
+    HMM_ERR_UNSUPPORTED = 6   /* shape outside what the kernels implement */
+} hmm_status_t;
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* hmm_last_error(void);
+/* Library version string, e.g. "heteromm-b200 0.1.0 sm_100a". */
+const char* hmm_version(void);
+
+/* ---------------------------------------------------------------- score
+ * InnerProductCompute (reference steps/compute_score.h:172-205,
+ * steps/example_kernel/inner_product_compute.cpp:11-31).
+ * scores[q*n_rows + i] = sum_j mem[i*dim + j] * queries[q*dim + j]
+ * mem [n_rows][dim] fp32 row-major, queries [n_queries][dim], dim <= 1024. */
+hmm_status_t hmm_ip_score_f32(const float* mem, int64_t n_rows, int64_t dim,
+                              const float* queries, int64_t n_queries, float* scores,
+                              void* stream);
+
+/* --------------------------------------------------------------- select
+ * TopKRetrieval (reference steps/memory_retrieval.h:159-193,
+ * steps/example_kernel/topk_retrieval.cpp:13-31) on device-resident scores
+ * [n_queries][n].  out_idx [n_queries][k] int32; out_scores [n_queries][k]
+ * or NULL.  1 <= k <= 4096. */
+size_t hmm_topk_f32_workspace_size(int64_t n, int64_t n_queries, int64_t k);
+hmm_status_t hmm_topk_f32(const float* scores, int64_t n, int64_t n_queries, int64_t k,
+                          int32_t* out_idx, float* out_scores, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* ThresholdRetrieval (reference steps/memory_retrieval.h:200-234,
+ * steps/example_kernel/threshold_retrieval.cpp:11-32): bit i%64 of word
+ * i/64 is set iff scores[i] >= threshold.  bitmap [n_queries][ceil(n/64)]. */
+hmm_status_t hmm_threshold_bitmap_f32(const float* scores, int64_t n, int64_t n_queries,
+                                      float threshold, uint64_t* bitmap, void* stream);
+
+/* ---------------------------------------------------- fused score + select
+ * FusedComputeScoreAndRetrieval<FlatIndexMemory<float>, VectorQuery<float>,
+ * TopKIndex> (reference steps/fused_steps/template.h:21-135), batched over
+ * queries: InnerProductCompute -> TopKRetrieval (+ ThresholdRetrieval) in one
+ * pass; scores never round-trip through HBM.
+ *   out_idx     [n_queries][k] int32 (required)
+ *   out_scores  [n_queries][k] fp32 scores of the selected rows, or NULL
+ *   out_bitmap  [n_queries][ceil(n_rows/64)] threshold bitmap (>=), or NULL
+ * dim <= 1024, 1 <= k <= 4096, n_rows < 2^31. */
+size_t hmm_ip_topk_f32_workspace_size(int64_t n_rows, int64_t dim, int64_t n_queries,
+                                      int64_t k);
+hmm_status_t hmm_ip_topk_f32(const float* mem, int64_t n_rows, int64_t dim,
+                             const float* queries, int64_t n_queries, int64_t k,
+                             int32_t* out_idx, float* out_scores, float threshold,
+                             uint64_t* out_bitmap, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* Same on bf16 rows and queries (bf16 bit patterns as uint16), fp32
+ * accumulate: one shard of a row-sharded memory.  Row i of this shard has
+ * global index row_offset + i; out_idx [n_queries][k] int64 global indices,
+ * out_scores [n_queries][k] fp32 (required: the shard merge needs them).
+ * Scores equal the reference's fp32 inner product of the widened values. */
+size_t hmm_ip_topk_bf16_workspace_size(int64_t n_rows, int64_t dim, int64_t n_queries,
+                                       int64_t k);
+hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
+                              const uint16_t* queries, int64_t n_queries, int64_t k,
+                              int64_t row_offset, int64_t* out_idx, float* out_scores,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Final merge of per-shard candidates after the all-gather: cand_* are
+ * [n_shards][n_queries][k] (index -1 = empty slot); outputs [n_queries][k]
+ * by (score desc, global index asc).  No reference counterpart: the
+ * reference has no multi-device path; the merge preserves its top-k order. */
+size_t hmm_shard_merge_topk_workspace_size(int64_t n_shards, int64_t n_queries, int64_t k);
+hmm_status_t hmm_shard_merge_topk(const float* cand_scores, const int64_t* cand_idx,
+                                  int64_t n_shards, int64_t n_queries, int64_t k,
+                                  float* out_scores, int64_t* out_idx, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HETEROMM_CUDA_H_ */

@@ -52,7 +52,7 @@ sed -i 's/^class BM25IndexMemory : public Memory<BM25IndexData> {$/&\npublic:\n 
     "$SCRATCH/dev/types/memory.h"
 grep -q 'using content_type = BM25IndexData;' "$SCRATCH/dev/types/memory.h"
 
-CXX=${CXX:-g++}
+CXX=/usr/bin/g++
 
 # ---- the reference's 5 doctest unit-test binaries (unittest/Makefile:3-39 flags)
 for t in innerproduct:inner_product_compute topk_retrieval:topk_retrieval \
