@@ -299,6 +299,18 @@ merge_candidates_kernel(const uint64_t* __restrict__ cand, int64_t M, int k, int
     }
 }
 
+// The merge kernel's dynamic shared memory grows with k; its limit is set
+// once to the largest k any entry point accepts, never to one call's need,
+// so that launches with different k (on any path) stay within it.
+constexpr int MERGE_KMAX = 4096;
+template <typename IdxT>
+hmm_status_t prepare_merge_kernel() {
+    HMM_CUDA_TRY(cudaFuncSetAttribute(merge_candidates_kernel<IdxT>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)(sizeof(uint64_t) * MERGE_KMAX)));
+    return HMM_OK;
+}
+
 // bit i%64 of word i/64 = scores[i] >= thr.  One warp per 64-score word.
 __global__ void threshold_bitmap_kernel(const float* __restrict__ scores, int64_t n, int nq,
                                         float thr, uint64_t* __restrict__ bitmap) {
@@ -409,6 +421,8 @@ hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const 
         HMM_CUDA_TRY(cudaMemsetAsync(cand, 0, sizeof(uint64_t) * nq * p.n_parts * k, st));
     }
     const size_t msmem = sizeof(uint64_t) * next_pow2((int)k);
+    hmm_status_t ms = prepare_merge_kernel<IdxT>();
+    if (ms != HMM_OK) return ms;
     merge_candidates_kernel<IdxT><<<(unsigned)nq, 256, msmem, st>>>(
         cand, (int64_t)p.n_parts * k, (int)k, row_offset, out_idx, out_scores);
     return check_launch("merge_candidates_kernel");
@@ -479,7 +493,8 @@ hmm_status_t hmm_topk_f32(const float* scores, int64_t n, int64_t n_queries, int
     }
     const size_t msmem = sizeof(uint64_t) * next_pow2((int)k);
     auto mk = merge_candidates_kernel<int32_t>;
-    HMM_CUDA_TRY(cudaFuncSetAttribute(mk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
+    hmm_status_t ms = prepare_merge_kernel<int32_t>();
+    if (ms != HMM_OK) return ms;
     mk<<<(unsigned)n_queries, 256, msmem, st>>>(cand, parts * k, (int)k, 0, out_idx, out_scores);
     return check_launch("merge_candidates_kernel");
 }

@@ -84,7 +84,7 @@ hmm_status_t hmm_threshold_bitmap_f32(const float* scores, int64_t n, int64_t n_
  *   out_idx     [n_queries][k] int32 (required)
  *   out_scores  [n_queries][k] fp32 scores of the selected rows, or NULL
  *   out_bitmap  [n_queries][ceil(n_rows/64)] threshold bitmap (>=), or NULL
- * dim <= 1024, 1 <= k <= 4096, n_rows < 2^31. */
+ * dim <= 1024, 1 <= k <= 256, n_rows < 2^31. */
 size_t hmm_ip_topk_f32_workspace_size(int64_t n_rows, int64_t dim, int64_t n_queries,
                                       int64_t k);
 hmm_status_t hmm_ip_topk_f32(const float* mem, int64_t n_rows, int64_t dim,

@@ -126,3 +126,14 @@ def test_deterministic_repeat(cuda):
     b = hmm.ip_topk_f32(mem, qry, 64, THR)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+def test_varying_k_across_entry_points(cuda):
+    """A small-k top-k call must not shrink the merge kernel's shared-memory
+    limit for a later call with a larger k."""
+    s = dev(gen.normal_f32(61, (1, 5000)), cuda)
+    hmm.topk_f32(s, 64)
+    mem = gen.normal_f32(62, (3000, 96))
+    qry = gen.normal_f32(63, (7, 96))
+    idx, _, _ = hmm.ip_topk_f32(dev(mem, cuda), dev(qry, cuda), 200, THR)
+    assert np.array_equal(idx.cpu().numpy(), O.ip_topk_f32(mem, qry, 200, THR)[0])
