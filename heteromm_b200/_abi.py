@@ -34,6 +34,7 @@ SIGNATURES = {
     "hmm_ip_topk_f32": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _F, _P, _P, _S, _P]),
     "hmm_ip_topk_bf16_workspace_size": (_S, [_I, _I, _I, _I]),
     "hmm_ip_topk_bf16": (C.c_int, [_P, _I, _I, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
+    "hmm_ip_topk_f32_noalloc": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _F, _P, _P]),
     "hmm_shard_merge_topk_workspace_size": (_S, [_I, _I, _I]),
     "hmm_shard_merge_topk": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
 }

@@ -18,6 +18,7 @@
 // the SM; each CTA emits k candidates per query, and one CTA per query
 // merges them (block radix select + bitonic sort).
 #include <algorithm>
+#include <mutex>
 
 #include "hmm_common.cuh"
 
@@ -434,6 +435,36 @@ size_t fused_ws_bytes(int64_t n, int64_t nq, int64_t k) {
 }
 
 }  // namespace
+// Scratch of hmm_ip_topk_f32_noalloc: a fixed device array, so that the
+// entry point never allocates.  Host code may not use `g_noalloc_scratch` as
+// a device address; it looks the address up per device with
+// cudaGetSymbolAddress (see noalloc_scratch_ptr).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[HMM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device, looked up on
+// the first call per device (with that device current) and cached.
+hmm_status_t noalloc_scratch_ptr(void** out) {
+    static std::mutex mu;
+    static void* cache[128] = {nullptr};
+    int dev = 0;
+    HMM_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 128) return set_error(HMM_ERR_UNSUPPORTED, "device id %d", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(HMM_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s",
+                             cudaGetErrorString(e));
+        cache[dev] = p;
+    }
+    *out = cache[dev];
+    return HMM_OK;
+}
+
+}  // namespace
 }  // namespace hmm
 
 using namespace hmm;
@@ -551,6 +582,27 @@ hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
                                       out_idx, out_scores, 0.0f, nullptr, nullptr, workspace,
                                       workspace_bytes, static_cast<cudaStream_t>(stream),
                                       fused_ws_bytes(n_rows, n_queries, k));
+}
+
+hmm_status_t hmm_ip_topk_f32_noalloc(const float* mem, int64_t n_rows, int64_t dim,
+                                     const float* queries, int64_t n_queries, int64_t k,
+                                     int32_t* out_idx, float* out_scores, float threshold,
+                                     uint64_t* out_bitmap, void* stream) {
+    hmm_status_t s = check_common(mem, n_rows, dim, queries, n_queries, k);
+    if (s != HMM_OK) return s;
+    const size_t need = fused_ws_bytes(n_rows, n_queries, k);
+    if (need > HMM_NOALLOC_SCRATCH_BYTES)
+        return set_error(HMM_ERR_UNSUPPORTED,
+                         "hmm_ip_topk_f32_noalloc: this problem needs %zu bytes of scratch, above "
+                         "the fixed %u-byte limit; use hmm_ip_topk_f32 with a workspace",
+                         need, (unsigned)HMM_NOALLOC_SCRATCH_BYTES);
+    void* scratch = nullptr;
+    s = noalloc_scratch_ptr(&scratch);
+    if (s != HMM_OK) return s;
+    return run_fused<F32In, int32_t>(mem, n_rows, dim, queries, n_queries, k, 0, out_idx,
+                                     out_scores, threshold, out_bitmap, nullptr, scratch,
+                                     HMM_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream),
+                                     need);
 }
 
 size_t hmm_shard_merge_topk_workspace_size(int64_t n_shards, int64_t n_queries, int64_t k) {

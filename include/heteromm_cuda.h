@@ -115,6 +115,36 @@ hmm_status_t hmm_shard_merge_topk(const float* cand_scores, const int64_t* cand_
                                   float* out_scores, int64_t* out_idx, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------ allocation-free variant
+ * No counterpart in the reference: this entry point exists for callers that
+ * cannot allocate device memory and so cannot supply the workspace that
+ * hmm_ip_topk_f32 needs - for example a host reached through an FFI (cgo,
+ * JNI) that only holds device pointers handed to it by another runtime, or a
+ * serving process whose memory pool owns the whole device and forbids
+ * cudaMalloc once it is running.
+ *
+ * Same inputs, outputs and results as hmm_ip_topk_f32.  Its scratch lives in
+ * a fixed array of HMM_NOALLOC_SCRATCH_BYTES in device memory inside this
+ * library (every GPU that loads the library holds it until the process
+ * exits); it calls no cudaMalloc, cudaFree or other allocating routine.
+ *   - Problems whose scratch need (the value hmm_ip_topk_f32_workspace_size
+ *     returns) exceeds HMM_NOALLOC_SCRATCH_BYTES are rejected with
+ *     HMM_ERR_UNSUPPORTED; config-1 sized calls (65,536 x 128 rows, 64
+ *     queries, k = 64) need about 2 MiB.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - Every call on a device shares the one array, which keeps the previous
+ *     call's contents (nothing in it needs to start at zero: each call writes
+ *     every slot it later reads).  Calls that overlap on the same GPU - on
+ *     different streams, or from different host threads - race on the array
+ *     and must be serialised by the caller. */
+#define HMM_NOALLOC_SCRATCH_BYTES (4u << 20)
+hmm_status_t hmm_ip_topk_f32_noalloc(const float* mem, int64_t n_rows, int64_t dim,
+                                     const float* queries, int64_t n_queries, int64_t k,
+                                     int32_t* out_idx, float* out_scores, float threshold,
+                                     uint64_t* out_bitmap, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
