@@ -1,0 +1,567 @@
+// flat_tc.cu — tcgen05 (5th-gen tensor core) scoring of a bf16 row shard with
+// exact top-k selection: the sharded flat-retrieval hot path (inner product
+// of reference steps/example_kernel/inner_product_compute.cpp:11-31 fused
+// with the top-k of topk_retrieval.cpp:13-31), bit-exact to the reference's
+// sequential fp32 arithmetic.
+//
+// Tensor cores sum in their own order, so their scores are approximations.
+// The kernel uses them only to decide which (row, query) pairs can matter:
+//   s~ = tensor-core score of row r for query q (fp32 accumulate in TMEM)
+//   |s~ - s| <= EPS * max_j|a_rj| * sum_j|b_qj|   (s = the reference's score)
+// A pair is rescored exactly - fp32 multiply-add in ascending j from the row
+// tile still resident in shared memory, which rounds exactly as the
+// reference's separate multiply and add because bf16 products are exact in
+// fp32 - only when its upper bound s~ + margin reaches the query's current
+// threshold.  Exact (score, row) composites that beat the threshold enter a
+// per-query candidate pool in global memory; each time a pool reaches a
+// power-of-two fill mark, the warp that filled it computes the pool's k-th
+// best composite and raises the query's threshold (a k-th best of a subset
+// never exceeds the k-th best of the whole memory, so no true top-k row is
+// ever dropped).  A final merge takes the exact top-k of each pool.
+//
+// The threshold is seeded with the exact top-k of the first SEED_ROWS rows
+// (CUDA-core kernel of flat_topk.cu), so the first tiles already filter.
+//
+// Kernel layout (one persistent CTA per SM, 12 warps):
+//   warp 0      TMA producer: 128-row x 128-col bf16 tiles (two 64-column
+//               boxes, 128-byte swizzle) into a 4-stage ring
+//   warp 1      MMA issuer: 8 x tcgen05.mma (M=128, N=nq<=256, K=16) per tile
+//               into one of two TMEM accumulators (2 x 256 fp32 columns)
+//   warp 2      TMEM allocator
+//   warps 4-11  two epilogue warpgroups, alternating tiles: tcgen05.ld the
+//               accumulator, filter, rescore, append, release TMEM and smem
+// The queries (B operand, 256 x 128 bf16 = 64 KiB) stay in shared memory for
+// the whole kernel.  Every mbarrier wait is bounded; a wait that gives up
+// sets a status word and the CTA drains and exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "hmm_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace hmm {
+
+// from flat_topk.cu: the exact CUDA-core path (seed sample and small shards)
+hmm_status_t flat_bf16_exact(const uint16_t* mem, int64_t n, int64_t dim, const uint16_t* qry,
+                             int64_t nq, int64_t k, int64_t row_offset, int64_t* out_idx,
+                             float* out_scores, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t flat_bf16_exact_ws_bytes(int64_t n, int64_t nq, int64_t k);
+hmm_status_t launch_pool_merge(const uint64_t* pool, int64_t cap, const int* counts, int nq,
+                               int k, int64_t row_offset, int64_t* out_idx, float* out_scores,
+                               cudaStream_t st);
+
+namespace {
+
+using namespace sm100;
+
+constexpr int TC_M = 128;                      // rows per tile (MMA M)
+constexpr int TC_NMAX = 256;                   // queries per pass (MMA N)
+constexpr int TC_DIM = 128;                    // row width handled (MMA K total)
+constexpr int STAGES = 4;
+constexpr int A_BOX = TC_M * 128;              // 64 bf16 columns x 128 rows = 16 KiB
+constexpr int A_STAGE = 2 * A_BOX;             // 32 KiB per tile
+constexpr int B_BOX = TC_NMAX * 128;           // 32 KiB
+constexpr int B_BYTES = 2 * B_BOX;             // 64 KiB
+constexpr int NTHREADS = 384;
+constexpr int N_EPI_WARPS = 8;
+constexpr int QCAP = 256;                      // per-warp rescoring queue
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
+constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
+constexpr int SEED_ROWS = 8192;
+constexpr int POOL_CAP = 8192;
+constexpr int KMAX_TC = 128;
+
+struct __align__(8) Ctrl {
+    uint64_t a_full[STAGES];
+    uint64_t a_empty[STAGES];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t b_full;
+    uint32_t tmem_base;
+    int abort;
+    uint64_t tau[TC_NMAX];          // CTA copy of each query's threshold composite
+    float2 qt[TC_NMAX];             // (sum_j |b_qj| with margin, threshold score)
+    uint32_t queue[N_EPI_WARPS][QCAP];
+    unsigned hist[N_EPI_WARPS][256];
+};
+
+constexpr size_t TC_SMEM = 1024 /* alignment slack */ + B_BYTES + STAGES * A_STAGE + sizeof(Ctrl);
+
+struct TcArgs {
+    int64_t n_rows;
+    int64_t row_begin;
+    int n_tiles;
+    int nq;
+    int nqp;                 // nq rounded up to 16 (MMA N)
+    int k;
+    int pool_cap;
+    int wm0;                 // first fill mark that triggers a threshold raise
+    const uint16_t* qry;     // [nq][128]
+    uint64_t* tau_global;    // [nq]
+    uint64_t* pool;          // [nq][pool_cap]
+    int* pool_cnt;           // [nq]
+    int* status;             // [0]: timeout flag, [1]: pool overflow flag
+};
+
+__device__ __forceinline__ float tau_score(uint64_t t) {
+    return t == 0ull ? -INFINITY : cand_score(t);
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// The reference's fp32 dot product of row r of the A tile with query q of
+// the B tile, j ascending.  Both tiles are stored as 128-byte rows per
+// 64-column box with the 128-byte swizzle (16-byte chunk c of row r sits at
+// chunk c ^ (r & 7)).
+__device__ __forceinline__ float exact_dot(const unsigned char* As, int r,
+                                           const unsigned char* Bs, int q) {
+    float s = 0.0f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const unsigned char* ar = As + h * A_BOX + r * 128;
+        const unsigned char* br = Bs + h * B_BOX + q * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 a = *reinterpret_cast<const uint4*>(ar + ((c ^ (r & 7)) << 4));
+            const uint4 b = *reinterpret_cast<const uint4*>(br + ((c ^ (q & 7)) << 4));
+            s = fmaf(bf_lo(a.x), bf_lo(b.x), s); s = fmaf(bf_hi(a.x), bf_hi(b.x), s);
+            s = fmaf(bf_lo(a.y), bf_lo(b.y), s); s = fmaf(bf_hi(a.y), bf_hi(b.y), s);
+            s = fmaf(bf_lo(a.z), bf_lo(b.z), s); s = fmaf(bf_hi(a.z), bf_hi(b.z), s);
+            s = fmaf(bf_lo(a.w), bf_lo(b.w), s); s = fmaf(bf_hi(a.w), bf_hi(b.w), s);
+        }
+    }
+    return s;
+}
+
+// max_j |a_rj| over row r of the A tile (chunk order is irrelevant).
+__device__ __forceinline__ float row_absmax(const unsigned char* As, int r) {
+    __nv_bfloat162 m = __floats2bfloat162_rn(0.0f, 0.0f);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint4* p = reinterpret_cast<const uint4*>(As + h * A_BOX + r * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            uint4 a = p[c];
+            a.x &= 0x7fff7fffu; a.y &= 0x7fff7fffu; a.z &= 0x7fff7fffu; a.w &= 0x7fff7fffu;
+            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.x));
+            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.y));
+            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.z));
+            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.w));
+        }
+    }
+    return fmaxf(__low2float(m), __high2float(m));
+}
+
+// Every lane polls (so each observes the phase itself); the warp proceeds
+// only if all lanes saw it, keeping the warp converged either way.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint32_t limit = WAIT_LIMIT) {
+    const bool ok = mbar_wait_bounded(bar, parity, abort, limit);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void set_abort(Ctrl* ctl, int* status) {
+    atomicExch(&ctl->abort, 1);
+    atomicExch(&status[0], 1);
+}
+
+// Rescores the warp's queued pairs exactly and appends the ones that beat
+// their query's threshold to the pools; raises thresholds at fill marks.
+__device__ __noinline__ void flush_queue(Ctrl* ctl, int ew, int qc, const unsigned char* As,
+                                         const unsigned char* Bs, int64_t tile_row0,
+                                         const TcArgs& a) {
+    const int lane = threadIdx.x & 31;
+    for (int base = 0; base < qc; base += 32) {
+        const int i = base + lane;
+        int q = 0, raise = 0;
+        if (i < qc) {
+            const uint32_t e = ctl->queue[ew][i];
+            const int r = (int)(e >> 8);
+            q = (int)(e & 255u);
+            const float s = exact_dot(As, r, Bs, q);
+            const uint64_t E = make_cand(f32_key(s), (uint32_t)(tile_row0 + r));
+            if (E > ctl->tau[q]) {
+                const int pos = atomicAdd(&a.pool_cnt[q], 1);
+                if (pos < a.pool_cap) {
+                    a.pool[(int64_t)q * a.pool_cap + pos] = E;
+                    const int w = pos + 1;
+                    if (w >= a.wm0 && (w & (w - 1)) == 0) raise = w;
+                } else {
+                    atomicExch(&a.status[1], 1);
+                }
+            }
+        }
+        unsigned m = __ballot_sync(0xffffffffu, raise != 0);
+        while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const int W = __shfl_sync(0xffffffffu, raise, src);
+            const int qq = __shfl_sync(0xffffffffu, q, src);
+            const uint64_t T =
+                warp_select_threshold(a.pool + (int64_t)qq * a.pool_cap, W, a.k, ctl->hist[ew]);
+            if (lane == 0 && T != 0ull) {
+                atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
+                          (unsigned long long)T);
+                const unsigned long long old = atomicMax(
+                    reinterpret_cast<unsigned long long*>(&ctl->tau[qq]), (unsigned long long)T);
+                if (T > old) ctl->qt[qq].y = tau_score(T);
+            }
+            __syncwarp();
+        }
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
+                       const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* Bs = smem;
+    unsigned char* As = smem + B_BYTES;
+    Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + B_BYTES + STAGES * A_STAGE);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x;
+    const int my_tiles = (int)blockIdx.x < a.n_tiles ? (a.n_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    volatile int* abort = &ctl->abort;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&ctl->a_full[s], 1);
+            mbar_init(&ctl->a_empty[s], 128);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->acc_full[b], 1);
+            mbar_init(&ctl->acc_empty[b], 128);
+        }
+        mbar_init(&ctl->b_full, 1);
+        ctl->abort = 0;
+        fence_barrier_init();
+    }
+    for (int q = threadIdx.x; q < TC_NMAX; q += NTHREADS) {
+        float l1 = 0.0f;
+        uint64_t t = ~0ull;
+        if (q < a.nq) {
+            const uint16_t* p = a.qry + (int64_t)q * TC_DIM;
+            for (int j = 0; j < TC_DIM; ++j) l1 += fabsf(bf16_bits_to_f32(p[j]));
+            l1 *= 1.0f + 1.0f / 256.0f;   // covers the rounding of this sum
+            t = a.tau_global[q];
+        }
+        ctl->tau[q] = t;
+        ctl->qt[q] = make_float2(l1, q < a.nq ? tau_score(t) : INFINITY);
+    }
+    if (warp == 2) {
+        tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tmap(&tmA);
+            prefetch_tmap(&tmB);
+            mbar_expect_tx(&ctl->b_full, B_BYTES);
+            tma_load_2d(Bs, &tmB, &ctl->b_full, 0, 0);
+            tma_load_2d(Bs + B_BOX, &tmB, &ctl->b_full, 64, 0);
+        }
+        int issued = 0;
+        for (int i = 0; i < my_tiles; ++i) {
+            const int s = i % STAGES;
+            if (!warp_wait(&ctl->a_empty[s], ((i / STAGES) & 1) ^ 1, abort)) {
+                if (lane == 0) set_abort(ctl, a.status);
+                break;
+            }
+            if (lane == 0) {
+                const int y = (int)(a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M);
+                mbar_expect_tx(&ctl->a_full[s], A_STAGE);
+                tma_load_2d(As + s * A_STAGE, &tmA, &ctl->a_full[s], 0, y);
+                tma_load_2d(As + s * A_STAGE + A_BOX, &tmA, &ctl->a_full[s], 64, y);
+            }
+            __syncwarp();
+            issued = i + 1;
+        }
+        if (*abort) {
+            // drain: the latest arming of each stage must land before exit
+            for (int i = max(0, issued - STAGES); i < issued; ++i)
+                mbar_wait_bounded(&ctl->a_full[i % STAGES], (i / STAGES) & 1, abort, 1u << 20);
+            mbar_wait_bounded(&ctl->b_full, 0, abort, 1u << 20);
+        }
+    } else if (warp == 1) {
+        // -------------------------------------------------------- MMA issuer
+        const uint32_t idesc = idesc_f16(TC_M, a.nqp, 1);
+        int last = -1;
+        bool ok = warp_wait(&ctl->b_full, 0, abort);
+        if (!ok && lane == 0) set_abort(ctl, a.status);
+        for (int i = 0; ok && i < my_tiles; ++i) {
+            const int s = i % STAGES, b = i & 1;
+            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort) ||
+                !warp_wait(&ctl->acc_empty[b], ((i >> 1) & 1) ^ 1, abort)) {
+                if (lane == 0) set_abort(ctl, a.status);
+                break;
+            }
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t a0 = smem_u32(As + s * A_STAGE), b0 = smem_u32(Bs);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f16(tmem + b * TC_NMAX, desc_k_sw128(a0 + h * A_BOX + ks * 32),
+                                desc_k_sw128(b0 + h * B_BOX + ks * 32), idesc, (h | ks) != 0);
+                mma_commit(&ctl->acc_full[b]);
+            }
+            __syncwarp();
+            last = i;
+        }
+        if (*abort && last >= 0)
+            mbar_wait_bounded(&ctl->acc_full[last & 1], (last >> 1) & 1, abort, 1u << 20);
+    } else if (warp >= 4) {
+        // --------------------------------------------------------- epilogue
+        const int ew = warp - 4;            // 0..7
+        const int g = ew >> 2;              // warpgroup: tiles with i % 2 == g
+        const int sub = warp & 3;           // TMEM lanes 32*sub .. +31
+        const int r = sub * 32 + lane;      // tile row of this thread
+        bool ok = warp_wait(&ctl->b_full, 0, abort);
+        if (!ok && lane == 0) set_abort(ctl, a.status);
+        const int nchunks = a.nqp / 32 + ((a.nqp & 31) ? 1 : 0);
+        for (int i = g; ok && i < my_tiles; i += 2) {
+            const int s = i % STAGES, b = i & 1;
+            if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort) ||
+                !warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort)) {
+                if (lane == 0) set_abort(ctl, a.status);
+                break;
+            }
+            tc_fence_after();
+            const unsigned char* At = As + s * A_STAGE;
+            const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
+            const bool valid = tile_row0 + r < a.n_rows;
+
+            // refresh this warp's 32 queries from the shared thresholds
+            {
+                const int q = ew * 32 + lane;
+                if (q < a.nq) {
+                    const uint64_t t = *reinterpret_cast<volatile uint64_t*>(&a.tau_global[q]);
+                    if (t > ctl->tau[q]) {
+                        const unsigned long long old = atomicMax(
+                            reinterpret_cast<unsigned long long*>(&ctl->tau[q]),
+                            (unsigned long long)t);
+                        if (t > old) ctl->qt[q].y = tau_score(t);
+                    }
+                }
+            }
+            const float er = EPS * row_absmax(At, r);
+            int qc = 0;
+            for (int c = 0; c < nchunks; ++c) {
+                uint32_t v[32];
+                tmem_ld_x32(tmem + (uint32_t)(b * TC_NMAX) + ((uint32_t)(sub * 32) << 16) +
+                                (uint32_t)(c * 32),
+                            v);
+                tmem_wait_ld();
+                const int rem = a.nq - c * 32;
+                const uint32_t qmask = rem >= 32 ? 0xffffffffu : (rem > 0 ? (1u << rem) - 1u : 0u);
+                uint32_t bits = 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float2 t = ctl->qt[c * 32 + j];
+                    const float U = fmaf(er, t.x, __uint_as_float(v[j]));
+                    bits |= (uint32_t)(!(U < t.y)) << j;
+                }
+                bits = valid ? (bits & qmask) : 0u;
+                while (__any_sync(0xffffffffu, bits != 0)) {
+                    const bool has = bits != 0;
+                    const int j = has ? __ffs(bits) - 1 : 0;
+                    bits &= bits - 1;
+                    const unsigned m = __ballot_sync(0xffffffffu, has);
+                    if (has)
+                        ctl->queue[ew][qc + __popc(m & ((1u << lane) - 1u))] =
+                            ((uint32_t)r << 8) | (uint32_t)(c * 32 + j);
+                    qc += __popc(m);
+                    if (qc > QCAP - 32) {
+                        __syncwarp();
+                        flush_queue(ctl, ew, qc, At, Bs, tile_row0, a);
+                        qc = 0;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&ctl->acc_empty[b]);
+            __syncwarp();
+            if (qc > 0) flush_queue(ctl, ew, qc, At, Bs, tile_row0, a);
+            mbar_arrive(&ctl->a_empty[s]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// Seeds each query's pool with the exact top-k of the sample rows and sets
+// its starting threshold to the k-th of them.
+__global__ void seed_pool_kernel(const int64_t* __restrict__ seed_idx,
+                                 const float* __restrict__ seed_sc, int nq, int k,
+                                 uint64_t* __restrict__ pool, int pool_cap, int* __restrict__ cnt,
+                                 uint64_t* __restrict__ tau) {
+    const int q = blockIdx.x;
+    __shared__ int m;
+    if (threadIdx.x == 0) m = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const int64_t r = seed_idx[(int64_t)q * k + i];
+        if (r >= 0) {
+            pool[(int64_t)q * pool_cap + i] = make_cand(f32_key(seed_sc[(int64_t)q * k + i]),
+                                                        (uint32_t)r);
+            atomicAdd(&m, 1);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        cnt[q] = m;
+        tau[q] = m == k ? pool[(int64_t)q * pool_cap + k - 1] : 0ull;
+    }
+}
+
+// ----------------------------------------------------------- host helpers
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Row-major bf16 matrix [rows][128] as a 2-D tensor map with a
+// {64 columns, box_rows rows} box and the 128-byte swizzle.
+hmm_status_t make_tmap_bf16(CUtensorMap* m, const void* base, int64_t rows, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(HMM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)TC_DIM, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)TC_DIM * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(HMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return HMM_OK;
+}
+
+struct TcLayout {
+    size_t pool, cnt, tau, status, seed_idx, seed_sc, seed_ws, total;
+};
+
+TcLayout tc_layout(int64_t n, int64_t nq_pass, int64_t k) {
+    TcLayout L;
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    size_t o = 0;
+    L.pool = o; o += up(sizeof(uint64_t) * nq_pass * POOL_CAP);
+    L.cnt = o; o += up(sizeof(int) * nq_pass);
+    L.tau = o; o += up(sizeof(uint64_t) * nq_pass);
+    L.status = o; o += up(sizeof(int) * 4);
+    L.seed_idx = o; o += up(sizeof(int64_t) * nq_pass * k);
+    L.seed_sc = o; o += up(sizeof(float) * nq_pass * k);
+    L.seed_ws = o; o += up(flat_bf16_exact_ws_bytes(std::min<int64_t>(n, SEED_ROWS), nq_pass, k));
+    L.total = o;
+    return L;
+}
+
+}  // namespace
+
+bool tc_path_applies(int64_t n, int64_t dim, int64_t nq, int64_t k, const void* mem,
+                     const void* qry) {
+    return dim == TC_DIM && k >= 1 && k <= KMAX_TC && nq >= 1 && n > SEED_ROWS &&
+           (reinterpret_cast<uintptr_t>(mem) % 16) == 0 &&
+           (reinterpret_cast<uintptr_t>(qry) % 16) == 0;
+}
+
+size_t tc_ws_bytes(int64_t n, int64_t nq, int64_t k) {
+    return tc_layout(n, std::min<int64_t>(nq, TC_NMAX), k).total + 256;
+}
+
+// Scores one shard on tensor cores and returns its exact top-k (int64 rows
+// + row_offset, fp32 scores), query passes of at most 256.
+hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, int64_t nq,
+                          int64_t k, int64_t row_offset, int64_t* out_idx, float* out_scores,
+                          void* ws, size_t ws_bytes, cudaStream_t st) {
+    HMM_REQUIRE(n < (int64_t(1) << 31), "n_rows must be < 2^31");
+    HMM_CUDA_TRY(cudaFuncSetAttribute(tc_score_select_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
+    const int64_t seed = std::min<int64_t>(n, SEED_ROWS);
+    CUtensorMap tmA;
+    hmm_status_t s = make_tmap_bf16(&tmA, mem, n, TC_M);
+    if (s != HMM_OK) return s;
+    const int sms = device_sm_count();
+    for (int64_t q0 = 0; q0 < nq; q0 += TC_NMAX) {
+        const int nqp_pass = (int)std::min<int64_t>(TC_NMAX, nq - q0);
+        const TcLayout L = tc_layout(n, nqp_pass, k);
+        if (ws_bytes < L.total)
+            return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", ws_bytes, L.total);
+        unsigned char* w = static_cast<unsigned char*>(ws);
+        uint64_t* pool = reinterpret_cast<uint64_t*>(w + L.pool);
+        int* cnt = reinterpret_cast<int*>(w + L.cnt);
+        uint64_t* tau = reinterpret_cast<uint64_t*>(w + L.tau);
+        int* status = reinterpret_cast<int*>(w + L.status);
+        int64_t* seed_idx = reinterpret_cast<int64_t*>(w + L.seed_idx);
+        float* seed_sc = reinterpret_cast<float*>(w + L.seed_sc);
+        const uint16_t* qp = qry + q0 * TC_DIM;
+
+        HMM_CUDA_TRY(cudaMemsetAsync(pool, 0, sizeof(uint64_t) * nqp_pass * POOL_CAP, st));
+        HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int) * 4, st));
+        s = flat_bf16_exact(mem, seed, TC_DIM, qp, nqp_pass, k, 0, seed_idx, seed_sc,
+                            w + L.seed_ws, L.total - L.seed_ws, st);
+        if (s != HMM_OK) return s;
+        seed_pool_kernel<<<nqp_pass, 128, 0, st>>>(seed_idx, seed_sc, nqp_pass, (int)k, pool,
+                                                    POOL_CAP, cnt, tau);
+        s = check_launch("seed_pool_kernel");
+        if (s != HMM_OK) return s;
+
+        CUtensorMap tmB;
+        s = make_tmap_bf16(&tmB, qp, nqp_pass, TC_NMAX);
+        if (s != HMM_OK) return s;
+        TcArgs a;
+        a.n_rows = n;
+        a.row_begin = seed;
+        a.n_tiles = (int)((n - seed + TC_M - 1) / TC_M);
+        a.nq = nqp_pass;
+        a.nqp = (nqp_pass + 15) & ~15;
+        a.k = (int)k;
+        a.pool_cap = POOL_CAP;
+        a.wm0 = std::max(256, next_pow2(2 * (int)k));
+        a.qry = qp;
+        a.tau_global = tau;
+        a.pool = pool;
+        a.pool_cnt = cnt;
+        a.status = status;
+        const int grid = std::min(sms, a.n_tiles);
+        tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
+        s = check_launch("tc_score_select_kernel");
+        if (s != HMM_OK) return s;
+        s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, row_offset,
+                              out_idx + q0 * k, out_scores + q0 * k, st);
+        if (s != HMM_OK) return s;
+    }
+    return HMM_OK;
+}
+
+}  // namespace hmm

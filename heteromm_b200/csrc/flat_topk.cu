@@ -271,13 +271,15 @@ scores_topk_partition_kernel(const float* __restrict__ scores, int64_t n, int k,
 template <typename IdxT>
 __global__ void __launch_bounds__(256)
 merge_candidates_kernel(const uint64_t* __restrict__ cand, int64_t M, int k, int64_t row_offset,
-                        IdxT* __restrict__ out_idx, float* __restrict__ out_scores) {
+                        IdxT* __restrict__ out_idx, float* __restrict__ out_scores,
+                        const int* __restrict__ counts) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint64_t* best = reinterpret_cast<uint64_t*>(smem_raw);
     __shared__ unsigned sm[300];
     __shared__ int cnt;
     const int q = blockIdx.x;
     const uint64_t* src = cand + (int64_t)q * M;
+    if (counts && (int64_t)counts[q] < M) M = counts[q];   // per-query fill (pools)
     const int kp = next_pow2(k);
     const uint64_t T = block_select_threshold(src, M, k, sm);
     if (threadIdx.x == 0) cnt = 0;
@@ -425,7 +427,7 @@ hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const 
     hmm_status_t ms = prepare_merge_kernel<IdxT>();
     if (ms != HMM_OK) return ms;
     merge_candidates_kernel<IdxT><<<(unsigned)nq, 256, msmem, st>>>(
-        cand, (int64_t)p.n_parts * k, (int)k, row_offset, out_idx, out_scores);
+        cand, (int64_t)p.n_parts * k, (int)k, row_offset, out_idx, out_scores, nullptr);
     return check_launch("merge_candidates_kernel");
 }
 
@@ -435,6 +437,36 @@ size_t fused_ws_bytes(int64_t n, int64_t nq, int64_t k) {
 }
 
 }  // namespace
+// ---- entry points shared with the tensor-core path (flat_tc.cu)
+
+hmm_status_t flat_bf16_exact(const uint16_t* mem, int64_t n, int64_t dim, const uint16_t* qry,
+                             int64_t nq, int64_t k, int64_t row_offset, int64_t* out_idx,
+                             float* out_scores, void* ws, size_t ws_bytes, cudaStream_t st) {
+    return run_fused<BF16In, int64_t>(mem, n, dim, qry, nq, k, row_offset, out_idx, out_scores,
+                                      0.0f, nullptr, nullptr, ws, ws_bytes, st,
+                                      fused_ws_bytes(n, nq, k));
+}
+
+size_t flat_bf16_exact_ws_bytes(int64_t n, int64_t nq, int64_t k) { return fused_ws_bytes(n, nq, k); }
+
+hmm_status_t launch_pool_merge(const uint64_t* pool, int64_t cap, const int* counts, int nq,
+                               int k, int64_t row_offset, int64_t* out_idx, float* out_scores,
+                               cudaStream_t st) {
+    hmm_status_t s = prepare_merge_kernel<int64_t>();
+    if (s != HMM_OK) return s;
+    const size_t msmem = sizeof(uint64_t) * next_pow2(k);
+    merge_candidates_kernel<int64_t><<<(unsigned)nq, 256, msmem, st>>>(
+        pool, cap, k, row_offset, out_idx, out_scores, counts);
+    return check_launch("merge_candidates_kernel(pool)");
+}
+
+bool tc_path_applies(int64_t n, int64_t dim, int64_t nq, int64_t k, const void* mem,
+                     const void* qry);
+size_t tc_ws_bytes(int64_t n, int64_t nq, int64_t k);
+hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, int64_t nq,
+                          int64_t k, int64_t row_offset, int64_t* out_idx, float* out_scores,
+                          void* ws, size_t ws_bytes, cudaStream_t st);
+
 // Scratch of hmm_ip_topk_f32_noalloc: a fixed device array, so that the
 // entry point never allocates.  Host code may not use `g_noalloc_scratch` as
 // a device address; it looks the address up per device with
@@ -526,7 +558,8 @@ hmm_status_t hmm_topk_f32(const float* scores, int64_t n, int64_t n_queries, int
     auto mk = merge_candidates_kernel<int32_t>;
     hmm_status_t ms = prepare_merge_kernel<int32_t>();
     if (ms != HMM_OK) return ms;
-    mk<<<(unsigned)n_queries, 256, msmem, st>>>(cand, parts * k, (int)k, 0, out_idx, out_scores);
+    mk<<<(unsigned)n_queries, 256, msmem, st>>>(cand, parts * k, (int)k, 0, out_idx, out_scores,
+                                                nullptr);
     return check_launch("merge_candidates_kernel");
 }
 
@@ -565,9 +598,12 @@ hmm_status_t hmm_ip_topk_f32(const float* mem, int64_t n_rows, int64_t dim,
 
 size_t hmm_ip_topk_bf16_workspace_size(int64_t n_rows, int64_t dim, int64_t n_queries,
                                        int64_t k) {
-    (void)dim;
     if (n_rows < 0 || n_queries < 0 || k < 1) return 0;
-    return fused_ws_bytes(n_rows, n_queries, k);
+    const size_t v0 = fused_ws_bytes(n_rows, n_queries, k);
+    // the tensor-core path applies for aligned pointers; size for it whenever the shape fits
+    if (dim == 128 && k <= 128 && n_rows > 8192 && n_queries >= 1)
+        return std::max(v0, tc_ws_bytes(n_rows, n_queries, k));
+    return v0;
 }
 
 hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
@@ -578,6 +614,12 @@ hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
     if (s != HMM_OK) return s;
     HMM_REQUIRE(row_offset >= 0, "row_offset must be >= 0");
     HMM_REQUIRE(n_queries == 0 || out_scores, "out_scores is null");
+    HMM_REQUIRE(n_queries == 0 || out_idx, "out_idx is null");
+    if (n_queries > 0 && tc_path_applies(n_rows, dim, n_queries, k, mem, queries)) {
+        if (!workspace) return set_error(HMM_ERR_OOM, "workspace is null");
+        return flat_bf16_tc(mem, n_rows, queries, n_queries, k, row_offset, out_idx, out_scores,
+                            workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+    }
     return run_fused<BF16In, int64_t>(mem, n_rows, dim, queries, n_queries, k, row_offset,
                                       out_idx, out_scores, 0.0f, nullptr, nullptr, workspace,
                                       workspace_bytes, static_cast<cudaStream_t>(stream),

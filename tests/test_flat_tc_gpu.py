@@ -1,0 +1,78 @@
+"""GPU parity of the tensor-core (tcgen05) bf16 scoring path with exact
+top-k selection (hmm_ip_topk_bf16 for dim 128, k <= 128, n > 8192 rows)
+against the oracle: bit-exact indices and scores."""
+import numpy as np
+import pytest
+import torch
+
+import gen
+import heteromm_b200 as hmm
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, device):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def run(cuda, mem, qry, k, off=0):
+    idx, sc = hmm.ip_topk_bf16(dev(mem.view(np.int16), cuda), dev(qry.view(np.int16), cuda), k, off)
+    torch.cuda.synchronize()
+    return idx.cpu().numpy(), sc.cpu().numpy()
+
+
+@pytest.mark.parametrize("n,nq,k,seed", [
+    (20000, 16, 100, 1),      # a few tiles per SM
+    (12345, 1, 64, 2),        # one query (MMA N = 16), ragged last tile
+    (9000, 300, 32, 3),       # two query passes (256 + 44)
+    (300000, 256, 100, 4),    # every SM busy for many tiles
+])
+def test_tc_matches_oracle(cuda, n, nq, k, seed):
+    mem = gen.bf16_bits(gen.normal_f32(seed * 7, (n, 128)))
+    qry = gen.bf16_bits(gen.normal_f32(seed * 7 + 1, (nq, 128)))
+    idx, sc = run(cuda, mem, qry, k, 1000)
+    oidx, osc = O.ip_topk_bf16(mem, qry, k, 1000)
+    assert np.array_equal(idx, oidx)
+    assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
+
+
+def test_tc_duplicate_rows_and_ties(cuda):
+    """Many identical rows: every copy ties, only the lowest indices may win."""
+    n, nq, k = 30000, 8, 100
+    base = gen.bf16_bits(gen.normal_f32(51, (500, 128)))
+    mem = base[np.arange(n) % 500]
+    qry = gen.bf16_bits(gen.normal_f32(52, (nq, 128)))
+    idx, sc = run(cuda, mem, qry, k)
+    oidx, osc = O.ip_topk_bf16(mem, qry, k)
+    assert np.array_equal(idx, oidx)
+    assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
+
+
+def test_tc_large_magnitudes_and_zero_rows(cuda):
+    n, nq, k = 20000, 4, 50
+    x = gen.normal_f32(61, (n, 128))
+    x[::3] *= 1e4
+    x[5::7] = 0.0
+    mem = gen.bf16_bits(x)
+    qry = gen.bf16_bits(gen.normal_f32(62, (nq, 128)) * 100)
+    idx, sc = run(cuda, mem, qry, k)
+    oidx, osc = O.ip_topk_bf16(mem, qry, k)
+    assert np.array_equal(idx, oidx)
+    assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
+
+
+def test_tc_sharded_merge(cuda):
+    n, nq, k, shards = 80000, 32, 100, 4
+    mem = gen.bf16_bits(gen.normal_f32(71, (n, 128)))
+    qry = gen.bf16_bits(gen.normal_f32(72, (nq, 128)))
+    per = n // shards
+    cs, ci = [], []
+    for s in range(shards):
+        i, v = hmm.ip_topk_bf16(dev(mem[s * per:(s + 1) * per].view(np.int16), cuda),
+                                dev(qry.view(np.int16), cuda), k, s * per)
+        cs.append(v); ci.append(i)
+    ms, mi = hmm.shard_merge_topk(torch.stack(cs), torch.stack(ci), k)
+    oidx, osc = O.ip_topk_bf16(mem, qry, k)
+    assert np.array_equal(mi.cpu().numpy(), oidx)
+    assert np.array_equal(ms.cpu().numpy().view(np.uint32), osc.view(np.uint32))
