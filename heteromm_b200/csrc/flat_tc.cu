@@ -68,13 +68,15 @@ constexpr int B_BOX = TC_NMAX * 128;           // 32 KiB
 constexpr int B_BYTES = 2 * B_BOX;             // 64 KiB
 constexpr int NTHREADS = 384;
 constexpr int N_EPI_WARPS = 8;
-constexpr int QCAP = 256;                      // per-warp rescoring queue
+constexpr int QCAP = 128;                      // per-warp rescoring queue (deferred across tiles)
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t WAIT_LIMIT = 1u << 26;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
 constexpr int SEED_ROWS = 8192;
 constexpr int POOL_CAP = 8192;
 constexpr int KMAX_TC = 128;
+constexpr int RAISE_STEP = 256;                // appends between threshold raises
+constexpr int ER_RING = 8;                     // tiles of margins in flight (> epilogue lag)
 
 struct __align__(8) Ctrl {
     uint64_t a_full[STAGES];
@@ -86,8 +88,12 @@ struct __align__(8) Ctrl {
     int abort;
     uint64_t tau[TC_NMAX];          // CTA copy of each query's threshold composite
     float2 qt[TC_NMAX];             // (sum_j |b_qj| with margin, threshold score)
-    uint32_t queue[N_EPI_WARPS][QCAP];
+    uint64_t queue[N_EPI_WARPS][QCAP];   // (shard row << 8) | query
     unsigned hist[N_EPI_WARPS][256];
+    float wt[N_EPI_WARPS][TC_NMAX]; // per-warp, per-tile score thresholds
+    float l1max;                    // max over queries of sum_j |b_qj|
+    uint64_t er_full[ER_RING];      // margin of tile i published (64 arrivals)
+    float er_ring[ER_RING][4];      // EPS * max|a| per 32-row quarter of tile i
 };
 
 constexpr size_t TC_SMEM = 1024 /* alignment slack */ + B_BYTES + STAGES * A_STAGE + sizeof(Ctrl);
@@ -102,33 +108,54 @@ struct TcArgs {
     int pool_cap;
     int wm0;                 // first fill mark that triggers a threshold raise
     const uint16_t* qry;     // [nq][128]
+    const uint16_t* mem;     // [n_rows][128], for rescoring
     uint64_t* tau_global;    // [nq]
     uint64_t* pool;          // [nq][pool_cap]
     int* pool_cnt;           // [nq]
-    int* status;             // [0]: timeout flag, [1]: pool overflow flag
+    int* status;             // [0] timeout flag, [1] pool overflow flag,
+                             // [2] pairs rescored, [3] threshold raises
 };
 
 __device__ __forceinline__ float tau_score(uint64_t t) {
     return t == 0ull ? -INFINITY : cand_score(t);
 }
 
+// (a0 - b0, a1 - b1) in one packed fp32x2 subtraction (round to nearest).
+__device__ __forceinline__ float2 sub_f32x2(float a0, float a1, float b0, float b1) {
+    unsigned long long A, B, D;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(B) : "f"(b0), "f"(b1));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(D) : "l"(A), "l"(B));
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(D));
+    return r;
+}
+
+// max of three, NaN if any input is NaN.
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// The reference's fp32 dot product of row r of the A tile with query q of
-// the B tile, j ascending.  Both tiles are stored as 128-byte rows per
-// 64-column box with the 128-byte swizzle (16-byte chunk c of row r sits at
-// chunk c ^ (r & 7)).
-__device__ __forceinline__ float exact_dot(const unsigned char* As, int r,
-                                           const unsigned char* Bs, int q) {
+// The reference's fp32 dot product of a row with query q of the B tile,
+// j ascending.  The B tile is stored as 128-byte rows per 64-column box with
+// the 128-byte swizzle (16-byte chunk c of row q sits at chunk c ^ (q & 7)).
+// The row is read from global memory: the tile's shared-memory copy may
+// already be recycled, and the row was just streamed, so it is in L2.
+__device__ __forceinline__ float exact_dot_row(const uint16_t* __restrict__ row,
+                                               const unsigned char* Bs, int q) {
     float s = 0.0f;
+    const uint4* rp = reinterpret_cast<const uint4*>(row);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-        const unsigned char* ar = As + h * A_BOX + r * 128;
         const unsigned char* br = Bs + h * B_BOX + q * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            const uint4 a = *reinterpret_cast<const uint4*>(ar + ((c ^ (r & 7)) << 4));
+            const uint4 a = __ldg(rp + h * 8 + c);
             const uint4 b = *reinterpret_cast<const uint4*>(br + ((c ^ (q & 7)) << 4));
             s = fmaf(bf_lo(a.x), bf_lo(b.x), s); s = fmaf(bf_hi(a.x), bf_hi(b.x), s);
             s = fmaf(bf_lo(a.y), bf_lo(b.y), s); s = fmaf(bf_hi(a.y), bf_hi(b.y), s);
@@ -147,7 +174,7 @@ __device__ __forceinline__ float row_absmax(const unsigned char* As, int r) {
         const uint4* p = reinterpret_cast<const uint4*>(As + h * A_BOX + r * 128);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            uint4 a = p[c];
+            uint4 a = p[c ^ (r & 7)];   // lanes of a quarter-warp hit distinct banks
             a.x &= 0x7fff7fffu; a.y &= 0x7fff7fffu; a.z &= 0x7fff7fffu; a.w &= 0x7fff7fffu;
             m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.x));
             m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.y));
@@ -161,7 +188,7 @@ __device__ __forceinline__ float row_absmax(const unsigned char* As, int r) {
 // Every lane polls (so each observes the phase itself); the warp proceeds
 // only if all lanes saw it, keeping the warp converged either way.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint32_t limit = WAIT_LIMIT) {
+                                          uint64_t limit = WAIT_LIMIT_NS) {
     const bool ok = mbar_wait_bounded(bar, parity, abort, limit);
     return __all_sync(0xffffffffu, ok);
 }
@@ -173,25 +200,25 @@ __device__ __forceinline__ void set_abort(Ctrl* ctl, int* status) {
 
 // Rescores the warp's queued pairs exactly and appends the ones that beat
 // their query's threshold to the pools; raises thresholds at fill marks.
-__device__ __noinline__ void flush_queue(Ctrl* ctl, int ew, int qc, const unsigned char* As,
-                                         const unsigned char* Bs, int64_t tile_row0,
-                                         const TcArgs& a) {
+__device__ __forceinline__ void flush_queue(Ctrl* ctl, int ew, int qc,
+                                         const unsigned char* Bs, const TcArgs& a) {
     const int lane = threadIdx.x & 31;
+    if (lane == 0) atomicAdd(&a.status[2], qc);
     for (int base = 0; base < qc; base += 32) {
         const int i = base + lane;
         int q = 0, raise = 0;
         if (i < qc) {
-            const uint32_t e = ctl->queue[ew][i];
-            const int r = (int)(e >> 8);
+            const uint64_t e = ctl->queue[ew][i];
+            const int64_t row = (int64_t)(e >> 8);
             q = (int)(e & 255u);
-            const float s = exact_dot(As, r, Bs, q);
-            const uint64_t E = make_cand(f32_key(s), (uint32_t)(tile_row0 + r));
+            const float s = exact_dot_row(a.mem + row * TC_DIM, Bs, q);
+            const uint64_t E = make_cand(f32_key(s), (uint32_t)row);
             if (E > ctl->tau[q]) {
                 const int pos = atomicAdd(&a.pool_cnt[q], 1);
                 if (pos < a.pool_cap) {
                     a.pool[(int64_t)q * a.pool_cap + pos] = E;
                     const int w = pos + 1;
-                    if (w >= a.wm0 && (w & (w - 1)) == 0) raise = w;
+                    if (w >= a.wm0 && (w % RAISE_STEP) == 0) raise = w;
                 } else {
                     atomicExch(&a.status[1], 1);
                 }
@@ -205,6 +232,7 @@ __device__ __noinline__ void flush_queue(Ctrl* ctl, int ew, int qc, const unsign
             const int qq = __shfl_sync(0xffffffffu, q, src);
             const uint64_t T =
                 warp_select_threshold(a.pool + (int64_t)qq * a.pool_cap, W, a.k, ctl->hist[ew]);
+            if (lane == 0) atomicAdd(&a.status[3], 1);
             if (lane == 0 && T != 0ull) {
                 atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
                           (unsigned long long)T);
@@ -222,8 +250,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base, derived by pointer arithmetic so that the
+    // compiler keeps every access below in the shared address space
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* Bs = smem;
     unsigned char* As = smem + B_BYTES;
     Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + B_BYTES + STAGES * A_STAGE);
@@ -236,16 +265,19 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&ctl->a_full[s], 1);
-            mbar_init(&ctl->a_empty[s], 128);
+            mbar_init(&ctl->a_empty[s], 64 + 1);   // margin warps + the MMA commit
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->acc_full[b], 1);
             mbar_init(&ctl->acc_empty[b], 128);
         }
         mbar_init(&ctl->b_full, 1);
+        for (int e = 0; e < ER_RING; ++e) mbar_init(&ctl->er_full[e], 64);
         ctl->abort = 0;
+        ctl->l1max = 0.0f;
         fence_barrier_init();
     }
+    __syncthreads();
     for (int q = threadIdx.x; q < TC_NMAX; q += NTHREADS) {
         float l1 = 0.0f;
         uint64_t t = ~0ull;
@@ -257,6 +289,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         ctl->tau[q] = t;
         ctl->qt[q] = make_float2(l1, q < a.nq ? tau_score(t) : INFINITY);
+        atomicMax(reinterpret_cast<int*>(&ctl->l1max), __float_as_int(l1));   // l1 >= 0
     }
     if (warp == 2) {
         tmem_alloc(&ctl->tmem_base, TMEM_COLS);
@@ -295,8 +328,8 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         if (*abort) {
             // drain: the latest arming of each stage must land before exit
             for (int i = max(0, issued - STAGES); i < issued; ++i)
-                mbar_wait_bounded(&ctl->a_full[i % STAGES], (i / STAGES) & 1, abort, 1u << 20);
-            mbar_wait_bounded(&ctl->b_full, 0, abort, 1u << 20);
+                mbar_wait_bounded(&ctl->a_full[i % STAGES], (i / STAGES) & 1, abort, 100000000ull);
+            mbar_wait_bounded(&ctl->b_full, 0, abort, 100000000ull);
         }
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
@@ -321,12 +354,40 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                         mma_f16(tmem + b * TC_NMAX, desc_k_sw128(a0 + h * A_BOX + ks * 32),
                                 desc_k_sw128(b0 + h * B_BOX + ks * 32), idesc, (h | ks) != 0);
                 mma_commit(&ctl->acc_full[b]);
+                mma_commit(&ctl->a_empty[s]);
             }
             __syncwarp();
             last = i;
         }
         if (*abort && last >= 0)
-            mbar_wait_bounded(&ctl->acc_full[last & 1], (last >> 1) & 1, abort, 1u << 20);
+            mbar_wait_bounded(&ctl->acc_full[last & 1], (last >> 1) & 1, abort, 100000000ull);
+    } else if (warp == 2 || warp == 3) {
+        // ---------------------------------------------- margin (row bound) warps
+        // rows t and t + 64 of every tile (t = 0..63); quarter = rows / 32
+        const int t = (warp - 2) * 32 + lane;
+        for (int i = 0; i < my_tiles; ++i) {
+            const int s = i % STAGES;
+            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort)) {
+                if (lane == 0) set_abort(ctl, a.status);
+                break;
+            }
+            const unsigned char* At = As + s * A_STAGE;
+            const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
+            float e0 = tile_row0 + t < a.n_rows ? __fmul_ru(EPS, row_absmax(At, t)) : 0.0f;
+            float e1 = tile_row0 + t + 64 < a.n_rows ? __fmul_ru(EPS, row_absmax(At, t + 64)) : 0.0f;
+            mbar_arrive(&ctl->a_empty[s]);       // smem reads of this tile are done
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                e0 = fmaxf(e0, __shfl_xor_sync(0xffffffffu, e0, o));
+                e1 = fmaxf(e1, __shfl_xor_sync(0xffffffffu, e1, o));
+            }
+            if (lane == 0) {
+                ctl->er_ring[i % ER_RING][warp - 2] = e0;       // quarter 0 or 1
+                ctl->er_ring[i % ER_RING][warp - 2 + 2] = e1;   // quarter 2 or 3
+            }
+            __syncwarp();
+            mbar_arrive(&ctl->er_full[i % ER_RING]);
+        }
     } else if (warp >= 4) {
         // --------------------------------------------------------- epilogue
         const int ew = warp - 4;            // 0..7
@@ -336,47 +397,64 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         bool ok = warp_wait(&ctl->b_full, 0, abort);
         if (!ok && lane == 0) set_abort(ctl, a.status);
         const int nchunks = a.nqp / 32 + ((a.nqp & 31) ? 1 : 0);
+        int qc = 0;   // queued (row, query) pairs awaiting exact rescoring
         for (int i = g; ok && i < my_tiles; i += 2) {
-            const int s = i % STAGES, b = i & 1;
-            if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort) ||
-                !warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort)) {
+            const int b = i & 1;
+            // ---- off the critical path: the tile's margin is published
+            if (!warp_wait(&ctl->er_full[i % ER_RING], (i / ER_RING) & 1, abort)) {
+                if (lane == 0) set_abort(ctl, a.status);
+                break;
+            }
+            const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
+            const bool valid = tile_row0 + r < a.n_rows;
+
+            // start the load of this warp's 32 shared thresholds; applied after the filter
+            const int qr = ew * 32 + lane;
+            uint64_t t_new = 0;
+            if (qr < a.nq) t_new = *reinterpret_cast<volatile uint64_t*>(&a.tau_global[qr]);
+            const float ER = ctl->er_ring[i % ER_RING][sub];
+            // warp-uniform margin M >= EPS * max|a_r| * sum|b_q| for every row and
+            // query of this warp's tile; threshold per query rounded down, so
+            // s~ + margin >= tau  implies  s~ >= wt
+            const float M = __fmul_ru(ER, ctl->l1max);
+            float* wt = ctl->wt[ew];
+#pragma unroll
+            for (int c = 0; c < TC_NMAX / 32; ++c)
+                wt[c * 32 + lane] = __fsub_rd(ctl->qt[c * 32 + lane].y, M);
+            __syncwarp();
+
+            // ---- critical path: accumulator ready -> filter -> release
+            if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
             tc_fence_after();
-            const unsigned char* At = As + s * A_STAGE;
-            const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
-            const bool valid = tile_row0 + r < a.n_rows;
-
-            // refresh this warp's 32 queries from the shared thresholds
-            {
-                const int q = ew * 32 + lane;
-                if (q < a.nq) {
-                    const uint64_t t = *reinterpret_cast<volatile uint64_t*>(&a.tau_global[q]);
-                    if (t > ctl->tau[q]) {
-                        const unsigned long long old = atomicMax(
-                            reinterpret_cast<unsigned long long*>(&ctl->tau[q]),
-                            (unsigned long long)t);
-                        if (t > old) ctl->qt[q].y = tau_score(t);
-                    }
+            const uint32_t tbase = tmem + (uint32_t)(b * TC_NMAX) + ((uint32_t)(sub * 32) << 16);
+            // filters 32 accumulator columns (queries c*32 ..) of this thread's row
+            auto filter = [&](const uint32_t* v, int c) {
+                // fast test: max_j (s~_j - wt_j) < 0 for the whole chunk (NaN passes)
+                float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 t = *reinterpret_cast<const float4*>(wt + c * 32 + j);
+                    const float2 d0 = sub_f32x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), t.x, t.y);
+                    const float2 d1 =
+                        sub_f32x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]), t.z, t.w);
+                    m0 = max3_nan(m0, d0.x, d0.y);
+                    m1 = max3_nan(m1, d1.x, d1.y);
                 }
-            }
-            const float er = EPS * row_absmax(At, r);
-            int qc = 0;
-            for (int c = 0; c < nchunks; ++c) {
-                uint32_t v[32];
-                tmem_ld_x32(tmem + (uint32_t)(b * TC_NMAX) + ((uint32_t)(sub * 32) << 16) +
-                                (uint32_t)(c * 32),
-                            v);
-                tmem_wait_ld();
+                const bool hit = valid && !(fmaxf(m0, m1) < 0.0f) || (m0 != m0) || (m1 != m1);
+                if (!__any_sync(0xffffffffu, hit)) return;
                 const int rem = a.nq - c * 32;
                 const uint32_t qmask = rem >= 32 ? 0xffffffffu : (rem > 0 ? (1u << rem) - 1u : 0u);
                 uint32_t bits = 0;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float2 t = ctl->qt[c * 32 + j];
-                    const float U = fmaf(er, t.x, __uint_as_float(v[j]));
-                    bits |= (uint32_t)(!(U < t.y)) << j;
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 t = *reinterpret_cast<const float4*>(wt + c * 32 + j);
+                    bits |= (uint32_t)(!(__uint_as_float(v[j + 0]) < t.x)) << (j + 0);
+                    bits |= (uint32_t)(!(__uint_as_float(v[j + 1]) < t.y)) << (j + 1);
+                    bits |= (uint32_t)(!(__uint_as_float(v[j + 2]) < t.z)) << (j + 2);
+                    bits |= (uint32_t)(!(__uint_as_float(v[j + 3]) < t.w)) << (j + 3);
                 }
                 bits = valid ? (bits & qmask) : 0u;
                 while (__any_sync(0xffffffffu, bits != 0)) {
@@ -386,21 +464,38 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                     const unsigned m = __ballot_sync(0xffffffffu, has);
                     if (has)
                         ctl->queue[ew][qc + __popc(m & ((1u << lane) - 1u))] =
-                            ((uint32_t)r << 8) | (uint32_t)(c * 32 + j);
+                            ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
                     qc += __popc(m);
                     if (qc > QCAP - 32) {
                         __syncwarp();
-                        flush_queue(ctl, ew, qc, At, Bs, tile_row0, a);
+                        flush_queue(ctl, ew, qc, Bs, a);
                         qc = 0;
                     }
                 }
+            };
+            // software pipeline: the next chunk's TMEM load is in flight while
+            // the current chunk is filtered
+            uint32_t va[32], vb[32];
+            tmem_ld_x32(tbase, va);
+            tmem_wait_ld();
+            for (int c = 0; c < nchunks; c += 2) {
+                if (c + 1 < nchunks) tmem_ld_x32(tbase + (uint32_t)((c + 1) * 32), vb);
+                filter(va, c);
+                tmem_wait_ld();
+                if (c + 2 < nchunks) tmem_ld_x32(tbase + (uint32_t)((c + 2) * 32), va);
+                if (c + 1 < nchunks) filter(vb, c + 1);
+                tmem_wait_ld();
+            }
+            if (qr < a.nq && t_new > ctl->tau[qr]) {
+                const unsigned long long old = atomicMax(
+                    reinterpret_cast<unsigned long long*>(&ctl->tau[qr]), (unsigned long long)t_new);
+                if (t_new > old) ctl->qt[qr].y = tau_score(t_new);
             }
             tc_fence_before();
             mbar_arrive(&ctl->acc_empty[b]);
             __syncwarp();
-            if (qc > 0) flush_queue(ctl, ew, qc, At, Bs, tile_row0, a);
-            mbar_arrive(&ctl->a_empty[s]);
         }
+        if (qc > 0) flush_queue(ctl, ew, qc, Bs, a);   // B stays resident to the end
     }
 
     tc_fence_before();
@@ -549,6 +644,7 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         a.pool_cap = POOL_CAP;
         a.wm0 = std::max(256, next_pow2(2 * (int)k));
         a.qry = qp;
+        a.mem = mem;
         a.tau_global = tau;
         a.pool = pool;
         a.pool_cnt = cnt;

@@ -50,15 +50,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase with `parity`; gives up after `limit` polls or when
-// *abort becomes nonzero.  Returns false when it gave up.
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes or about `hint_ns` pass, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase with `parity`; gives up after `limit_ns` nanoseconds of
+// wall time or when *abort becomes nonzero.  Returns false when it gave up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort, uint32_t limit) {
-    for (uint32_t i = 0; i < limit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 255u && *abort) return false;
+                                                  volatile int* abort, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if ((i & 7u) == 7u) {
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > limit_ns) return false;
+        }
     }
-    return false;
 }
 
 // ------------------------------------------------------------------ TMA
