@@ -22,17 +22,12 @@
 // The threshold is seeded with the exact top-k of the first SEED_ROWS rows
 // (CUDA-core kernel of flat_topk.cu), so the first tiles already filter.
 //
-// Kernel layout (one persistent CTA per SM, 12 warps):
-//   warp 0      TMA producer: 128-row x 128-col bf16 tiles (two 64-column
-//               boxes, 128-byte swizzle) into a 4-stage ring
-//   warp 1      MMA issuer: 8 x tcgen05.mma (M=128, N=nq<=256, K=16) per tile
-//               into one of two TMEM accumulators (2 x 256 fp32 columns)
-//   warp 2      TMEM allocator
-//   warps 4-11  two epilogue warpgroups, alternating tiles: tcgen05.ld the
-//               accumulator, filter, rescore, append, release TMEM and smem
-// The queries (B operand, 256 x 128 bf16 = 64 KiB) stay in shared memory for
-// the whole kernel.  Every mbarrier wait is bounded; a wait that gives up
-// sets a status word and the CTA drains and exits.
+// The thresholds themselves are folded into the tensor-core accumulator: a
+// ninth K = 16 MMA per tile adds -t'_q (t'_q = the query's threshold score
+// rounded down to bf16), so the epilogue only needs a 3-input max tree over
+// each row's folded scores against one per-row margin.  The kernel's thread
+// roles are listed at the kernel.  Every mbarrier wait is bounded; a wait that
+// gives up sets a status word and the CTA drains and exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -64,11 +59,14 @@ constexpr int TC_DIM = 128;                    // row width handled (MMA K total
 constexpr int STAGES = 4;
 constexpr int A_BOX = TC_M * 128;              // 64 bf16 columns x 128 rows = 16 KiB
 constexpr int A_STAGE = 2 * A_BOX;             // 32 KiB per tile
-constexpr int B_BOX = TC_NMAX * 128;           // 32 KiB
-constexpr int B_BYTES = 2 * B_BOX;             // 64 KiB
-constexpr int NTHREADS = 384;
-constexpr int N_EPI_WARPS = 8;
-constexpr int QCAP = 128;                      // per-warp rescoring queue (deferred across tiles)
+constexpr int Q_BOX = TC_NMAX * 128;           // 256 queries x 64 columns = 32 KiB
+constexpr int Q_BYTES = 2 * Q_BOX;             // 64 KiB
+constexpr int FA_BYTES = TC_M * 32;            // threshold-fold A operand: 128 rows x 16 bf16
+constexpr int FB_BYTES = TC_NMAX * 32;         // threshold-fold B operand: 256 rows x 16 bf16
+constexpr int N_EPI_WARPS = 8;                 // two epilogue warpgroups (even / odd tiles)
+constexpr int NTHREADS = 32 * (8 + N_EPI_WARPS);
+constexpr int QCAP = 96;                       // per-warp rescoring queue (deferred across tiles)
+constexpr int FLUSH_MARK = 48;                 // queue fill that triggers a flush after a tile
 constexpr int TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
@@ -76,34 +74,33 @@ constexpr int SEED_ROWS = 8192;
 constexpr int POOL_CAP = 8192;
 constexpr int KMAX_TC = 128;
 constexpr int RAISE_STEP = 256;                // appends between threshold raises
-constexpr int ER_RING = 8;                     // tiles of margins in flight (> epilogue lag)
+constexpr int MR_RING = 8;                     // tiles of row bounds in flight (>= STAGES + 2)
 
 struct __align__(8) Ctrl {
-    uint64_t a_full[STAGES];
-    uint64_t a_empty[STAGES];
-    uint64_t acc_full[2];
-    uint64_t acc_empty[2];
-    uint64_t b_full;
+    uint64_t a_full[STAGES];        // tile landed (TMA tx)
+    uint64_t a_empty[STAGES];       // tile consumed: row-bound threads + MMA commit
+    uint64_t acc_full[2];           // accumulator written (MMA commit)
+    uint64_t acc_empty[2];          // accumulator drained by its epilogue warpgroup
+    uint64_t b_full;                // queries landed
+    uint64_t mr_full[MR_RING];      // row bounds of tile i published
     uint32_t tmem_base;
     int abort;
+    float l1max;                    // max over queries of sum_j |b_qj|
+    float tmax;                     // max |folded threshold| ever written to the fold operand
     uint64_t tau[TC_NMAX];          // CTA copy of each query's threshold composite
-    float2 qt[TC_NMAX];             // (sum_j |b_qj| with margin, threshold score)
     uint64_t queue[N_EPI_WARPS][QCAP];   // (shard row << 8) | query
     unsigned hist[N_EPI_WARPS][256];
-    float wt[N_EPI_WARPS][TC_NMAX]; // per-warp, per-tile score thresholds
-    float l1max;                    // max over queries of sum_j |b_qj|
-    uint64_t er_full[ER_RING];      // margin of tile i published (64 arrivals)
-    float er_ring[ER_RING][4];      // EPS * max|a| per 32-row quarter of tile i
+    float mrow[MR_RING][TC_M];      // EPS * max|a_r| per row of tile i
 };
 
-constexpr size_t TC_SMEM = 1024 /* alignment slack */ + B_BYTES + STAGES * A_STAGE + sizeof(Ctrl);
+constexpr size_t TC_SMEM =
+    1024 /* alignment slack */ + Q_BYTES + STAGES * A_STAGE + FA_BYTES + FB_BYTES + sizeof(Ctrl);
 
 struct TcArgs {
     int64_t n_rows;
     int64_t row_begin;
-    int n_tiles;
+    int n_tiles;             // 128-row tiles over [row_begin, n_rows)
     int nq;
-    int nqp;                 // nq rounded up to 16 (MMA N)
     int k;
     int pool_cap;
     int wm0;                 // first fill mark that triggers a threshold raise
@@ -120,17 +117,6 @@ __device__ __forceinline__ float tau_score(uint64_t t) {
     return t == 0ull ? -INFINITY : cand_score(t);
 }
 
-// (a0 - b0, a1 - b1) in one packed fp32x2 subtraction (round to nearest).
-__device__ __forceinline__ float2 sub_f32x2(float a0, float a1, float b0, float b1) {
-    unsigned long long A, B, D;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(B) : "f"(b0), "f"(b1));
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(D) : "l"(A), "l"(B));
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(D));
-    return r;
-}
-
 // max of three, NaN if any input is NaN.
 __device__ __forceinline__ float max3_nan(float a, float b, float c) {
     float d;
@@ -141,32 +127,61 @@ __device__ __forceinline__ float max3_nan(float a, float b, float c) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// The reference's fp32 dot product of a row with query q of the B tile,
-// j ascending.  The B tile is stored as 128-byte rows per 64-column box with
-// the 128-byte swizzle (16-byte chunk c of row q sits at chunk c ^ (q & 7)).
-// The row is read from global memory: the tile's shared-memory copy may
-// already be recycled, and the row was just streamed, so it is in L2.
-__device__ __forceinline__ float exact_dot_row(const uint16_t* __restrict__ row,
-                                               const unsigned char* Bs, int q) {
+// Largest bf16 value <= x (round toward -inf), as fp32.
+__device__ __forceinline__ float bf16_floor(float x) {
+    const uint32_t u = __float_as_uint(x);
+    uint32_t hi = u & 0xffff0000u;                         // truncation: toward 0
+    if ((u & 0xffffu) != 0u && (u & 0x80000000u)) hi += 0x10000u;   // negative: away from 0
+    return __uint_as_float(hi);
+}
+
+// The folded threshold t' = t_hi + t_lo <= t (the score part of threshold
+// composite T) as two bf16: t_hi = bf16_floor(t), t_lo = bf16_floor(t - t_hi)
+// (t - t_hi is exact in fp32), so t - t' < 2^-16 |t|.  Returns the packed
+// bf16x2 (-t_hi, -t_lo) for K columns 0 and 1 of the fold B operand, and
+// |t_hi| + |t_lo| in *mag (an empty threshold folds to +inf: nothing is filtered).
+__device__ __forceinline__ uint32_t neg_fold_pair(uint64_t T, float* mag) {
+    const float t = tau_score(T);
+    if (!(t > -INFINITY)) { *mag = 0.0f; return 0x7f80u; }   // (+inf, +0)
+    const float th = bf16_floor(t);
+    const float tl = bf16_floor(t - th);
+    *mag = fabsf(th) + fabsf(tl);
+    return ((__float_as_uint(th) ^ 0x80000000u) >> 16) | ((__float_as_uint(tl) ^ 0x80000000u) & 0xffff0000u);
+}
+
+// Writes query q's folded threshold into the fold B operand (row q, K
+// columns 0-1 as one 4-byte store, so a concurrent MMA sees the old or the
+// new pair, both <= the current threshold; 32-byte swizzle: 16-byte chunk c
+// of row q sits at c ^ ((q >> 2) & 1)).
+__device__ __forceinline__ void write_fold(unsigned char* FB, Ctrl* ctl, int q, uint64_t T) {
+    float mag;
+    const uint32_t bits = neg_fold_pair(T, &mag);
+    *reinterpret_cast<uint32_t*>(FB + q * 32 + ((((q >> 2) & 1)) << 4)) = bits;
+    atomicMax(reinterpret_cast<int*>(&ctl->tmax), __float_as_int(__fmul_ru(mag, 1.0f + 1.0f / 1024.0f)));
+    fence_proxy_async_smem();
+}
+
+// The reference's fp32 dot product of a memory row and a query, j
+// ascending, both read from global memory (the row was just streamed and is
+// in L2; the queries are small and stay cached).
+__device__ __forceinline__ float exact_dot_rows(const uint16_t* __restrict__ row,
+                                                const uint16_t* __restrict__ qrow) {
     float s = 0.0f;
     const uint4* rp = reinterpret_cast<const uint4*>(row);
+    const uint4* qp = reinterpret_cast<const uint4*>(qrow);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const unsigned char* br = Bs + h * B_BOX + q * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint4 a = __ldg(rp + h * 8 + c);
-            const uint4 b = *reinterpret_cast<const uint4*>(br + ((c ^ (q & 7)) << 4));
-            s = fmaf(bf_lo(a.x), bf_lo(b.x), s); s = fmaf(bf_hi(a.x), bf_hi(b.x), s);
-            s = fmaf(bf_lo(a.y), bf_lo(b.y), s); s = fmaf(bf_hi(a.y), bf_hi(b.y), s);
-            s = fmaf(bf_lo(a.z), bf_lo(b.z), s); s = fmaf(bf_hi(a.z), bf_hi(b.z), s);
-            s = fmaf(bf_lo(a.w), bf_lo(b.w), s); s = fmaf(bf_hi(a.w), bf_hi(b.w), s);
-        }
+    for (int c = 0; c < 16; ++c) {
+        const uint4 a = __ldg(rp + c);
+        const uint4 b = __ldg(qp + c);
+        s = fmaf(bf_lo(a.x), bf_lo(b.x), s); s = fmaf(bf_hi(a.x), bf_hi(b.x), s);
+        s = fmaf(bf_lo(a.y), bf_lo(b.y), s); s = fmaf(bf_hi(a.y), bf_hi(b.y), s);
+        s = fmaf(bf_lo(a.z), bf_lo(b.z), s); s = fmaf(bf_hi(a.z), bf_hi(b.z), s);
+        s = fmaf(bf_lo(a.w), bf_lo(b.w), s); s = fmaf(bf_hi(a.w), bf_hi(b.w), s);
     }
     return s;
 }
 
-// max_j |a_rj| over row r of the A tile (chunk order is irrelevant).
+// max_j |a_rj| over row r of a tile (chunk order is irrelevant).
 __device__ __forceinline__ float row_absmax(const unsigned char* As, int r) {
     __nv_bfloat162 m = __floats2bfloat162_rn(0.0f, 0.0f);
 #pragma unroll
@@ -198,10 +213,17 @@ __device__ __forceinline__ void set_abort(Ctrl* ctl, int* status) {
     atomicExch(&status[0], 1);
 }
 
+// Raises query q's CTA threshold to T (if higher) and refolds it.
+__device__ __forceinline__ void raise_tau(Ctrl* ctl, unsigned char* FB, int q, uint64_t T) {
+    const unsigned long long old =
+        atomicMax(reinterpret_cast<unsigned long long*>(&ctl->tau[q]), (unsigned long long)T);
+    if (T > old) write_fold(FB, ctl, q, T);
+}
+
 // Rescores the warp's queued pairs exactly and appends the ones that beat
 // their query's threshold to the pools; raises thresholds at fill marks.
-__device__ __forceinline__ void flush_queue(Ctrl* ctl, int ew, int qc,
-                                         const unsigned char* Bs, const TcArgs& a) {
+__device__ __noinline__ void flush_queue(Ctrl* ctl, unsigned char* FB, int ew, int qc,
+                                         const TcArgs& a) {
     const int lane = threadIdx.x & 31;
     if (lane == 0) atomicAdd(&a.status[2], qc);
     for (int base = 0; base < qc; base += 32) {
@@ -211,7 +233,7 @@ __device__ __forceinline__ void flush_queue(Ctrl* ctl, int ew, int qc,
             const uint64_t e = ctl->queue[ew][i];
             const int64_t row = (int64_t)(e >> 8);
             q = (int)(e & 255u);
-            const float s = exact_dot_row(a.mem + row * TC_DIM, Bs, q);
+            const float s = exact_dot_rows(a.mem + row * TC_DIM, a.qry + (int64_t)q * TC_DIM);
             const uint64_t E = make_cand(f32_key(s), (uint32_t)row);
             if (E > ctl->tau[q]) {
                 const int pos = atomicAdd(&a.pool_cnt[q], 1);
@@ -236,9 +258,7 @@ __device__ __forceinline__ void flush_queue(Ctrl* ctl, int ew, int qc,
             if (lane == 0 && T != 0ull) {
                 atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
                           (unsigned long long)T);
-                const unsigned long long old = atomicMax(
-                    reinterpret_cast<unsigned long long*>(&ctl->tau[qq]), (unsigned long long)T);
-                if (T > old) ctl->qt[qq].y = tau_score(T);
+                raise_tau(ctl, FB, qq, T);
             }
             __syncwarp();
         }
@@ -246,6 +266,20 @@ __device__ __forceinline__ void flush_queue(Ctrl* ctl, int ew, int qc,
     __syncwarp();
 }
 
+// One persistent CTA per SM.  Roles (16 warps):
+//   warp 0      TMA producer: the 256 queries once, then 128-row x 128-col bf16
+//               tiles (two 64-column boxes, 128-byte swizzle) into a 4-stage ring
+//   warp 1      MMA issuer: per tile, 8 x tcgen05.mma (M = 128 rows, N = 256
+//               queries, K = 16) plus one K = 16 MMA that adds -t'_q (each
+//               query's threshold, folded as a bf16 rounded down) into the same
+//               TMEM accumulator (two accumulators of 256 fp32 columns)
+//   warp 2      TMEM allocator
+//   warps 4-7   row bounds: EPS * max|a_r| for each row of a landed tile; with
+//               the MMA commit they free the tile's stage
+//   warps 8-15  epilogue, two warpgroups (even / odd tiles): thread = row
+//               (TMEM lane); a 3-input max tree over the row's 256 folded
+//               scores s~ - t'_q against the row's margin; rows that reach it
+//               go to exact rescoring
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
@@ -253,9 +287,11 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
     // 1024-byte aligned base, derived by pointer arithmetic so that the
     // compiler keeps every access below in the shared address space
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    unsigned char* Bs = smem;
-    unsigned char* As = smem + B_BYTES;
-    Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + B_BYTES + STAGES * A_STAGE);
+    unsigned char* Qs = smem;
+    unsigned char* As = Qs + Q_BYTES;
+    unsigned char* FA = As + STAGES * A_STAGE;     // 1024-aligned
+    unsigned char* FB = FA + FA_BYTES;
+    Ctrl* ctl = reinterpret_cast<Ctrl*>(FB + FB_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x;
@@ -265,32 +301,42 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&ctl->a_full[s], 1);
-            mbar_init(&ctl->a_empty[s], 64 + 1);   // margin warps + the MMA commit
+            mbar_init(&ctl->a_empty[s], TC_M + 1);   // row-bound threads + the MMA commit
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->acc_full[b], 1);
-            mbar_init(&ctl->acc_empty[b], 128);
+            mbar_init(&ctl->acc_empty[b], 4);        // the 4 warps of a warpgroup
         }
         mbar_init(&ctl->b_full, 1);
-        for (int e = 0; e < ER_RING; ++e) mbar_init(&ctl->er_full[e], 64);
+        for (int e = 0; e < MR_RING; ++e) mbar_init(&ctl->mr_full[e], 4);
         ctl->abort = 0;
         ctl->l1max = 0.0f;
+        ctl->tmax = 0.0f;
         fence_barrier_init();
     }
+    // fold operands: A' = 1 in K column 0, B' = -t'_q in K column 0, zero elsewhere
+    for (int i = threadIdx.x; i < (FA_BYTES + FB_BYTES) / 4; i += NTHREADS)
+        reinterpret_cast<uint32_t*>(FA)[i] = 0u;
     __syncthreads();
+    for (int r = threadIdx.x; r < TC_M; r += NTHREADS)   // (1.0, 1.0) in K columns 0-1
+        *reinterpret_cast<uint32_t*>(FA + r * 32 + (((r >> 2) & 1) << 4)) = 0x3f803f80u;
     for (int q = threadIdx.x; q < TC_NMAX; q += NTHREADS) {
         float l1 = 0.0f;
-        uint64_t t = ~0ull;
+        uint64_t t = ~0ull;   // padded queries: never selected (fold = -inf below)
         if (q < a.nq) {
             const uint16_t* p = a.qry + (int64_t)q * TC_DIM;
             for (int j = 0; j < TC_DIM; ++j) l1 += fabsf(bf16_bits_to_f32(p[j]));
             l1 *= 1.0f + 1.0f / 256.0f;   // covers the rounding of this sum
             t = a.tau_global[q];
+            atomicMax(reinterpret_cast<int*>(&ctl->l1max), __float_as_int(l1));   // l1 >= 0
         }
         ctl->tau[q] = t;
-        ctl->qt[q] = make_float2(l1, q < a.nq ? tau_score(t) : INFINITY);
-        atomicMax(reinterpret_cast<int*>(&ctl->l1max), __float_as_int(l1));   // l1 >= 0
+        float mag = 0.0f;
+        const uint32_t bits = q < a.nq ? neg_fold_pair(t, &mag) : 0xff80u;   // (-inf, +0)
+        *reinterpret_cast<uint32_t*>(FB + q * 32 + (((q >> 2) & 1) << 4)) = bits;
+        atomicMax(reinterpret_cast<int*>(&ctl->tmax), __float_as_int(__fmul_ru(mag, 1.0f + 1.0f / 1024.0f)));
     }
+    fence_proxy_async_smem();
     if (warp == 2) {
         tmem_alloc(&ctl->tmem_base, TMEM_COLS);
         tmem_relinquish();
@@ -305,9 +351,9 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         if (lane == 0) {
             prefetch_tmap(&tmA);
             prefetch_tmap(&tmB);
-            mbar_expect_tx(&ctl->b_full, B_BYTES);
-            tma_load_2d(Bs, &tmB, &ctl->b_full, 0, 0);
-            tma_load_2d(Bs + B_BOX, &tmB, &ctl->b_full, 64, 0);
+            mbar_expect_tx(&ctl->b_full, Q_BYTES);
+            tma_load_2d(Qs, &tmB, &ctl->b_full, 0, 0);
+            tma_load_2d(Qs + Q_BOX, &tmB, &ctl->b_full, 64, 0);
         }
         int issued = 0;
         for (int i = 0; i < my_tiles; ++i) {
@@ -333,7 +379,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         }
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
-        const uint32_t idesc = idesc_f16(TC_M, a.nqp, 1);
+        const uint32_t idesc = idesc_f16(TC_M, TC_NMAX, 1);
         int last = -1;
         bool ok = warp_wait(&ctl->b_full, 0, abort);
         if (!ok && lane == 0) set_abort(ctl, a.status);
@@ -346,13 +392,16 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             }
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t a0 = smem_u32(As + s * A_STAGE), b0 = smem_u32(Bs);
+                const uint32_t a0 = smem_u32(As + s * A_STAGE), q0 = smem_u32(Qs);
+                const uint32_t d = tmem + (uint32_t)(b * TC_NMAX);
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
-                        mma_f16(tmem + b * TC_NMAX, desc_k_sw128(a0 + h * A_BOX + ks * 32),
-                                desc_k_sw128(b0 + h * B_BOX + ks * 32), idesc, (h | ks) != 0);
+                        mma_f16(d, desc_k_sw128(a0 + h * A_BOX + ks * 32),
+                                desc_k_sw128(q0 + h * Q_BOX + ks * 32), idesc, (h | ks) != 0);
+                // fold: D[r][q] += 1 * (-t'_q)
+                mma_f16(d, desc_k_sw32(smem_u32(FA)), desc_k_sw32(smem_u32(FB)), idesc, 1u);
                 mma_commit(&ctl->acc_full[b]);
                 mma_commit(&ctl->a_empty[s]);
             }
@@ -361,67 +410,44 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         if (*abort && last >= 0)
             mbar_wait_bounded(&ctl->acc_full[last & 1], (last >> 1) & 1, abort, 100000000ull);
-    } else if (warp == 2 || warp == 3) {
-        // ---------------------------------------------- margin (row bound) warps
-        // rows t and t + 64 of every tile (t = 0..63); quarter = rows / 32
-        const int t = (warp - 2) * 32 + lane;
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------------------------------------------- row-bound warps
+        const int r = (warp - 4) * 32 + lane;
         for (int i = 0; i < my_tiles; ++i) {
             const int s = i % STAGES;
             if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
-            const unsigned char* At = As + s * A_STAGE;
-            const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
-            float e0 = tile_row0 + t < a.n_rows ? __fmul_ru(EPS, row_absmax(At, t)) : 0.0f;
-            float e1 = tile_row0 + t + 64 < a.n_rows ? __fmul_ru(EPS, row_absmax(At, t + 64)) : 0.0f;
+            const int64_t row = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M + r;
+            const float e = row < a.n_rows ? __fmul_ru(EPS, row_absmax(As + s * A_STAGE, r)) : 0.0f;
             mbar_arrive(&ctl->a_empty[s]);       // smem reads of this tile are done
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                e0 = fmaxf(e0, __shfl_xor_sync(0xffffffffu, e0, o));
-                e1 = fmaxf(e1, __shfl_xor_sync(0xffffffffu, e1, o));
-            }
-            if (lane == 0) {
-                ctl->er_ring[i % ER_RING][warp - 2] = e0;       // quarter 0 or 1
-                ctl->er_ring[i % ER_RING][warp - 2 + 2] = e1;   // quarter 2 or 3
-            }
+            ctl->mrow[i % MR_RING][r] = e;
             __syncwarp();
-            mbar_arrive(&ctl->er_full[i % ER_RING]);
+            if (lane == 0) mbar_arrive(&ctl->mr_full[i % MR_RING]);
         }
-    } else if (warp >= 4) {
+    } else if (warp >= 8) {
         // --------------------------------------------------------- epilogue
-        const int ew = warp - 4;            // 0..7
+        const int ew = warp - 8;            // 0..7
         const int g = ew >> 2;              // warpgroup: tiles with i % 2 == g
         const int sub = warp & 3;           // TMEM lanes 32*sub .. +31
         const int r = sub * 32 + lane;      // tile row of this thread
-        bool ok = warp_wait(&ctl->b_full, 0, abort);
-        if (!ok && lane == 0) set_abort(ctl, a.status);
-        const int nchunks = a.nqp / 32 + ((a.nqp & 31) ? 1 : 0);
+        const int nchunks = (a.nq + 31) / 32;
         int qc = 0;   // queued (row, query) pairs awaiting exact rescoring
-        for (int i = g; ok && i < my_tiles; i += 2) {
+        for (int i = g; i < my_tiles; i += 2) {
             const int b = i & 1;
-            // ---- off the critical path: the tile's margin is published
-            if (!warp_wait(&ctl->er_full[i % ER_RING], (i / ER_RING) & 1, abort)) {
+            // ---- off the critical path: the tile's row bounds are published
+            if (!warp_wait(&ctl->mr_full[i % MR_RING], (i / MR_RING) & 1, abort)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
             const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
             const bool valid = tile_row0 + r < a.n_rows;
-
             // start the load of this warp's 32 shared thresholds; applied after the filter
             const int qr = ew * 32 + lane;
             uint64_t t_new = 0;
             if (qr < a.nq) t_new = *reinterpret_cast<volatile uint64_t*>(&a.tau_global[qr]);
-            const float ER = ctl->er_ring[i % ER_RING][sub];
-            // warp-uniform margin M >= EPS * max|a_r| * sum|b_q| for every row and
-            // query of this warp's tile; threshold per query rounded down, so
-            // s~ + margin >= tau  implies  s~ >= wt
-            const float M = __fmul_ru(ER, ctl->l1max);
-            float* wt = ctl->wt[ew];
-#pragma unroll
-            for (int c = 0; c < TC_NMAX / 32; ++c)
-                wt[c * 32 + lane] = __fsub_rd(ctl->qt[c * 32 + lane].y, M);
-            __syncwarp();
+            const float er = ctl->mrow[i % MR_RING][r];
 
             // ---- critical path: accumulator ready -> filter -> release
             if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort)) {
@@ -429,73 +455,69 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                 break;
             }
             tc_fence_after();
+            // |s~ - t' - (s - t')| <= EPS * (max|a_r| * sum|b_q| + |t'|) for every
+            // query; a pair can beat its threshold only if s~ - t' >= -margin
+            const float margin = __fmaf_ru(er, ctl->l1max, __fmul_ru(EPS, ctl->tmax));
+            const float neg = valid ? -margin : INFINITY;   // rows past the end never pass
             const uint32_t tbase = tmem + (uint32_t)(b * TC_NMAX) + ((uint32_t)(sub * 32) << 16);
-            // filters 32 accumulator columns (queries c*32 ..) of this thread's row
-            auto filter = [&](const uint32_t* v, int c) {
-                // fast test: max_j (s~_j - wt_j) < 0 for the whole chunk (NaN passes)
-                float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll 1
+            for (int c0 = 0; c0 < nchunks; c0 += 2) {
+                uint32_t v[2][32];
+                tmem_ld_x32(tbase + (uint32_t)(c0 * 32), v[0]);
+                if (c0 + 1 < nchunks) tmem_ld_x32(tbase + (uint32_t)(c0 * 32 + 32), v[1]);
+                tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    const float4 t = *reinterpret_cast<const float4*>(wt + c * 32 + j);
-                    const float2 d0 = sub_f32x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), t.x, t.y);
-                    const float2 d1 =
-                        sub_f32x2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]), t.z, t.w);
-                    m0 = max3_nan(m0, d0.x, d0.y);
-                    m1 = max3_nan(m1, d1.x, d1.y);
-                }
-                const bool hit = valid && !(fmaxf(m0, m1) < 0.0f) || (m0 != m0) || (m1 != m1);
-                if (!__any_sync(0xffffffffu, hit)) return;
-                const int rem = a.nq - c * 32;
-                const uint32_t qmask = rem >= 32 ? 0xffffffffu : (rem > 0 ? (1u << rem) - 1u : 0u);
-                uint32_t bits = 0;
+                for (int h = 0; h < 2; ++h) {
+                    const int c = c0 + h;
+                    float m[11];
 #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    const float4 t = *reinterpret_cast<const float4*>(wt + c * 32 + j);
-                    bits |= (uint32_t)(!(__uint_as_float(v[j + 0]) < t.x)) << (j + 0);
-                    bits |= (uint32_t)(!(__uint_as_float(v[j + 1]) < t.y)) << (j + 1);
-                    bits |= (uint32_t)(!(__uint_as_float(v[j + 2]) < t.z)) << (j + 2);
-                    bits |= (uint32_t)(!(__uint_as_float(v[j + 3]) < t.w)) << (j + 3);
-                }
-                bits = valid ? (bits & qmask) : 0u;
-                while (__any_sync(0xffffffffu, bits != 0)) {
-                    const bool has = bits != 0;
-                    const int j = has ? __ffs(bits) - 1 : 0;
-                    bits &= bits - 1;
-                    const unsigned m = __ballot_sync(0xffffffffu, has);
-                    if (has)
-                        ctl->queue[ew][qc + __popc(m & ((1u << lane) - 1u))] =
-                            ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
-                    qc += __popc(m);
-                    if (qc > QCAP - 32) {
-                        __syncwarp();
-                        flush_queue(ctl, ew, qc, Bs, a);
-                        qc = 0;
+                    for (int j = 0; j < 10; ++j)
+                        m[j] = max3_nan(__uint_as_float(v[h][3 * j]), __uint_as_float(v[h][3 * j + 1]),
+                                        __uint_as_float(v[h][3 * j + 2]));
+                    m[10] = max3_nan(__uint_as_float(v[h][30]), __uint_as_float(v[h][31]),
+                                     __uint_as_float(v[h][31]));
+                    const float m0 = max3_nan(m[0], m[1], m[2]), m1 = max3_nan(m[3], m[4], m[5]);
+                    const float m2 = max3_nan(m[6], m[7], m[8]), m3 = max3_nan(m[9], m[10], m[10]);
+                    const float mx = max3_nan(max3_nan(m0, m1, m2), m3, m3);
+                    const bool hit = c < nchunks && !(mx < neg);   // NaN passes
+                    if (!__any_sync(0xffffffffu, hit)) continue;
+                    // rare: queue the (row, query) pairs of this chunk that reach -margin
+                    uint32_t bits = 0;
+                    if (hit) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            bits |= (uint32_t)(!(__uint_as_float(v[h][j]) < neg)) << j;
+                        const int rem = a.nq - c * 32;
+                        bits &= rem >= 32 ? 0xffffffffu : (rem > 0 ? (1u << rem) - 1u : 0u);
+                    }
+                    while (__any_sync(0xffffffffu, bits != 0)) {
+                        const bool has = bits != 0;
+                        const int j = has ? __ffs(bits) - 1 : 0;
+                        bits &= bits - 1;
+                        const unsigned mk = __ballot_sync(0xffffffffu, has);
+                        if (has)
+                            ctl->queue[ew][qc + __popc(mk & ((1u << lane) - 1u))] =
+                                ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
+                        qc += __popc(mk);
+                        if (qc > QCAP - 32) {   // only when a tile floods the queue
+                            __syncwarp();
+                            flush_queue(ctl, FB, ew, qc, a);
+                            qc = 0;
+                        }
                     }
                 }
-            };
-            // software pipeline: the next chunk's TMEM load is in flight while
-            // the current chunk is filtered
-            uint32_t va[32], vb[32];
-            tmem_ld_x32(tbase, va);
-            tmem_wait_ld();
-            for (int c = 0; c < nchunks; c += 2) {
-                if (c + 1 < nchunks) tmem_ld_x32(tbase + (uint32_t)((c + 1) * 32), vb);
-                filter(va, c);
-                tmem_wait_ld();
-                if (c + 2 < nchunks) tmem_ld_x32(tbase + (uint32_t)((c + 2) * 32), va);
-                if (c + 1 < nchunks) filter(vb, c + 1);
-                tmem_wait_ld();
-            }
-            if (qr < a.nq && t_new > ctl->tau[qr]) {
-                const unsigned long long old = atomicMax(
-                    reinterpret_cast<unsigned long long*>(&ctl->tau[qr]), (unsigned long long)t_new);
-                if (t_new > old) ctl->qt[qr].y = tau_score(t_new);
             }
             tc_fence_before();
-            mbar_arrive(&ctl->acc_empty[b]);
             __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->acc_empty[b]);
+            // rescoring happens off the accumulator's critical path
+            if (qc >= FLUSH_MARK) {
+                flush_queue(ctl, FB, ew, qc, a);
+                qc = 0;
+            }
+            if (qr < a.nq && t_new > ctl->tau[qr]) raise_tau(ctl, FB, qr, t_new);
         }
-        if (qc > 0) flush_queue(ctl, ew, qc, Bs, a);   // B stays resident to the end
+        if (qc > 0) flush_queue(ctl, FB, ew, qc, a);
     }
 
     tc_fence_before();
@@ -639,7 +661,6 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         a.row_begin = seed;
         a.n_tiles = (int)((n - seed + TC_M - 1) / TC_M);
         a.nq = nqp_pass;
-        a.nqp = (nqp_pass + 15) & ~15;
         a.k = (int)k;
         a.pool_cap = POOL_CAP;
         a.wm0 = std::max(256, next_pow2(2 * (int)k));
@@ -649,9 +670,11 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         a.pool = pool;
         a.pool_cnt = cnt;
         a.status = status;
-        const int grid = std::min(sms, a.n_tiles);
+        const int grid = std::max(1, std::min(sms, a.n_tiles));
         tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
         s = check_launch("tc_score_select_kernel");
+        if (s != HMM_OK) return s;
+
         if (s != HMM_OK) return s;
         s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, row_offset,
                               out_idx + q0 * k, out_scores + q0 * k, st);

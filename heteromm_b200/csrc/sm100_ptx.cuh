@@ -199,5 +199,18 @@ __host__ __device__ constexpr uint32_t idesc_f8(int M, int N, int a_format, int 
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Generic-proxy writes to shared memory made visible to later async-proxy
+// (tensor core / TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand of 32-byte rows (16
+// bf16) with the 32-byte swizzle: 8-row atoms of 256 bytes, SBO = 256.
+__device__ __forceinline__ uint64_t desc_k_sw32(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+}
+
 }  // namespace sm100
 }  // namespace hmm
