@@ -37,6 +37,9 @@ SIGNATURES = {
     "hmm_ip_topk_f32_noalloc": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _F, _P, _P]),
     "hmm_shard_merge_topk_workspace_size": (_S, [_I, _I, _I]),
     "hmm_shard_merge_topk": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
+    "hmm_kernel_launches": (_I, []),
+    "hmm_profile_enable": (C.c_int, [C.c_int]),
+    "hmm_profile_read": (C.c_int, [_P, _P]),
 }
 
 
@@ -81,3 +84,21 @@ def call(name: str, *args) -> int:
 
 def last_error() -> str:
     return load().hmm_last_error().decode()
+
+
+def kernel_launches() -> int:
+    """Kernels the CUDA library has launched since it was loaded."""
+    return int(load().hmm_kernel_launches())
+
+
+def profile_enable(on: bool) -> None:
+    """Starts / stops CUDA-event timing of the dominant scoring kernel."""
+    call("hmm_profile_enable", 1 if on else 0)
+
+
+def profile_read() -> tuple:
+    """(summed ms, launches) of the scoring-kernel launches timed since the last read."""
+    ms = C.c_double(0.0)
+    n = C.c_int64(0)
+    call("hmm_profile_read", C.byref(ms), C.byref(n))
+    return ms.value, n.value

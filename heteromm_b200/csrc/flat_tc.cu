@@ -671,14 +671,36 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         a.pool_cnt = cnt;
         a.status = status;
         const int grid = std::max(1, std::min(sms, a.n_tiles));
+        const ProfileMark pm = profile_begin(st);
         tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
         s = check_launch("tc_score_select_kernel");
+        profile_end(pm, st);
         if (s != HMM_OK) return s;
 
-        if (s != HMM_OK) return s;
         s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, row_offset,
                               out_idx + q0 * k, out_scores + q0 * k, st);
         if (s != HMM_OK) return s;
+
+        // The kernel reports a bounded wait that gave up (status[0]) and a
+        // query whose candidate pool filled up (status[1]; only inputs whose
+        // row order makes the running k-th best climb for thousands of rows,
+        // e.g. rows sorted by score, get there).  A full pool means dropped
+        // candidates, so that pass is recomputed on the exact CUDA-core path,
+        // which needs no pool and fits the same workspace.
+        int host_status[4] = {0, 0, 0, 0};
+        HMM_CUDA_TRY(cudaMemcpyAsync(host_status, status, sizeof(host_status),
+                                     cudaMemcpyDeviceToHost, st));
+        HMM_CUDA_TRY(cudaStreamSynchronize(st));
+        if (host_status[0] != 0)
+            return set_error(HMM_ERR_TIMEOUT,
+                             "tc_score_select_kernel: a bounded pipeline wait gave up; the "
+                             "outputs of queries [%lld, %lld) are invalid",
+                             (long long)q0, (long long)(q0 + nqp_pass));
+        if (host_status[1] != 0) {
+            s = flat_bf16_exact(mem, n, TC_DIM, qp, nqp_pass, k, row_offset, out_idx + q0 * k,
+                                out_scores + q0 * k, ws, ws_bytes, st);
+            if (s != HMM_OK) return s;
+        }
     }
     return HMM_OK;
 }

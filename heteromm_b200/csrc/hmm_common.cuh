@@ -16,6 +16,13 @@ namespace hmm {
 hmm_status_t set_error(hmm_status_t st, const char* fmt, ...);
 // Maps the current CUDA error state after a launch to a status.
 hmm_status_t check_launch(const char* what);
+// CUDA-event bracket around one launch of a dominant kernel, recorded only
+// while hmm_profile_enable(1) is in effect (both events null otherwise).
+struct ProfileMark {
+    cudaEvent_t start, stop;
+};
+ProfileMark profile_begin(cudaStream_t st);
+void profile_end(const ProfileMark& m, cudaStream_t st);
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 

@@ -97,7 +97,12 @@ hmm_status_t hmm_ip_topk_f32(const float* mem, int64_t n_rows, int64_t dim,
  * accumulate: one shard of a row-sharded memory.  Row i of this shard has
  * global index row_offset + i; out_idx [n_queries][k] int64 global indices,
  * out_scores [n_queries][k] fp32 (required: the shard merge needs them).
- * Scores equal the reference's fp32 inner product of the widened values. */
+ * Scores equal the reference's fp32 inner product of the widened values.
+ * For dim == 128, k <= 128, n_rows > 8192 and 16-byte aligned pointers the
+ * rows are scored on the tensor cores (tcgen05) and the candidates rescored
+ * exactly; that path waits for `stream` before returning (it reads back the
+ * kernel's status word) and returns HMM_ERR_TIMEOUT if a bounded device wait
+ * gave up.  Other shapes run the exact CUDA-core kernel asynchronously. */
 size_t hmm_ip_topk_bf16_workspace_size(int64_t n_rows, int64_t dim, int64_t n_queries,
                                        int64_t k);
 hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
@@ -144,6 +149,17 @@ hmm_status_t hmm_ip_topk_f32_noalloc(const float* mem, int64_t n_rows, int64_t d
                                      const float* queries, int64_t n_queries, int64_t k,
                                      int32_t* out_idx, float* out_scores, float threshold,
                                      uint64_t* out_bitmap, void* stream);
+
+/* ------------------------------------------------------ instrumentation
+ * No reference counterpart (the reference steps are timed by their callers).
+ * hmm_kernel_launches: kernels this library has launched since it was loaded.
+ * hmm_profile_enable(1): from then on, record a CUDA event pair on the
+ * launching stream around each launch of the dominant scoring kernel
+ * (tc_score_select_kernel); hmm_profile_read waits for the recorded pairs and
+ * returns their summed duration and count, then forgets them. */
+int64_t hmm_kernel_launches(void);
+hmm_status_t hmm_profile_enable(int enable);
+hmm_status_t hmm_profile_read(double* total_ms, int64_t* launches);
 
 #ifdef __cplusplus
 }

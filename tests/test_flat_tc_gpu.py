@@ -76,3 +76,39 @@ def test_tc_sharded_merge(cuda):
     oidx, osc = O.ip_topk_bf16(mem, qry, k)
     assert np.array_equal(mi.cpu().numpy(), oidx)
     assert np.array_equal(ms.cpu().numpy().view(np.uint32), osc.view(np.uint32))
+
+
+def test_tc_pool_overflow_falls_back_to_exact(cuda):
+    """Rows ordered so that query 0's score is the row index: every row beats
+    the running top-k, so query 0's candidate pool fills up.  The call must
+    notice the dropped candidates and recompute the pass exactly (two extra
+    kernel launches on top of the tensor-core path's five)."""
+    from heteromm_b200 import _abi
+    n, nq, k = 65000, 4, 100
+    x = gen.normal_f32(81, (n, 128))
+    i = np.arange(n)
+    x[:, 0] = 256.0 * (i // 256)      # bf16-exact: 256 * m, m < 256
+    x[:, 1] = (i % 256).astype(np.float32)
+    mem = gen.bf16_bits(x)
+    q = gen.normal_f32(82, (nq, 128))
+    q[0] = 0.0
+    q[0, :2] = 1.0                    # score of row i for query 0 is exactly i
+    qry = gen.bf16_bits(q)
+    l0 = _abi.kernel_launches()
+    idx, sc = run(cuda, mem, qry, k)
+    launches = _abi.kernel_launches() - l0
+    oidx, osc = O.ip_topk_bf16(mem, qry, k)
+    assert np.array_equal(idx[0], np.arange(n - 1, n - 1 - k, -1))
+    assert np.array_equal(idx, oidx)
+    assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
+    assert launches == 7, launches
+
+
+def test_tc_normal_call_launch_count(cuda):
+    from heteromm_b200 import _abi
+    mem = gen.bf16_bits(gen.normal_f32(91, (20000, 128)))
+    qry = gen.bf16_bits(gen.normal_f32(92, (8, 128)))
+    run(cuda, mem, qry, 10)
+    l0 = _abi.kernel_launches()
+    run(cuda, mem, qry, 10)
+    assert _abi.kernel_launches() - l0 == 5
