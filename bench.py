@@ -262,7 +262,7 @@ def run_ours(args, rank, world, local):
             "gpu_launches": launches,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t,
                          "unit": "TFLOP/s", "frac": achieved / peak_t,
-                         "traffic": traffic_per_launch(per),
+                         "traffic": traffic_per_launch("tc_score_select_kernel", per),
                          "kernel": "tc_score_select_kernel", "kernel_ms": kern_ms,
                          "kernel_launches_timed": k_n,
                          "peak_kind": f"{pk_kind} bf16 sustained (cuBLAS, 4 s loop)",
@@ -358,16 +358,152 @@ def gen_rows_cpu(count: int):
     return out.view(torch.int16).numpy().view("uint16")
 
 
-def traffic_per_launch(rows: int):
-    """DRAM bytes (read + write) of one tc_score_select_kernel launch from the
-    committed ncu capture, scaled from its row count to `rows` (the kernel
-    streams each row once, so its traffic grows in proportion)."""
-    p = os.path.join(ROOT, "profiles", "tc_score_select_kernel.traffic.json")
+# ---------------------------------------------------------------- config 2
+P_BATCH, P_HEADS, P_LEN, P_DIM = 8, 32, 32768, 128
+P_PAGE, P_BLOCK, P_TOP = 16, 64, 64
+SEED_K, SEED_PERM, SEED_Q = 3, 4, 5
+
+
+def run_paged(args, rank, world, local):
+    """Paged-KV block-sparse decode: (batch x heads) sequences of P_LEN bf16
+    tokens in 16-token pages (shuffled physical order), fp32 mean summaries of
+    64-token blocks, top-64 blocks by q . summary, softmax attention over them.
+    Sequences are split across ranks (no exchange)."""
+    import heteromm_b200 as hmm
+    from heteromm_b200 import _abi
+    dev = torch.device("cuda", local)
+    hmm.load()
+    n_all = args.seqs if args.seqs else P_BATCH * P_HEADS
+    per = n_all // world
+    pps = P_LEN // P_PAGE
+    n_pages = per * pps
+    g = torch.Generator(device=dev)
+    kp = torch.empty((n_pages, P_PAGE, P_DIM), dtype=torch.bfloat16, device=dev)
+    vp = torch.empty_like(kp)
+    step_pages = 1 << 16
+    for c in range(0, n_pages, step_pages):
+        g.manual_seed(SEED_K * 1000003 + rank * 7919 + c)
+        kp[c:c + step_pages] = torch.randn(kp[c:c + step_pages].shape, generator=g, device=dev)
+        vp[c:c + step_pages] = torch.randn(vp[c:c + step_pages].shape, generator=g, device=dev)
+    gc = torch.Generator()
+    gc.manual_seed(SEED_PERM + rank)
+    table = torch.randperm(n_pages, generator=gc).to(torch.int32).reshape(per, pps).to(dev)
+    gc.manual_seed(SEED_Q + rank)
+    q = torch.randn((per, P_DIM), generator=gc).to(torch.bfloat16).to(dev)
+    k16, v16, q16 = kp.view(torch.int16), vp.view(torch.int16), q.view(torch.int16)
+    torch.cuda.synchronize()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    summ = hmm.paged_kv_summary_bf16(k16, table, P_LEN, P_BLOCK)
+    e1.record()
+    torch.cuda.synchronize()
+    build_ms = e0.elapsed_time(e1)
+
+    def step(qq):
+        return hmm.block_sparse_decode_bf16(qq, summ, k16, v16, table, P_LEN, P_BLOCK, P_TOP)
+
+    for _ in range(args.warmup):
+        step(q16)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    _abi.profile_read()
+    _abi.profile_enable(True)
+    stream = torch.cuda.current_stream()
+    with ClockSampler(local) as clk:
+        l0 = _abi.kernel_launches()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(q16)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        launches = _abi.kernel_launches() - l0
+    _abi.profile_enable(False)
+    k_total, k_n = _abi.profile_read()
+    ms = e0.elapsed_time(e1) / args.steps
+    kern_ms = k_total / max(k_n, 1)
+
+    # end to end: q from pinned host memory, selected blocks + outputs back
+    q_host = q16.cpu().pin_memory()
+    q_dev = torch.empty_like(q16)
+    ob = torch.empty((per, P_TOP), dtype=torch.int32).pin_memory()
+    oo = torch.empty((per, P_DIM), dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        b, o = step(q_dev)
+        ob.copy_(b, non_blocking=True)
+        oo.copy_(o, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, kern_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return None
+    pk, pk_kind = peaks()
+    kv_bytes = per * P_TOP * P_BLOCK * P_DIM * 2 * 2          # selected K and V
+    summ_bytes = per * (P_LEN // P_BLOCK) * P_DIM * 4
+    achieved = kv_bytes / (kern_ms * 1e-3) / 1e9
+    res = {
+        "metric": "paged-KV block-sparse decode: (batch, head) queries per second",
+        "value": n_all / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V, shuffled physical pages)",
+        "config": {"workload": f"paged-KV decode: batch {P_BATCH} x {P_HEADS} heads, "
+                               f"{P_LEN} tokens x {P_DIM} bf16, page {P_PAGE}, "
+                               f"block {P_BLOCK}, top-{P_TOP}",
+                   "parallelism": f"(batch, head) split x{world}",
+                   "l2": "inputs larger than L2 (604 MB read per step)",
+                   "summary_build_ms": build_ms,
+                   "step_gbs": (kv_bytes + summ_bytes) / (ms * 1e-3) / 1e9},
+        "e2e": {"value": n_all / (e2e_ms * 1e-3), "unit": "queries/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": per * P_DIM * 2,
+                "d2h_bytes_per_step": per * (P_TOP * 4 + P_DIM * 4)},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "traffic": traffic_per_launch("bsa_page_kernel", per),
+                     "kernel": "bsa_page_kernel<128,16>", "kernel_ms": kern_ms,
+                     "kernel_launches_timed": k_n, "peak_kind": f"{pk_kind} copy bandwidth"},
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        n_s = 8
+        tb = table.long()
+        t_total = 0.0
+        for s_i in range(n_s):
+            keys = kp[tb[s_i]].float().reshape(P_LEN, P_DIM).cpu().numpy()
+            vals = vp[tb[s_i]].float().reshape(P_LEN, P_DIM).cpu().numpy()
+            qq = q[s_i].float().cpu().numpy()
+            t = time.perf_counter()
+            O.ref_paged_decode_f32(keys, vals, qq, P_BLOCK, P_TOP)
+            t_total += time.perf_counter() - t
+        res["cpu_baseline"] = {"value": n_s / t_total, "unit": "queries/s", "cores": 1,
+                               "kind": "reference",
+                               "sample": f"{n_s} sequences: the reference's PagedKVIndexBuilder "
+                                         f"+ InnerProductCompute + TopKRetrieval + "
+                                         f"BlockSparseAttention per sequence (summary build "
+                                         f"included), {t_total:.2f} s"}
+    return res
+
+
+def traffic_per_launch(kernel: str, units: int):
+    """DRAM bytes (read + write) of one launch of `kernel` from its committed
+    ncu capture, scaled from the capture's units (rows, sequences) to `units`:
+    each kernel streams every unit once, so its traffic grows in proportion."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}.traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as f:
         d = json.load(f)
-    return d["dram_bytes_per_launch"] * rows / d["rows"]
+    return d["dram_bytes_per_launch"] * units / d["units"]
 
 
 def main():
@@ -378,6 +514,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", choices=["flat", "paged"], default="flat",
+                    help="flat: the sharded flat retrieval benchmark (default); "
+                         "paged: the paged-KV block-sparse decode step")
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="paged: number of (batch, head) sequences (default 8 x 32; fewer "
+                         "are for profiler captures only)")
     ap.add_argument("--rows", type=int, default=N_ROWS,
                     help="total rows (default 64Mi, the benchmark workload; smaller "
                          "values are for profiler captures only)")
@@ -392,7 +534,8 @@ def main():
         res = run_reference(args, rank, world)
     else:
         rank, world, local = init_dist()
-        res = run_ours(args, rank, world, local)
+        runner = run_paged if args.config == "paged" else run_ours
+        res = runner(args, rank, world, local)
         if world > 1:
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()

@@ -12,6 +12,8 @@ import os
 from . import build as _build
 
 HMM_OK = 0
+HMM_ERR_INVALID, HMM_ERR_CUDA, HMM_ERR_OOM = 1, 2, 3
+HMM_ERR_BOUNDS, HMM_ERR_TIMEOUT, HMM_ERR_UNSUPPORTED = 4, 5, 6
 STATUS_NAMES = {
     0: "HMM_OK", 1: "HMM_ERR_INVALID", 2: "HMM_ERR_CUDA", 3: "HMM_ERR_OOM",
     4: "HMM_ERR_BOUNDS", 5: "HMM_ERR_TIMEOUT", 6: "HMM_ERR_UNSUPPORTED",
@@ -37,6 +39,15 @@ SIGNATURES = {
     "hmm_ip_topk_f32_noalloc": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _F, _P, _P]),
     "hmm_shard_merge_topk_workspace_size": (_S, [_I, _I, _I]),
     "hmm_shard_merge_topk": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
+    "hmm_paged_kv_summary_f32": (C.c_int, [_P, _I, _I, _I, _P, _I, _I, _P, _P]),
+    "hmm_paged_workspace_size": (_S, [_I, _I, _I, _I]),
+    "hmm_paged_kv_summary_bf16": (C.c_int, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S,
+                                            _P]),
+    "hmm_block_pages": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _P]),
+    "hmm_block_sparse_attention_bf16": (C.c_int, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I,
+                                                  _P, _I, _P, _P, _S, _P]),
+    "hmm_block_sparse_decode_bf16": (C.c_int, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I,
+                                               _I, _P, _P, _P, _S, _P]),
     "hmm_kernel_launches": (_I, []),
     "hmm_profile_enable": (C.c_int, [C.c_int]),
     "hmm_profile_read": (C.c_int, [_P, _P]),

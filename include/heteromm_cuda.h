@@ -150,12 +150,95 @@ hmm_status_t hmm_ip_topk_f32_noalloc(const float* mem, int64_t n_rows, int64_t d
                                      int32_t* out_idx, float* out_scores, float threshold,
                                      uint64_t* out_bitmap, void* stream);
 
+/* ------------------------------------------------------------ paged KV
+ * Paged KV cache: physical page `phys` holds `page_tokens` consecutive tokens
+ * of one sequence as [page_tokens][D] bf16 (K and V in separate page arrays
+ * of n_pages pages); page_table[s*pages_per_seq + p] is the physical page of
+ * logical page p of sequence s.  D % 4 == 0, 4 <= D <= 512,
+ * seq_len <= pages_per_seq * page_tokens, every sequence has seq_len tokens.
+ * A page-table entry outside [0, n_pages) read by a kernel (or a negative
+ * block id) makes the call return HMM_ERR_BOUNDS; the kernels never follow
+ * such an entry.  Calls that report device-side bounds wait for `stream`.
+ *
+ * PagedKVIndexBuilder (reference steps/build_memory.h:152-182,
+ * steps/example_kernel/paged_kv_index_builder.cpp:18-85) on contiguous fp32
+ * keys [n_seq][L][D]: page p pools tokens [p*page_size, min(+page_size, L))
+ * (fp32 sum in token order, then / count) and, with a non-NULL weight
+ * [out_dim][D], projects it (fp32, d ascending, no FMA).
+ * out [n_seq][ceil(L/page_size)][weight ? out_dim : D], bit-identical to the
+ * reference.  L == 0 writes nothing (the reference's empty memory). */
+hmm_status_t hmm_paged_kv_summary_f32(const float* keys, int64_t n_seq, int64_t L, int64_t D,
+                                      const float* weight, int64_t out_dim, int64_t page_size,
+                                      float* out, void* stream);
+
+/* Workspace for the three paged calls below (n_sel = selected blocks per
+ * sequence, or top_blocks; the summary needs 256 bytes). */
+size_t hmm_paged_workspace_size(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_t D);
+
+/* Block summaries of a paged bf16 key cache: summary b of sequence s is the
+ * fp32 mean of tokens [b*block_tokens, min(+block_tokens, seq_len)), summed
+ * in token order as paged_kv_index_builder.cpp:57-67 does (the projection is
+ * left out).  out [n_seq][ceil(seq_len/block_tokens)][D] fp32, 16-byte
+ * aligned.  Bit-identical to the reference arithmetic. */
+hmm_status_t hmm_paged_kv_summary_bf16(const uint16_t* k_pages, int64_t n_pages,
+                                       const int32_t* page_table, int64_t n_seq,
+                                       int64_t pages_per_seq, int64_t seq_len,
+                                       int64_t page_tokens, int64_t block_tokens, int64_t D,
+                                       float* out, void* workspace, size_t workspace_bytes,
+                                       void* stream);
+
+/* Physical pages of the selected blocks (the reference has no page table; this
+ * is the paged form of the token list of block_sparse_attention.cpp:53-63):
+ * for each sequence, logical pages [b*pages_per_block, (b+1)*pages_per_block)
+ * of each selected block b in selection order, clipped to [0, pages_per_seq),
+ * mapped through the page table.  out_pages [n_seq][n_sel*pages_per_block]
+ * (-1 after the last), out_counts [n_seq] (nullable).  Integer, bit-exact. */
+hmm_status_t hmm_block_pages(const int32_t* page_table, int64_t n_seq, int64_t pages_per_seq,
+                             const int32_t* blocks, int64_t n_sel, int64_t pages_per_block,
+                             int32_t* out_pages, int32_t* out_counts, void* stream);
+
+/* BlockSparseAttention (reference steps/apply_memory.h:169-213,
+ * steps/example_kernel/block_sparse_attention.cpp:21-126), one query per
+ * sequence (decode), over the paged bf16 cache: tokens = concatenation of
+ * [b*block_tokens, min(+block_tokens, seq_len)) over the selected blocks in
+ * order; s_i = (q.k_i) * (1/sqrtf(D)); softmax with the maximum subtracted;
+ * out = sum_i w_i v_i.  An empty token list gives zeros.  fp32 results agree
+ * with the reference's to ~1e-6 relative (the device expf and the summation
+ * order differ from glibc's and from sequential order); the token / page
+ * lists are exact.  blocks [n_seq][n_sel] (n_sel <= 4096), q [n_seq][D] bf16,
+ * out [n_seq][D] fp32. */
+hmm_status_t hmm_block_sparse_attention_bf16(const uint16_t* q, const uint16_t* k_pages,
+                                             const uint16_t* v_pages, int64_t n_pages,
+                                             const int32_t* page_table, int64_t n_seq,
+                                             int64_t pages_per_seq, int64_t seq_len,
+                                             int64_t page_tokens, int64_t block_tokens,
+                                             int64_t D, const int32_t* blocks, int64_t n_sel,
+                                             float* out, void* workspace,
+                                             size_t workspace_bytes, void* stream);
+
+/* One decode step of the paged-KV path: per sequence, score the block
+ * summaries [n_seq][ceil(seq_len/block_tokens)][D] fp32 (16-byte aligned)
+ * against q widened from bf16 (InnerProductCompute arithmetic: fp32, d
+ * ascending, no FMA), keep the top_blocks best (TopKRetrieval: best first,
+ * ties to the lowest block id; bit-exact), then block-sparse attention over
+ * them as above.  out_blocks [n_seq][top_blocks] (nullable; -1 past the
+ * number of blocks) receives the selection. */
+hmm_status_t hmm_block_sparse_decode_bf16(const uint16_t* q, const float* summaries,
+                                          const uint16_t* k_pages, const uint16_t* v_pages,
+                                          int64_t n_pages, const int32_t* page_table,
+                                          int64_t n_seq, int64_t pages_per_seq,
+                                          int64_t seq_len, int64_t page_tokens,
+                                          int64_t block_tokens, int64_t D, int64_t top_blocks,
+                                          int32_t* out_blocks, float* out, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------ instrumentation
  * No reference counterpart (the reference steps are timed by their callers).
  * hmm_kernel_launches: kernels this library has launched since it was loaded.
  * hmm_profile_enable(1): from then on, record a CUDA event pair on the
- * launching stream around each launch of the dominant scoring kernel
- * (tc_score_select_kernel); hmm_profile_read waits for the recorded pairs and
+ * launching stream around each launch of the dominant kernel of an entry
+ * point (tc_score_select_kernel, bsa_split_kernel); hmm_profile_read waits
+ * for the recorded pairs and
  * returns their summed duration and count, then forgets them. */
 int64_t hmm_kernel_launches(void);
 hmm_status_t hmm_profile_enable(int enable);
