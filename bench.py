@@ -494,6 +494,121 @@ def run_paged(args, rank, world, local):
     return res
 
 
+# ---------------------------------------------------------------- config 3
+B_DOCS, B_VOCAB, B_MEAN, B_NQ, B_QLEN, B_K = 1_000_000, 30522, 60.0, 1024, 8, 10
+SEED_CORPUS, SEED_BQ = 6, 8
+
+
+def run_bm25(args, rank, world, local):
+    """BM25 top-10 over a 1M-doc CSR index (Zipf(1.1) terms over 30,522,
+    Poisson(60) lengths), 1,024 queries of 8 distinct Zipf terms.  Queries are
+    split across ranks (every rank holds the whole index; no exchange)."""
+    import heteromm_b200 as hmm
+    from heteromm_b200 import _abi
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import gen
+    dev = torch.device("cuda", local)
+    hmm.load()
+    n_docs = args.docs if args.docs else B_DOCS
+    tp, pd, tf, dl = gen.bm25_corpus(SEED_CORPUS, n_docs, B_VOCAB, B_MEAN)
+    n_q = args.queries if args.queries else B_NQ
+    qall = gen.bm25_queries(SEED_BQ, n_q, B_QLEN, B_VOCAB)
+    per = n_q // world
+    q_np = qall[rank * per:(rank + 1) * per]
+    t0 = time.perf_counter()
+    index = hmm.BM25Index(tp, pd, tf, dl, dev)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    q = torch.from_numpy(q_np).to(dev)
+    for _ in range(args.warmup):
+        index.topk(q, B_K)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _abi.profile_read()
+    _abi.profile_enable(True)
+    with ClockSampler(local) as clk:
+        l0 = _abi.kernel_launches()
+        e0.record(stream)
+        for _ in range(args.steps):
+            index.topk(q, B_K)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        launches = _abi.kernel_launches() - l0
+    _abi.profile_enable(False)
+    k_total, k_n = _abi.profile_read()
+    ms = e0.elapsed_time(e1) / args.steps
+    kern_ms = k_total / max(k_n, 1)
+    q_host = torch.from_numpy(q_np).pin_memory()
+    q_dev = torch.empty_like(q)
+    oi = torch.empty((per, B_K), dtype=torch.int32).pin_memory()
+    osc = torch.empty((per, B_K), dtype=torch.float64).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        i, sc = index.topk(q_dev, B_K)
+        oi.copy_(i, non_blocking=True)
+        osc.copy_(sc, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, kern_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return None
+    pk, pk_kind = peaks()
+    df = tp[1:] - tp[:-1]
+    post = int(df[q_np].sum())      # postings scored per step (all query terms distinct)
+    # algorithmic bytes: an int32 doc id + uint16 tf per posting, plus one fp64
+    # score per document per query for the top-k scan
+    bytes_alg = post * 6 + per * n_docs * 8
+    achieved = bytes_alg / (kern_ms * 1e-3) / 1e9
+    res = {
+        "metric": "BM25 top-10 queries per second", "value": n_q / (ms * 1e-3),
+        "unit": "queries/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded Zipf/Poisson corpus standing in for a BeIR-style corpus)",
+        "config": {"workload": f"BM25: {n_docs} docs, vocab {B_VOCAB}, {tp[-1]} postings, "
+                               f"{n_q} queries x {B_QLEN} terms, top-{B_K}",
+                   "parallelism": f"query split x{world}",
+                   "postings_per_step": post, "index_prepare_s": build_s,
+                   "l2": "inputs larger than L2 (postings read per step > 126 MB)"},
+        "e2e": {"value": n_q / (e2e_ms * 1e-3), "unit": "queries/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": per * B_QLEN * 4,
+                "d2h_bytes_per_step": per * B_K * (4 + 8)},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "kernel": "bm25_range_kernel", "kernel_ms": kern_ms,
+                     "kernel_launches_timed": k_n, "peak_kind": f"{pk_kind} copy bandwidth",
+                     "traffic": traffic_per_launch("bm25_range_kernel", per)},
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        sub_docs = 100_000
+        ctp, cpd, ctf, _ = gen.bm25_corpus(SEED_CORPUS, sub_docs, B_VOCAB, B_MEAN)
+        idx = O.RefBM25(ctp, cpd, ctf, sub_docs)
+        n_cq = 8
+        t = time.perf_counter()
+        for i in range(n_cq):
+            idx.query(qall[i])
+        dt = time.perf_counter() - t
+        idx.close()
+        res["cpu_baseline"] = {"value": n_cq / dt, "unit": "queries/s", "cores": 1,
+                               "kind": "reference",
+                               "sample": f"{n_cq} queries on a {sub_docs}-doc corpus from the "
+                                         f"same generator (the reference scans every document "
+                                         f"per query term), {dt:.2f} s"}
+    return res
+
+
 def traffic_per_launch(kernel: str, units: int):
     """DRAM bytes (read + write) of one launch of `kernel` from its committed
     ncu capture, scaled from the capture's units (rows, sequences) to `units`:
@@ -514,9 +629,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["flat", "paged"], default="flat",
+    ap.add_argument("--config", choices=["flat", "paged", "bm25"], default="flat",
                     help="flat: the sharded flat retrieval benchmark (default); "
-                         "paged: the paged-KV block-sparse decode step")
+                         "paged: the paged-KV block-sparse decode step; "
+                         "bm25: BM25 top-10 over a CSR index")
+    ap.add_argument("--queries", type=int, default=0,
+                    help="bm25: number of queries (default 1,024; fewer are for profiler "
+                         "captures only)")
+    ap.add_argument("--docs", type=int, default=0,
+                    help="bm25: number of documents (default 1M; fewer are for profiler "
+                         "captures only)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="paged: number of (batch, head) sequences (default 8 x 32; fewer "
                          "are for profiler captures only)")
@@ -534,7 +656,7 @@ def main():
         res = run_reference(args, rank, world)
     else:
         rank, world, local = init_dist()
-        runner = run_paged if args.config == "paged" else run_ours
+        runner = {"flat": run_ours, "paged": run_paged, "bm25": run_bm25}[args.config]
         res = runner(args, rank, world, local)
         if world > 1:
             torch.distributed.barrier()

@@ -48,6 +48,13 @@ SIGNATURES = {
                                                   _P, _I, _P, _P, _S, _P]),
     "hmm_block_sparse_decode_bf16": (C.c_int, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I,
                                                _I, _P, _P, _P, _S, _P]),
+    "hmm_bm25_stats_host": (C.c_int, [_P, _I, _P, _I, _P, _P]),
+    "hmm_bm25_skips_count": (_S, [_I, _I]),
+    "hmm_bm25_prepare": (C.c_int, [_P, _P, _P, _I, _P, _I, _P, C.c_double, _P, _P, _P, _S,
+                                   _P]),
+    "hmm_bm25_topk_workspace_size": (_S, [_I, _I, _I]),
+    "hmm_bm25_topk_csr": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _P, _S,
+                                    _P]),
     "hmm_kernel_launches": (_I, []),
     "hmm_profile_enable": (C.c_int, [C.c_int]),
     "hmm_profile_read": (C.c_int, [_P, _P]),

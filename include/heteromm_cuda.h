@@ -232,6 +232,54 @@ hmm_status_t hmm_block_sparse_decode_bf16(const uint16_t* q, const float* summar
                                           int32_t* out_blocks, float* out, void* workspace,
                                           size_t workspace_bytes, void* stream);
 
+/* ----------------------------------------------------------------- BM25
+ * FusedBM25Retrieval (reference steps/example_kernel/bm25_fpga_retrieval.cpp:
+ * 143-205) over a CSR inverted index: postings of term t are
+ * [term_ptr[t], term_ptr[t+1]) with ascending doc ids post_doc (int32) and
+ * term frequencies post_tf (uint16); doc_len[d] = sum of doc d's term
+ * frequencies.  Scores are fp64 BM25 (k1 = 1.2, b = 0.75) summed over the
+ * query's distinct in-vocabulary terms in ascending term-id order (the
+ * reference sums in unordered_map order), bit-identical to the reference's
+ * doubles for that order.  Top-k best first, ties to the lowest doc id; docs
+ * without a query term score 0.0 and rank like any other doc.
+ *
+ * hmm_bm25_stats_host (host arrays, no device work): idf[t] =
+ * log((N - df + 0.5) / (df + 0.5) + 1.0) (0 for df = 0) and avg_dl exactly
+ * as the reference computes them (:158-178), with the host's libm. */
+hmm_status_t hmm_bm25_stats_host(const int64_t* term_ptr, int64_t n_terms,
+                                 const int32_t* doc_len, int64_t n_docs, double* idf,
+                                 double* avg_dl);
+
+/* Index preparation, once per index (device arrays): skips
+ * [n_terms][ceil(n_docs/HMM_BM25_RANGE_DOCS)+1] int32 (hmm_bm25_skips_count
+ * entries): the first posting of each term at each doc-range boundary; impact
+ * [n_postings] fp64: the amount posting p adds to its doc's score,
+ * idf * (tf * (k1 + 1)) / (tf + k1 * (1 - b + b * dl / avg_dl)) with the
+ * reference's operation order (it depends on the term, the doc and corpus
+ * statistics only; the reference ignores the query's own term frequency).
+ * idf [n_terms] fp64 is the device copy of hmm_bm25_stats_host's.  A posting
+ * whose doc id is outside [0, n_docs) returns HMM_ERR_BOUNDS (the call waits
+ * for `stream`); workspace >= 256 bytes. */
+#define HMM_BM25_RANGE_DOCS 4096
+size_t hmm_bm25_skips_count(int64_t n_terms, int64_t n_docs);
+hmm_status_t hmm_bm25_prepare(const int64_t* term_ptr, const int32_t* post_doc,
+                              const uint16_t* post_tf, int64_t n_terms, const int32_t* doc_len,
+                              int64_t n_docs, const double* idf, double avg_dl, int32_t* skips,
+                              double* impact, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* Top-k per query over the prepared index.  qterms [n_queries][qlen] int32
+ * (ids outside [0, n_terms) and repeats are ignored; qlen <= 64),
+ * 1 <= k <= 128 with ceil(n_docs/HMM_BM25_RANGE_DOCS) * k <= 16384.
+ * out_idx [n_queries][k] int32 (-1 past min(k, n_docs)), out_scores
+ * [n_queries][k] fp64 or NULL.  Asynchronous. */
+size_t hmm_bm25_topk_workspace_size(int64_t n_docs, int64_t n_queries, int64_t k);
+hmm_status_t hmm_bm25_topk_csr(const int32_t* post_doc, const double* impact,
+                               int64_t n_postings, int64_t n_terms, int64_t n_docs,
+                               const int32_t* skips, const int32_t* qterms, int64_t n_queries,
+                               int64_t qlen, int64_t k, int32_t* out_idx, double* out_scores,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------ instrumentation
  * No reference counterpart (the reference steps are timed by their callers).
  * hmm_kernel_launches: kernels this library has launched since it was loaded.
