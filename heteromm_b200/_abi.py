@@ -46,6 +46,8 @@ SIGNATURES = {
     "hmm_block_pages": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _P]),
     "hmm_block_sparse_attention_bf16": (C.c_int, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I,
                                                   _P, _I, _P, _P, _S, _P]),
+    "hmm_block_sparse_attention_f32": (C.c_int, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P, _P,
+                                                 _S, _P]),
     "hmm_block_sparse_decode_bf16": (C.c_int, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I,
                                                _I, _P, _P, _P, _S, _P]),
     "hmm_bm25_stats_host": (C.c_int, [_P, _I, _P, _I, _P, _P]),
@@ -55,6 +57,11 @@ SIGNATURES = {
     "hmm_bm25_topk_workspace_size": (_S, [_I, _I, _I]),
     "hmm_bm25_topk_csr": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _P, _S,
                                     _P]),
+    "hmm_indexer_workspace_size": (_S, [_I, _I]),
+    "hmm_lserve_topk_i16": (C.c_int, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _P, _S, _P]),
+    "hmm_seer_budget_i16": (C.c_int, [_P, _I, _P, _P, _I, _I, _I, _P, _P, _S, _P]),
+    "hmm_seer_words_per_query": (_I, [_I, _I]),
+    "hmm_seer_threshold_i16": (C.c_int, [_P, _I, _P, _P, _I, _I, _I, _P, _P]),
     "hmm_kernel_launches": (_I, []),
     "hmm_profile_enable": (C.c_int, [C.c_int]),
     "hmm_profile_read": (C.c_int, [_P, _P]),

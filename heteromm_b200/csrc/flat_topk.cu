@@ -460,6 +460,17 @@ hmm_status_t launch_pool_merge(const uint64_t* pool, int64_t cap, const int* cou
     return check_launch("merge_candidates_kernel(pool)");
 }
 
+// Same merge with int32 indices (the indexer entry points).
+hmm_status_t launch_cand_merge_i32(const uint64_t* cand, int64_t cap, const int* counts, int nq,
+                                   int k, int32_t* out_idx, float* out_scores, cudaStream_t st) {
+    hmm_status_t s = prepare_merge_kernel<int32_t>();
+    if (s != HMM_OK) return s;
+    const size_t msmem = sizeof(uint64_t) * next_pow2(k);
+    merge_candidates_kernel<int32_t><<<(unsigned)nq, 256, msmem, st>>>(
+        cand, cap, k, 0, out_idx, out_scores, counts);
+    return check_launch("merge_candidates_kernel(i32)");
+}
+
 bool tc_path_applies(int64_t n, int64_t dim, int64_t nq, int64_t k, const void* mem,
                      const void* qry);
 size_t tc_ws_bytes(int64_t n, int64_t nq, int64_t k);

@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <type_traits>
 
 #include "heteromm_cuda.h"
 #include "hmm_common.cuh"
@@ -41,6 +42,7 @@ struct PagedCache {
     int seq_len;
     int page_tokens;
     int D;
+    bool contiguous;         // [n_seq][seq_len][D] without a page table
 };
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -49,8 +51,10 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w 
 // First element of logical token t of sequence s in `base` (a K or V page
 // array laid out like c.pages), or nullptr after flagging status bit 0 when
 // the page-table entry is outside [0, n_pages).
-__device__ __forceinline__ const uint16_t* token_row(const PagedCache& c, const uint16_t* base,
-                                                     int s, int t, int* status) {
+template <typename T = uint16_t>
+__device__ __forceinline__ const T* token_row(const PagedCache& c, const T* base, int s, int t,
+                                              int* status) {
+    if (c.contiguous) return base + ((int64_t)s * c.seq_len + t) * c.D;
     const int p = t / c.page_tokens;
     const int32_t phys = __ldg(c.table + (int64_t)s * c.pages_per_seq + p);
     if (phys < 0 || (int64_t)phys >= c.n_pages) {
@@ -202,6 +206,9 @@ struct BsaArgs {
     PagedCache k;            // K cache (pages, table, geometry)
     const uint16_t* v;       // V pages, same layout and table as K
     const uint16_t* q;       // [n_seq][D] bf16
+    const float* kf;         // fp32 element form (contiguous caches): K, V, q
+    const float* vf;
+    const float* qf32;
     const int32_t* blocks;   // [n_seq][blocks_stride], first n_sel used
     int blocks_stride;
     int n_sel;
@@ -250,6 +257,20 @@ __device__ __forceinline__ int list_token(const int* pre, const int32_t* bl, int
 
 // One block per (split, sequence): scores of its share of the token list,
 // softmax statistics of that share, and the unnormalised weighted sum of V.
+template <typename T>
+__device__ __forceinline__ void load4(const T* row, int gi, float* o);
+template <>
+__device__ __forceinline__ void load4<uint16_t>(const uint16_t* row, int gi, float* o) {
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(row) + gi);
+    o[0] = bf16_lo(w.x); o[1] = bf16_hi(w.x); o[2] = bf16_lo(w.y); o[3] = bf16_hi(w.y);
+}
+template <>
+__device__ __forceinline__ void load4<float>(const float* row, int gi, float* o) {
+    const float4 w = __ldg(reinterpret_cast<const float4*>(row) + gi);
+    o[0] = w.x; o[1] = w.y; o[2] = w.z; o[3] = w.w;
+}
+
+template <typename T>
 __global__ void __launch_bounds__(BSA_THREADS) bsa_split_kernel(const BsaArgs a) {
     extern __shared__ float bsm[];
     const int split = blockIdx.x, s = blockIdx.y;
@@ -295,30 +316,35 @@ __global__ void __launch_bounds__(BSA_THREADS) bsa_split_kernel(const BsaArgs a)
         return;
     }
 
+    const T* kbase = std::is_same<T, float>::value ? reinterpret_cast<const T*>(a.kf)
+                                                  : reinterpret_cast<const T*>(a.k.pages);
+    const T* vbase = std::is_same<T, float>::value ? reinterpret_cast<const T*>(a.vf)
+                                                  : reinterpret_cast<const T*>(a.v);
+    const T* qrow = (std::is_same<T, float>::value ? reinterpret_cast<const T*>(a.qf32)
+                                                   : reinterpret_cast<const T*>(a.q)) +
+                    (int64_t)s * D;
     // q in registers: lane owns column groups lane + 32g
     float qf[PK_GROUPS][4];
 #pragma unroll
     for (int g = 0; g < PK_GROUPS; ++g) {
         const int gi = lane + 32 * g;
-        uint2 w = gi < ng ? reinterpret_cast<const uint2*>(a.q + (int64_t)s * D)[gi]
-                          : make_uint2(0u, 0u);
-        qf[g][0] = bf16_lo(w.x); qf[g][1] = bf16_hi(w.x);
-        qf[g][2] = bf16_lo(w.y); qf[g][3] = bf16_hi(w.y);
+        if (gi < ng) load4<T>(qrow, gi, qf[g]);
+        else qf[g][0] = qf[g][1] = qf[g][2] = qf[g][3] = 0.0f;
     }
 
     // pass 1: s_j = (q . k_j) * scale; four tokens per warp in flight
     for (int jb = j0 + warp * 4; jb < j1; jb += BSA_WARPS * 4) {
-        uint2 kv[4][PK_GROUPS];
+        float kv[4][PK_GROUPS][4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int j = jb + u;
-            const uint16_t* row = nullptr;
-            if (j < j1) row = token_row(a.k, a.k.pages, s, list_token(pre, bl, a.n_sel, a.block_tokens, j), a.status);
+            const T* row = nullptr;
+            if (j < j1) row = token_row<T>(a.k, kbase, s, list_token(pre, bl, a.n_sel, a.block_tokens, j), a.status);
 #pragma unroll
             for (int g = 0; g < PK_GROUPS; ++g) {
                 const int gi = lane + 32 * g;
-                kv[u][g] = (row && gi < ng) ? __ldg(reinterpret_cast<const uint2*>(row) + gi)
-                                            : make_uint2(0u, 0u);
+                if (row && gi < ng) load4<T>(row, gi, kv[u][g]);
+                else kv[u][g][0] = kv[u][g][1] = kv[u][g][2] = kv[u][g][3] = 0.0f;
             }
         }
 #pragma unroll
@@ -326,10 +352,10 @@ __global__ void __launch_bounds__(BSA_THREADS) bsa_split_kernel(const BsaArgs a)
             float dot = 0.0f;
 #pragma unroll
             for (int g = 0; g < PK_GROUPS; ++g) {
-                dot = fmaf(qf[g][0], bf16_lo(kv[u][g].x), dot);
-                dot = fmaf(qf[g][1], bf16_hi(kv[u][g].x), dot);
-                dot = fmaf(qf[g][2], bf16_lo(kv[u][g].y), dot);
-                dot = fmaf(qf[g][3], bf16_hi(kv[u][g].y), dot);
+                dot = fmaf(qf[g][0], kv[u][g][0], dot);
+                dot = fmaf(qf[g][1], kv[u][g][1], dot);
+                dot = fmaf(qf[g][2], kv[u][g][2], dot);
+                dot = fmaf(qf[g][3], kv[u][g][3], dot);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
@@ -357,33 +383,30 @@ __global__ void __launch_bounds__(BSA_THREADS) bsa_split_kernel(const BsaArgs a)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[g][i] = 0.0f;
     for (int jb = j0 + warp * 4; jb < j1; jb += BSA_WARPS * 4) {
-        uint2 vv[4][PK_GROUPS];
+        float vv[4][PK_GROUPS][4];
         float e[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int j = jb + u;
-            const uint16_t* row = nullptr;
+            const T* row = nullptr;
             e[u] = 0.0f;
             if (j < j1) {
-                row = token_row(a.k, a.v, s, list_token(pre, bl, a.n_sel, a.block_tokens, j), a.status);
+                row = token_row<T>(a.k, vbase, s, list_token(pre, bl, a.n_sel, a.block_tokens, j), a.status);
                 e[u] = sc[j - j0];
             }
 #pragma unroll
             for (int g = 0; g < PK_GROUPS; ++g) {
                 const int gi = lane + 32 * g;
-                vv[u][g] = (row && gi < ng) ? __ldg(reinterpret_cast<const uint2*>(row) + gi)
-                                            : make_uint2(0u, 0u);
+                if (row && gi < ng) load4<T>(row, gi, vv[u][g]);
+                else vv[u][g][0] = vv[u][g][1] = vv[u][g][2] = vv[u][g][3] = 0.0f;
             }
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int g = 0; g < PK_GROUPS; ++g) {
-                acc[g][0] = fmaf(e[u], bf16_lo(vv[u][g].x), acc[g][0]);
-                acc[g][1] = fmaf(e[u], bf16_hi(vv[u][g].x), acc[g][1]);
-                acc[g][2] = fmaf(e[u], bf16_lo(vv[u][g].y), acc[g][2]);
-                acc[g][3] = fmaf(e[u], bf16_hi(vv[u][g].y), acc[g][3]);
-            }
+            for (int g = 0; g < PK_GROUPS; ++g)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[g][i] = fmaf(e[u], vv[u][g][i], acc[g][i]);
     }
 #pragma unroll
     for (int g = 0; g < PK_GROUPS; ++g) {
@@ -713,7 +736,8 @@ bool page_path_applies(int64_t D, int64_t page_tokens, int64_t block_tokens, con
 
 hmm_status_t run_bsa(const BsaArgs& a0, int64_t n_seq, int64_t D, float* out, unsigned char* ws,
                      size_t ws_bytes, cudaStream_t st) {
-    if (page_path_applies(D, a0.k.page_tokens, a0.block_tokens, a0.k.pages, a0.v, a0.q)) {
+    if (!a0.kf && !a0.k.contiguous &&
+        page_path_applies(D, a0.k.page_tokens, a0.block_tokens, a0.k.pages, a0.v, a0.q)) {
         const BsaPlan p = bsa_page_plan(n_seq, a0.n_sel, a0.block_tokens, a0.k.page_tokens, D);
         const size_t need = up256(p.part_bytes) + 256;
         if (!ws || ws_bytes < need)
@@ -739,10 +763,12 @@ hmm_status_t run_bsa(const BsaArgs& a0, int64_t n_seq, int64_t D, float* out, un
     a.splits = p.splits;
     a.split_tokens = p.split_tokens;
     a.part = reinterpret_cast<float*>(ws);
-    HMM_CUDA_TRY(cudaFuncSetAttribute(bsa_split_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    const bool f32 = a.kf != nullptr;
+    auto kern = f32 ? bsa_split_kernel<float> : bsa_split_kernel<uint16_t>;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)p.smem));
     const ProfileMark pm = profile_begin(st);
-    bsa_split_kernel<<<dim3((unsigned)p.splits, (unsigned)n_seq), BSA_THREADS, p.smem, st>>>(a);
+    kern<<<dim3((unsigned)p.splits, (unsigned)n_seq), BSA_THREADS, p.smem, st>>>(a);
     hmm_status_t s = check_launch("bsa_split_kernel");
     profile_end(pm, st);
     if (s != HMM_OK) return s;
@@ -800,7 +826,7 @@ extern "C" hmm_status_t hmm_paged_kv_summary_bf16(const uint16_t* k_pages, int64
     int* status = static_cast<int*>(workspace);
     HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
     PagedCache c{k_pages, page_table, n_pages, (int)pages_per_seq, (int)seq_len,
-                 (int)page_tokens, (int)D};
+                 (int)page_tokens, (int)D, false};
     const int n_blocks = (int)((seq_len + block_tokens - 1) / block_tokens);
     const int64_t units = n_seq * n_blocks;
     const unsigned grid = (unsigned)((units + 7) / 8);
@@ -876,7 +902,7 @@ extern "C" hmm_status_t hmm_block_sparse_attention_bf16(
     HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
     BsaArgs a{};
     a.k = PagedCache{k_pages, page_table, n_pages, (int)pages_per_seq, (int)seq_len,
-                     (int)page_tokens, (int)D};
+                     (int)page_tokens, (int)D, false};
     a.v = v_pages;
     a.q = q;
     a.blocks = blocks;
@@ -935,7 +961,7 @@ extern "C" hmm_status_t hmm_block_sparse_decode_bf16(
     const int64_t n_sel = std::min<int64_t>(top_blocks, n_blocks);
     BsaArgs a{};
     a.k = PagedCache{k_pages, page_table, n_pages, (int)pages_per_seq, (int)seq_len,
-                     (int)page_tokens, (int)D};
+                     (int)page_tokens, (int)D, false};
     a.v = v_pages;
     a.q = q;
     a.blocks = sel;
@@ -947,4 +973,52 @@ extern "C" hmm_status_t hmm_block_sparse_decode_bf16(
     s = run_bsa(a, n_seq, D, out, ws, st_off + 256, st);
     if (s != HMM_OK) return s;
     return read_status(status, st, "hmm_block_sparse_decode_bf16");
+}
+
+extern "C" hmm_status_t hmm_block_sparse_attention_f32(const float* q, const float* keys,
+                                                       const float* values, int64_t n_seq,
+                                                       int64_t L, int64_t D,
+                                                       int64_t block_tokens,
+                                                       const int32_t* blocks, int64_t n_sel,
+                                                       float* out, void* workspace,
+                                                       size_t workspace_bytes, void* stream) {
+    HMM_REQUIRE(n_seq >= 0 && n_seq <= 65535, "n_seq must be in [0, 65535]");
+    HMM_REQUIRE(D >= 4 && D <= PK_MAX_D && D % 4 == 0,
+                "D must be a multiple of 4 in [4, %d], got %lld", PK_MAX_D, (long long)D);
+    HMM_REQUIRE(L >= 0 && L < (int64_t(1) << 31), "L out of range");
+    HMM_REQUIRE(block_tokens >= 1, "block_tokens must be >= 1");
+    HMM_REQUIRE(n_sel >= 0 && n_sel <= BSA_MAX_SEL, "n_sel must be in [0, %d]", BSA_MAX_SEL);
+    if (n_seq == 0) return HMM_OK;
+    HMM_REQUIRE(q && out && (blocks || n_sel == 0), "null pointer");
+    HMM_REQUIRE(L == 0 || (keys && values), "null keys / values");
+    HMM_REQUIRE((reinterpret_cast<uintptr_t>(q) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(keys) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(values) % 16) == 0,
+                "q, keys and values must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (n_sel == 0 || L == 0) {
+        HMM_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(float) * n_seq * D, st));
+        return HMM_OK;
+    }
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    const size_t st_off = up256(bsa_part_bytes(n_seq, n_sel, block_tokens, D));
+    if (!ws || workspace_bytes < st_off + 256)
+        return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", workspace_bytes,
+                         st_off + 256);
+    int* status = reinterpret_cast<int*>(ws + st_off);
+    HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
+    BsaArgs a{};
+    a.k = PagedCache{nullptr, nullptr, n_seq, 1, (int)L, (int)L, (int)D, true};
+    a.kf = keys;
+    a.vf = values;
+    a.qf32 = q;
+    a.blocks = blocks;
+    a.blocks_stride = (int)n_sel;
+    a.n_sel = (int)n_sel;
+    a.block_tokens = (int)block_tokens;
+    a.scale = 1.0f / sqrtf((float)D);
+    a.status = status;
+    hmm_status_t s = run_bsa(a, n_seq, D, out, ws, st_off + 256, st);
+    if (s != HMM_OK) return s;
+    return read_status(status, st, "hmm_block_sparse_attention_f32");
 }

@@ -102,3 +102,23 @@ def block_sparse_decode_bf16(q: torch.Tensor, summaries: torch.Tensor, k_pages: 
          block_tokens, D, top_blocks, blocks.data_ptr(), out.data_ptr(), ws.data_ptr(),
          ws.numel(), _stream())
     return blocks, out
+
+
+def block_sparse_attention_f32(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                               block_tokens: int, blocks: torch.Tensor) -> torch.Tensor:
+    """Attention over contiguous fp32 K/V [n_seq, L, D] (or [L, D]): [n_seq, D] fp32."""
+    for t, n in ((q, "q"), (keys, "keys"), (values, "values")):
+        _check(t, torch.float32, n)
+    _check(blocks, torch.int32, "blocks")
+    k3 = keys if keys.dim() == 3 else keys.unsqueeze(0)
+    v3 = values if values.dim() == 3 else values.unsqueeze(0)
+    q2 = q if q.dim() == 2 else q.unsqueeze(0)
+    b2 = blocks if blocks.dim() == 2 else blocks.unsqueeze(0)
+    n_seq, L, D = k3.shape
+    n_sel = b2.shape[1]
+    out = torch.empty((n_seq, D), dtype=torch.float32, device=q.device)
+    ws = workspace(load().hmm_paged_workspace_size(n_seq, n_sel, block_tokens, D), q.device)
+    call("hmm_block_sparse_attention_f32", q2.data_ptr(), k3.data_ptr(), v3.data_ptr(), n_seq, L,
+         D, block_tokens, b2.data_ptr(), n_sel, out.data_ptr(), ws.data_ptr(), ws.numel(),
+         _stream())
+    return out if q.dim() == 2 else out[0]

@@ -216,6 +216,16 @@ hmm_status_t hmm_block_sparse_attention_bf16(const uint16_t* q, const uint16_t* 
                                              float* out, void* workspace,
                                              size_t workspace_bytes, void* stream);
 
+/* The same attention on contiguous fp32 K/V (the reference's own
+ * KVCacheData<float> layout): keys, values [n_seq][L][D] fp32, q [n_seq][D]
+ * fp32, all 16-byte aligned.  Same token rule, same tolerance. */
+hmm_status_t hmm_block_sparse_attention_f32(const float* q, const float* keys,
+                                            const float* values, int64_t n_seq, int64_t L,
+                                            int64_t D, int64_t block_tokens,
+                                            const int32_t* blocks, int64_t n_sel, float* out,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* stream);
+
 /* One decode step of the paged-KV path: per sequence, score the block
  * summaries [n_seq][ceil(seq_len/block_tokens)][D] fp32 (16-byte aligned)
  * against q widened from bf16 (InnerProductCompute arithmetic: fp32, d
@@ -279,6 +289,43 @@ hmm_status_t hmm_bm25_topk_csr(const int32_t* post_doc, const double* impact,
                                const int32_t* skips, const int32_t* qterms, int64_t n_queries,
                                int64_t qlen, int64_t k, int32_t* out_idx, double* out_scores,
                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ indexers
+ * int16 sparse-attention indexers of one index head (the CPU references in
+ * kernels/lserve/indexer_lserve_tb.cpp:20-92,
+ * kernels/seerattention/indexer_seer_token_budget_tb.cpp:19-73,
+ * kernels/seerattention/indexer_seer_threshold_tb.cpp:18-77).
+ * past [L][D], queries [n_queries][D], new_keys [n_queries][D] int16 (4-byte
+ * aligned), D even <= 256.  Query q sits at position L + q/8 and sees
+ * positions 0 .. L + q/8: position p < L is past[p], position L + g is
+ * new_keys[min(8g + 7, q)].  Scores are exact int64 dot products (float
+ * where the reference converts them).  Top-k outputs are best first, ties to
+ * the lowest position / block, -1 padded; bit-exact. */
+size_t hmm_indexer_workspace_size(int64_t L, int64_t n_queries);
+
+/* LServe: per query, the top-k blocks of `block` positions (a power of two
+ * <= 32; the reference uses 16) by the maximum float score in the block.
+ * out [n_queries][topk] int32. */
+hmm_status_t hmm_lserve_topk_i16(const int16_t* past, int64_t L, const int16_t* queries,
+                                 const int16_t* new_keys, int64_t n_queries, int64_t D,
+                                 int64_t topk, int64_t block, int32_t* out, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* SeerAttention token budget: per query, the top-k positions by float
+ * score.  out [n_queries][topk] int32. */
+hmm_status_t hmm_seer_budget_i16(const int16_t* past, int64_t L, const int16_t* queries,
+                                 const int16_t* new_keys, int64_t n_queries, int64_t D,
+                                 int64_t topk, int32_t* out, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* SeerAttention threshold: bit p % 64 of word p / 64 of query q's row is set
+ * iff position p is visible and dot > threshold (strict).  out_bitmap
+ * [n_queries][hmm_seer_words_per_query(L, n_queries)] uint64 (rows cover the
+ * last query's window rounded up to 128 positions). */
+int64_t hmm_seer_words_per_query(int64_t L, int64_t n_queries);
+hmm_status_t hmm_seer_threshold_i16(const int16_t* past, int64_t L, const int16_t* queries,
+                                    const int16_t* new_keys, int64_t n_queries, int64_t D,
+                                    int64_t threshold, uint64_t* out_bitmap, void* stream);
 
 /* ------------------------------------------------------ instrumentation
  * No reference counterpart (the reference steps are timed by their callers).

@@ -166,3 +166,21 @@ def test_bounds_are_reported(cuda):
                                         torch.tensor([[0, -1], [1, 2]], dtype=torch.int32,
                                                      device=cuda))
     assert e.value.status == HMM_ERR_BOUNDS
+
+
+@pytest.mark.parametrize("L,D,bt,nsel", [(333, 64, 8, 5), (1000, 128, 64, 6), (50, 4, 7, 3)])
+def test_block_sparse_attention_f32_contiguous(cuda, L, D, bt, nsel):
+    """The reference's own layout: contiguous fp32 K/V, fp32 query."""
+    n_seq = 3
+    keys = gen.normal_f32(370 + L, (n_seq, L, D))
+    vals = gen.normal_f32(371 + L, (n_seq, L, D))
+    q = gen.normal_f32(372 + L, (n_seq, D))
+    nb = (L + bt - 1) // bt
+    blocks = np.stack([np.argsort(gen.uniform_f64(373 + s, nb))[:nsel]
+                       for s in range(n_seq)]).astype(np.int32)
+    blocks[2, 0] = nb + 3                  # past the end
+    out = hmm.block_sparse_attention_f32(T(q, cuda), T(keys, cuda), T(vals, cuda), bt,
+                                         T(blocks, cuda)).cpu().numpy()
+    for s in range(n_seq):
+        ref = O.block_sparse_attention_f32(keys[s], vals[s], blocks[s], q[s], bt)
+        np.testing.assert_allclose(out[s], ref, rtol=RTOL, atol=ATOL)
