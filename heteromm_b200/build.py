@@ -3,7 +3,8 @@
   lib/libheteromm_cuda.so   the C ABI (include/heteromm_cuda.h) and its sm_100a
                             kernels, compiled by nvcc from csrc/*.cu
   lib/libheteromm_steps.so  the C++17 heteromm step API (include/heteromm/dev),
-                            CPU bodies and GPU adapters, linked to the former
+                            CPU bodies and GPU adapters (src/*.cpp), linked
+                            to the former
 
 nvcc cross-compiles for sm_100a without a GPU; the built .so files travel with
 the repository snapshot to the GPU machine.
@@ -58,7 +59,8 @@ def build_steps(force: bool = False) -> str:
         return ""
     deps = srcs + glob.glob(os.path.join(INC, "heteromm", "**", "*.h"), recursive=True) + [CUDA_LIB]
     if force or _newer(STEPS_LIB, deps):
-        cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", f"-I{INC}",
+        cmd = ["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-Wall",
+               "-Wextra", f"-I{INC}",
                "-I/usr/local/cuda/include", "-o", STEPS_LIB, *srcs, f"-L{LIB_DIR}",
                "-lheteromm_cuda", "-Wl,-rpath,$ORIGIN", "-L/usr/local/cuda/lib64", "-lcudart"]
         _run(cmd)

@@ -1,0 +1,97 @@
+// device.h — shared plumbing of the GPU adapters behind the step classes:
+// status -> exception mapping and a grow-only per-thread device scratch.
+// Adapters are synchronous, like the reference steps: upload, run on the
+// legacy default stream, copy results back.
+#ifndef HETEROMM_B200_SRC_DEVICE_H_
+#define HETEROMM_B200_SRC_DEVICE_H_
+
+#include <cuda_runtime_api.h>
+
+#include <cstddef>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "heteromm_cuda.h"
+
+namespace heteromm {
+namespace gpu {
+
+// Nonzero status -> std::runtime_error carrying hmm_last_error(), the
+// reference's way of failing a kernel (exceptions out of run_*_kernel).
+inline void check(hmm_status_t st, const char* what) {
+    if (st != HMM_OK) throw std::runtime_error(std::string(what) + ": " + hmm_last_error());
+}
+
+inline void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// A device allocation reused across calls (grows, never shrinks).
+class DeviceBuffer {
+public:
+    DeviceBuffer() = default;
+    DeviceBuffer(const DeviceBuffer&) = delete;
+    DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+    ~DeviceBuffer() {
+        if (p_) cudaFree(p_);
+    }
+    void* get(size_t bytes) {
+        if (bytes > n_) {
+            if (p_) cudaFree(p_);
+            p_ = nullptr;
+            n_ = 0;
+            check_cuda(cudaMalloc(&p_, bytes < 256 ? 256 : bytes), "cudaMalloc");
+            n_ = bytes < 256 ? 256 : bytes;
+        }
+        return p_;
+    }
+    size_t size() const { return n_; }
+
+private:
+    void* p_ = nullptr;
+    size_t n_ = 0;
+};
+
+// Named scratch slots of the calling thread.
+enum Slot { kMem, kQuery, kOut, kOut2, kIdx, kWork, kAux, kAux2, kAux3, kSlots };
+inline DeviceBuffer& scratch(Slot s) {
+    thread_local DeviceBuffer buf[kSlots];
+    return buf[s];
+}
+
+template <typename T>
+T* upload(Slot s, const std::vector<T>& host) {
+    T* d = static_cast<T*>(scratch(s).get(sizeof(T) * (host.empty() ? 1 : host.size())));
+    if (!host.empty())
+        check_cuda(cudaMemcpy(d, host.data(), sizeof(T) * host.size(), cudaMemcpyHostToDevice),
+                   "cudaMemcpy H2D");
+    return d;
+}
+
+template <typename T>
+void download(std::vector<T>& host, const T* dev) {
+    if (!host.empty())
+        check_cuda(cudaMemcpy(host.data(), dev, sizeof(T) * host.size(), cudaMemcpyDeviceToHost),
+                   "cudaMemcpy D2H");
+}
+
+// Rows of a vector-of-vectors packed into one row-major array; every row
+// must have `cols` values.
+template <typename T>
+std::vector<T> pack_rows(const std::vector<std::vector<T>>& rows, size_t cols, const char* what) {
+    std::vector<T> out;
+    out.reserve(rows.size() * cols);
+    for (const auto& r : rows) {
+        if (r.size() < cols)
+            throw std::invalid_argument(std::string(what) + ": a row is shorter than the query");
+        out.insert(out.end(), r.begin(), r.begin() + (std::ptrdiff_t)cols);
+    }
+    return out;
+}
+
+}  // namespace gpu
+}  // namespace heteromm
+
+#endif  // HETEROMM_B200_SRC_DEVICE_H_

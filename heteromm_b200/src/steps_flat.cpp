@@ -1,0 +1,206 @@
+// steps_flat.cpp — InnerProductCompute, TopKRetrieval, ThresholdRetrieval and
+// InnerProductTopKRetrieval: CPU bodies (the reference's arithmetic,
+// steps/example_kernel/inner_product_compute.cpp:11-31,
+// topk_retrieval.cpp:13-31, threshold_retrieval.cpp:11-32) and GPU adapters
+// onto hmm_ip_score_f32 / hmm_topk_f32 / hmm_threshold_bitmap_f32 /
+// hmm_ip_topk_f32.
+#include <algorithm>
+#include <cmath>
+#include <iostream>
+#include <numeric>
+
+#include "device.h"
+#include "heteromm/dev/steps/compute_score.h"
+#include "heteromm/dev/steps/fused_steps/template.h"
+#include "heteromm/dev/steps/memory_retrieval.h"
+
+namespace heteromm {
+namespace step {
+
+namespace {
+// fp32 dot products in index order, each product rounded before the add.
+std::vector<float> cpu_scores(const std::vector<std::vector<float>>& mem,
+                              const std::vector<float>& q) {
+    std::vector<float> s(mem.size(), 0.0f);
+    for (size_t i = 0; i < mem.size(); ++i) {
+        float dot = 0.0f;
+        for (size_t j = 0; j < q.size(); ++j) dot += mem[i][j] * q[j];   // built without contraction
+        s[i] = dot;
+    }
+    return s;
+}
+
+// Indices of the min(k, n) best scores, best first, ties to the lowest index
+// (the reference's partial_sort by `>`, with its tie order pinned).
+std::vector<int> cpu_topk(const std::vector<float>& s, size_t k) {
+    const size_t n = s.size(), m = std::min(k, n);
+    std::vector<int> idx(n);
+    std::iota(idx.begin(), idx.end(), 0);
+    std::partial_sort(idx.begin(), idx.begin() + (std::ptrdiff_t)m, idx.end(), [&](int a, int b) {
+        const bool an = s[a] != s[a], bn = s[b] != s[b];
+        if (an || bn) return an != bn ? bn : a < b;   // NaN ranks below every number
+        return s[a] != s[b] ? s[a] > s[b] : a < b;
+    });
+    idx.resize(m);
+    return idx;
+}
+
+std::vector<unsigned long long> cpu_bitmap(const std::vector<float>& s, float thr) {
+    std::vector<unsigned long long> bm((s.size() + 63) / 64, 0ULL);
+    for (size_t i = 0; i < s.size(); ++i)
+        if (s[i] >= thr) bm[i / 64] |= 1ULL << (i % 64);
+    return bm;
+}
+
+void fpga_stub(const char* step) {
+    std::clog << "[" << step << "] FPGA kernel not implemented. exiting." << std::endl;
+}
+}  // namespace
+
+// ------------------------------------------------------------ InnerProduct
+void InnerProductCompute::run_test_kernel(const data_type::FlatIndexMemory<float>& memory,
+                                          const data_type::VectorQuery<float>& query,
+                                          data_type::VectorScore<float>& score) {
+    score.set_data(cpu_scores(memory.data_ref(), query.data_ref()));
+}
+
+void InnerProductCompute::run_cpu_kernel(const data_type::FlatIndexMemory<float>& memory,
+                                         const data_type::VectorQuery<float>& query,
+                                         data_type::VectorScore<float>& score) {
+    run_test_kernel(memory, query, score);
+}
+
+void InnerProductCompute::run_gpu_kernel(const data_type::FlatIndexMemory<float>& memory,
+                                         const data_type::VectorQuery<float>& query,
+                                         data_type::VectorScore<float>& score) {
+    const auto& rows = memory.data_ref();
+    const auto& q = query.data_ref();
+    const size_t n = rows.size(), d = q.size();
+    std::vector<float> out(n);
+    if (n > 0 && d > 0) {
+        const float* dm = gpu::upload(gpu::kMem, gpu::pack_rows(rows, d, "InnerProductCompute"));
+        const float* dq = gpu::upload(gpu::kQuery, q);
+        float* ds = static_cast<float*>(gpu::scratch(gpu::kOut).get(sizeof(float) * n));
+        gpu::check(hmm_ip_score_f32(dm, (int64_t)n, (int64_t)d, dq, 1, ds, nullptr),
+                   "InnerProductCompute GPU kernel");
+        gpu::download(out, ds);
+    } else {
+        std::fill(out.begin(), out.end(), 0.0f);
+    }
+    score.set_data(out);
+}
+
+void InnerProductCompute::run_fpga_kernel(const data_type::FlatIndexMemory<float>&,
+                                          const data_type::VectorQuery<float>&,
+                                          data_type::VectorScore<float>&) {
+    fpga_stub("InnerProductCompute");
+}
+
+// ------------------------------------------------------------------ TopK
+void TopKRetrieval::run_test_kernel(const data_type::VectorScore<float>& score,
+                                    data_type::TopKIndex& index) {
+    index.set_data(cpu_topk(score.data_ref(), k_));
+}
+
+void TopKRetrieval::run_cpu_kernel(const data_type::VectorScore<float>& score,
+                                   data_type::TopKIndex& index) {
+    run_test_kernel(score, index);
+}
+
+void TopKRetrieval::run_gpu_kernel(const data_type::VectorScore<float>& score,
+                                   data_type::TopKIndex& index) {
+    const auto& s = score.data_ref();
+    const size_t n = s.size(), m = std::min(k_, n);
+    std::vector<int> out(m);
+    if (m > 0) {
+        const float* ds = gpu::upload(gpu::kQuery, s);
+        int32_t* di = static_cast<int32_t*>(gpu::scratch(gpu::kIdx).get(sizeof(int32_t) * m));
+        const size_t ws = hmm_topk_f32_workspace_size((int64_t)n, 1, (int64_t)m);
+        void* w = gpu::scratch(gpu::kWork).get(ws);
+        gpu::check(hmm_topk_f32(ds, (int64_t)n, 1, (int64_t)m, di, nullptr, w, ws, nullptr),
+                   "TopKRetrieval GPU kernel");
+        gpu::download(out, di);
+    }
+    index.set_data(out);
+}
+
+void TopKRetrieval::run_fpga_kernel(const data_type::VectorScore<float>&, data_type::TopKIndex&) {
+    fpga_stub("TopKRetrieval");
+}
+
+// ------------------------------------------------------------- Threshold
+void ThresholdRetrieval::run_test_kernel(const data_type::VectorScore<float>& score,
+                                         data_type::ThresholdBitmapIndex& index) {
+    const auto& s = score.data_ref();
+    index = data_type::ThresholdBitmapIndex(cpu_bitmap(s, threshold_), s.size());
+}
+
+void ThresholdRetrieval::run_cpu_kernel(const data_type::VectorScore<float>& score,
+                                        data_type::ThresholdBitmapIndex& index) {
+    run_test_kernel(score, index);
+}
+
+void ThresholdRetrieval::run_gpu_kernel(const data_type::VectorScore<float>& score,
+                                        data_type::ThresholdBitmapIndex& index) {
+    const auto& s = score.data_ref();
+    const size_t n = s.size();
+    std::vector<unsigned long long> bm((n + 63) / 64);
+    if (n > 0) {
+        const float* ds = gpu::upload(gpu::kQuery, s);
+        auto* db = static_cast<uint64_t*>(gpu::scratch(gpu::kOut).get(sizeof(uint64_t) * bm.size()));
+        gpu::check(hmm_threshold_bitmap_f32(ds, (int64_t)n, 1, threshold_, db, nullptr),
+                   "ThresholdRetrieval GPU kernel");
+        gpu::download(bm, reinterpret_cast<const unsigned long long*>(db));
+    }
+    index = data_type::ThresholdBitmapIndex(bm, n);
+}
+
+void ThresholdRetrieval::run_fpga_kernel(const data_type::VectorScore<float>&,
+                                         data_type::ThresholdBitmapIndex&) {
+    fpga_stub("ThresholdRetrieval");
+}
+
+// ------------------------------------------------- fused inner product top-k
+void InnerProductTopKRetrieval::run_test_kernel(const data_type::FlatIndexMemory<float>& memory,
+                                                const data_type::VectorQuery<float>& query,
+                                                data_type::TopKIndex& index) {
+    index.set_data(cpu_topk(cpu_scores(memory.data_ref(), query.data_ref()), k_));
+}
+
+void InnerProductTopKRetrieval::run_cpu_kernel(const data_type::FlatIndexMemory<float>& memory,
+                                               const data_type::VectorQuery<float>& query,
+                                               data_type::TopKIndex& index) {
+    run_test_kernel(memory, query, index);
+}
+
+void InnerProductTopKRetrieval::run_gpu_kernel(const data_type::FlatIndexMemory<float>& memory,
+                                               const data_type::VectorQuery<float>& query,
+                                               data_type::TopKIndex& index) {
+    const auto& rows = memory.data_ref();
+    const auto& q = query.data_ref();
+    const size_t n = rows.size(), d = q.size(), m = std::min(k_, n);
+    std::vector<int> out(m);
+    if (m > 0 && d > 0) {
+        const float* dm = gpu::upload(gpu::kMem, gpu::pack_rows(rows, d, "InnerProductTopK"));
+        const float* dq = gpu::upload(gpu::kQuery, q);
+        int32_t* di = static_cast<int32_t*>(gpu::scratch(gpu::kIdx).get(sizeof(int32_t) * m));
+        const size_t ws = hmm_ip_topk_f32_workspace_size((int64_t)n, (int64_t)d, 1, (int64_t)m);
+        void* w = gpu::scratch(gpu::kWork).get(ws);
+        gpu::check(hmm_ip_topk_f32(dm, (int64_t)n, (int64_t)d, dq, 1, (int64_t)m, di, nullptr,
+                                   0.0f, nullptr, w, ws, nullptr),
+                   "InnerProductTopKRetrieval GPU kernel");
+        gpu::download(out, di);
+    } else if (m > 0) {
+        std::iota(out.begin(), out.end(), 0);   // all scores 0: the lowest indices
+    }
+    index.set_data(out);
+}
+
+void InnerProductTopKRetrieval::run_fpga_kernel(const data_type::FlatIndexMemory<float>&,
+                                                const data_type::VectorQuery<float>&,
+                                                data_type::TopKIndex&) {
+    fpga_stub("InnerProductTopKRetrieval");
+}
+
+}  // namespace step
+}  // namespace heteromm
