@@ -609,6 +609,143 @@ def run_bm25(args, rank, world, local):
     return res
 
 
+# ---------------------------------------------------------------- config 4
+D_TOKENS, D_HEADS, D_KEYS, D_DIM, D_TOPK = 4096, 64, 131072, 128, 2048
+SEED_DQ, SEED_DK, SEED_DW = 9, 10, 11
+
+
+def fp8_gemm_peak(dev, seconds: float = 1.0) -> float:
+    """Dense FP8 (e4m3) GEMM throughput of cuBLAS on this GPU (torch._scaled_mm,
+    8192^3, back to back for about `seconds`), TFLOP/s: the measured FP8
+    denominator for the tensor roofline."""
+    n = 8192
+    a = torch.randn((n, n), device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn((n, n), device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=dev)
+    torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 0
+    e0.record()
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(10):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        reps += 10
+        torch.cuda.synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    return 2.0 * n ** 3 * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+
+
+def run_dsa(args, rank, world, local):
+    """DSA lightning-indexer prefill: 4,096 query tokens x 64 heads x 128 e4m3
+    against 131,072 e4m3 keys, weights U(0,1), causal (token t at position
+    131,072 - 4,096 + t), top-2,048 keys per token.  Query tokens are split
+    across ranks (no exchange)."""
+    import heteromm_b200 as hmm
+    from heteromm_b200 import _abi
+    dev = torch.device("cuda", local)
+    hmm.load()
+    T = (args.tokens if args.tokens else D_TOKENS) // world
+    t0 = rank * T
+    pos0 = D_KEYS - D_TOKENS + t0
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED_DQ * 1000003 + rank)
+    x = torch.randn((T, D_HEADS, D_DIM), generator=g, device=dev)
+    q = (x * (448.0 / x.abs().max())).to(torch.float8_e4m3fn).view(torch.uint8)
+    g.manual_seed(SEED_DK)
+    y = torch.randn((D_KEYS, D_DIM), generator=g, device=dev)
+    k = (y * (448.0 / y.abs().max())).to(torch.float8_e4m3fn).view(torch.uint8)
+    g.manual_seed(SEED_DW * 1000003 + rank)
+    w = torch.rand((T, D_HEADS), generator=g, device=dev)
+    del x, y
+
+    def step(qq):
+        return hmm.dsa_indexer_fp8(qq, k, w, pos0, D_TOPK)
+
+    for _ in range(args.warmup):
+        step(q)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _abi.profile_read()
+    _abi.profile_enable(True)
+    with ClockSampler(local) as clk:
+        l0 = _abi.kernel_launches()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step(q)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        launches = _abi.kernel_launches() - l0
+    _abi.profile_enable(False)
+    k_total, k_n = _abi.profile_read()
+    ms = e0.elapsed_time(e1) / args.steps
+    kern_ms = k_total / max(k_n, 1)
+    q_host = q.cpu().pin_memory()
+    q_dev = torch.empty_like(q)
+    oi = torch.empty((T, D_TOPK), dtype=torch.int32).pin_memory()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        i, _ = step(q_dev)
+        oi.copy_(i, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, kern_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return None
+    n_tok = T * world
+    vis = sum(min(D_KEYS, pos0 + t + 1) for t in range(T))     # this rank's (token, key) pairs
+    flop = 2.0 * D_HEADS * D_DIM * vis
+    achieved = flop / (kern_ms * 1e-3) / 1e12
+    peak = fp8_gemm_peak(dev)
+    res = {
+        "metric": "DSA indexer query tokens per second", "value": n_tok / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "e4m3",
+        "data": "synthetic (seeded N(0,1) scaled to the e4m3 range, w ~ U(0,1))",
+        "config": {"workload": f"DSA indexer: {n_tok} tokens x {D_HEADS} heads x {D_DIM} e4m3, "
+                               f"{D_KEYS} keys, causal, top-{D_TOPK}",
+                   "parallelism": f"token split x{world}",
+                   "l2": "score rows (T x 131,072 fp32, 2 GB) larger than L2"},
+        "e2e": {"value": n_tok / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": T * D_HEADS * D_DIM,
+                "d2h_bytes_per_step": T * D_TOPK * 4},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "kernel": "dsa_scores_kernel",
+                     "kernel_ms": kern_ms, "kernel_launches_timed": k_n,
+                     "peak_kind": "measured here: cuBLAS e4m3 GEMM 8192^3 (torch._scaled_mm), "
+                                  "1 s back to back"},
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        n_s = 8
+        qs = q[:n_s].cpu().numpy()
+        ks = k.cpu().numpy()
+        ws = w[:n_s].cpu().numpy()
+        t = time.perf_counter()
+        O.dsa_indexer_fp8(qs, ks, ws, pos0, D_TOPK)
+        dt = time.perf_counter() - t
+        res["cpu_baseline"] = {"value": n_s / dt, "unit": "tokens/s",
+                               "cores": os.cpu_count() or 1, "kind": "port",
+                               "sample": f"{n_s} query tokens against all {D_KEYS} keys, exact "
+                                         f"scores + top-{D_TOPK} (oracle restatement, OpenMP "
+                                         f"over tokens), {dt:.2f} s"}
+    return res
+
+
 def traffic_per_launch(kernel: str, units: int):
     """DRAM bytes (read + write) of one launch of `kernel` from its committed
     ncu capture, scaled from the capture's units (rows, sequences) to `units`:
@@ -629,10 +766,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", choices=["flat", "paged", "bm25"], default="flat",
+    ap.add_argument("--config", choices=["flat", "paged", "bm25", "dsa"], default="flat",
                     help="flat: the sharded flat retrieval benchmark (default); "
                          "paged: the paged-KV block-sparse decode step; "
-                         "bm25: BM25 top-10 over a CSR index")
+                         "bm25: BM25 top-10 over a CSR index; dsa: the FP8 DSA indexer")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="dsa: number of query tokens (default 4,096; fewer are for profiler "
+                         "captures only)")
     ap.add_argument("--queries", type=int, default=0,
                     help="bm25: number of queries (default 1,024; fewer are for profiler "
                          "captures only)")
@@ -656,7 +796,8 @@ def main():
         res = run_reference(args, rank, world)
     else:
         rank, world, local = init_dist()
-        runner = {"flat": run_ours, "paged": run_paged, "bm25": run_bm25}[args.config]
+        runner = {"flat": run_ours, "paged": run_paged, "bm25": run_bm25,
+                  "dsa": run_dsa}[args.config]
         res = runner(args, rank, world, local)
         if world > 1:
             torch.distributed.barrier()

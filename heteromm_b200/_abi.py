@@ -62,6 +62,9 @@ SIGNATURES = {
     "hmm_seer_budget_i16": (C.c_int, [_P, _I, _P, _P, _I, _I, _I, _P, _P, _S, _P]),
     "hmm_seer_words_per_query": (_I, [_I, _I]),
     "hmm_seer_threshold_i16": (C.c_int, [_P, _I, _P, _P, _I, _I, _I, _P, _P]),
+    "hmm_dsa_indexer_fp8_workspace_size": (_S, [_I, _I, _I, _I]),
+    "hmm_dsa_indexer_fp8": (C.c_int, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _S,
+                                      _P]),
     "hmm_kernel_launches": (_I, []),
     "hmm_profile_enable": (C.c_int, [C.c_int]),
     "hmm_profile_read": (C.c_int, [_P, _P]),

@@ -1,0 +1,417 @@
+// dsa.cu — DSA lightning indexer on tcgen05 FP8 (e4m3) tensor cores.
+//
+// Reference: indexer_top_ref (kernels/dsa_indexer/indexer_tb.cpp:17-57) with
+// the multi-head FP8 form of _fp8_index
+// (kernels/deepseek_engram/deepseek_v32_dsa_bench.py:77-101):
+//   score[t][j] = sum_h w[t][h] * ReLU(q[t][h] . k[j]),  j visible to t,
+// then the top-k keys per query token.  Query token t sits at position
+// pos0 + t and sees keys j <= pos0 + t.
+//
+// One persistent CTA per SM, 12 warps:
+//   warp 0      TMA producer: the 256 query rows (4 tokens x 64 heads, or
+//               8 x 32, 16 x 16) of a token group into one of two 32 KB
+//               buffers, then 128-key x 128-byte tiles into an 8-stage ring
+//   warp 1      MMA issuer: per tile 4 x tcgen05.mma.kind::f8f6f4 (M = 128
+//               keys, N = 256 query rows, K = 32) into one of two TMEM
+//               accumulators of 256 fp32 columns
+//   warp 2      TMEM allocator
+//   warps 4-19  epilogue, four warpgroups (tile parity x token half):
+//               thread = key; per token, sum_h w * max(x, 0) over the
+//               token's head columns (weights staged in shared memory per
+//               warp and group), causal mask, coalesced fp32 score rows
+// The top-k over each token's score row is the flat top-k kernel
+// (hmm_topk_f32).  Scores are fp32 tensor-core sums of exact e4m3 products;
+// they differ from the exact dot products by the accumulation's rounding.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "heteromm_cuda.h"
+#include "hmm_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace hmm {
+using namespace sm100;
+
+namespace {
+
+constexpr int DK = 128;                 // head dim (bytes per fp8 row)
+constexpr int KT = 128;                 // keys per tile (MMA M, TMEM lanes)
+constexpr int NQ = 256;                 // query rows per group (MMA N)
+constexpr int D_STAGES = 8;
+constexpr int K_TILE_BYTES = KT * DK;   // 16 KB
+constexpr int Q_TILE_BYTES = NQ * DK;   // 32 KB
+constexpr int D_EPI_WG = 4;              // epilogue warpgroups: (tile parity, token half)
+constexpr int D_THREADS = 128 + 128 * D_EPI_WG;
+constexpr uint64_t D_WAIT_NS = 2000000000ull;
+
+struct DsaCtrl {
+    float wsm[4 * D_EPI_WG][NQ / 2];        // each epilogue warp's token weights for its group
+    uint64_t a_full[D_STAGES], a_empty[D_STAGES];
+    uint64_t q_full[2], q_empty[2];
+    uint64_t acc_full[2], acc_empty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr size_t D_SMEM = 1024 + 2 * Q_TILE_BYTES + D_STAGES * K_TILE_BYTES + sizeof(DsaCtrl);
+
+struct DsaArgs {
+    const float* w;       // [T][H]
+    float* scores;        // [T][L]
+    int* status;          // [0] timeout
+    int64_t T, L, pos0;
+    int H, tg;            // heads, tokens per group (NQ / H)
+    int n_groups, key_tiles;
+};
+
+__device__ __forceinline__ int group_tiles(const DsaArgs& a, int g) {
+    const int64_t t_last = min(a.T, (int64_t)(g + 1) * a.tg) - 1;
+    const int64_t vis = a.pos0 + t_last + 1;            // keys visible to the group's last token
+    if (vis <= 0) return 0;
+    return (int)min((int64_t)a.key_tiles, (vis + KT - 1) / KT);
+}
+
+__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    const bool ok = mbar_wait_bounded(bar, parity, abort, D_WAIT_NS);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void dsa_abort(DsaCtrl* c, int* status) {
+    atomicExch(&c->abort, 1);
+    atomicExch(&status[0], 1);
+}
+
+__global__ void __launch_bounds__(D_THREADS, 1)
+dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
+                  const DsaArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    unsigned char* Qs = smem;                                  // 2 x 32 KB
+    unsigned char* Ks = Qs + 2 * Q_TILE_BYTES;                 // D_STAGES x 16 KB
+    DsaCtrl* ctl = reinterpret_cast<DsaCtrl*>(Ks + D_STAGES * K_TILE_BYTES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x;
+    volatile int* abort = &ctl->abort;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < D_STAGES; ++s) {
+            mbar_init(&ctl->a_full[s], 1);
+            mbar_init(&ctl->a_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->q_full[b], 1);
+            mbar_init(&ctl->q_empty[b], 1);
+            mbar_init(&ctl->acc_full[b], 1);
+            mbar_init(&ctl->acc_empty[b], 8);   // two warpgroups per accumulator
+        }
+        ctl->abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(&ctl->tmem_base, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+
+    if (warp == 0) {
+        // -------------------------------------------------------- producer
+        if (lane == 0) {
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmQ);
+        }
+        int i = 0, k = 0, issued = 0, qk = 0;   // k counts the groups that load queries
+        bool ok = true;
+        for (int g = blockIdx.x; ok && g < a.n_groups; g += G) {
+            const int nt = group_tiles(a, g);
+            if (nt == 0) continue;
+            const int qb = k & 1;
+            if (!wait_all(&ctl->q_empty[qb], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+            if (lane == 0) {
+                mbar_expect_tx(&ctl->q_full[qb], Q_TILE_BYTES);
+                tma_load_2d(Qs + qb * Q_TILE_BYTES, &tmQ, &ctl->q_full[qb], 0, g * NQ);
+            }
+            qk = ++k;
+            for (int t = 0; t < nt; ++t, ++i) {
+                const int s = i % D_STAGES;
+                if (!wait_all(&ctl->a_empty[s], ((i / D_STAGES) & 1) ^ 1, abort)) { ok = false; break; }
+                if (lane == 0) {
+                    mbar_expect_tx(&ctl->a_full[s], K_TILE_BYTES);
+                    tma_load_2d(Ks + s * K_TILE_BYTES, &tmK, &ctl->a_full[s], 0, t * KT);
+                }
+                __syncwarp();
+                issued = i + 1;
+            }
+        }
+        if (!ok) {
+            if (lane == 0) dsa_abort(ctl, a.status);
+            // drain: the copies in flight must land before the CTA exits
+            for (int j = max(0, issued - D_STAGES); j < issued; ++j)
+                mbar_wait_bounded(&ctl->a_full[j % D_STAGES], (j / D_STAGES) & 1, abort, 100000000ull);
+            for (int j = max(0, qk - 2); j < qk; ++j)
+                mbar_wait_bounded(&ctl->q_full[j & 1], (j >> 1) & 1, abort, 100000000ull);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------- MMA
+        const uint32_t idesc = idesc_f8(KT, NQ, 0, 0);
+        int i = 0, k = 0, last = -1;   // k counts the groups that use queries
+        bool ok = true;
+        for (int g = blockIdx.x; ok && g < a.n_groups; g += G) {
+            const int nt = group_tiles(a, g);
+            if (nt == 0) continue;
+            const int qb = k & 1;
+            if (!wait_all(&ctl->q_full[qb], (k >> 1) & 1, abort)) { ok = false; break; }
+            ++k;
+            for (int t = 0; t < nt; ++t, ++i) {
+                const int s = i % D_STAGES, b = i & 1;
+                if (!wait_all(&ctl->a_full[s], (i / D_STAGES) & 1, abort) ||
+                    !wait_all(&ctl->acc_empty[b], ((i >> 1) & 1) ^ 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t ka = smem_u32(Ks + s * K_TILE_BYTES);
+                    const uint32_t qa = smem_u32(Qs + qb * Q_TILE_BYTES);
+                    const uint32_t d = tmem + (uint32_t)(b * NQ);
+#pragma unroll
+                    for (int ks = 0; ks < DK / 32; ++ks)
+                        mma_f8(d, desc_k_sw128(ka + ks * 32), desc_k_sw128(qa + ks * 32), idesc,
+                               ks != 0);
+                    mma_commit(&ctl->acc_full[b]);
+                    mma_commit(&ctl->a_empty[s]);
+                    if (t == nt - 1) mma_commit(&ctl->q_empty[qb]);
+                }
+                __syncwarp();
+                last = i;
+            }
+        }
+        if (!ok) {
+            if (lane == 0) dsa_abort(ctl, a.status);
+            if (last >= 0)
+                mbar_wait_bounded(&ctl->acc_full[last & 1], (last >> 1) & 1, abort, 100000000ull);
+        }
+    } else if (warp >= 4) {
+        // -------------------------------------------------------- epilogue
+        const int ew = warp - 4;               // 0..15
+        const int wg = ew >> 2;                // 0..3
+        const int par = wg & 1;                // tiles with i % 2 == par
+        const int half = wg >> 1;              // tokens [half * tg / 2, (half + 1) * tg / 2)
+        const int sub = warp & 3;              // TMEM lanes 32*sub .. +31
+        const int r = sub * 32 + lane;         // key within the tile
+        const int tg2 = a.tg >> 1;
+        float* wsm = ctl->wsm[ew];   // per warp: no cross-warp barrier on any path
+        int i = 0, g_loaded = -1;
+        bool ok = true;
+        for (int g = blockIdx.x; ok && g < a.n_groups; g += G) {
+            const int nt = group_tiles(a, g);
+            for (int t = 0; t < nt; ++t, ++i) {
+                if ((i & 1) != par) continue;
+                if (g_loaded != g) {
+                    // this warp's tokens' weights for group g
+                    __syncwarp();
+                    const int n = tg2 * a.H;
+                    const int64_t base = ((int64_t)g * a.tg + half * tg2) * a.H;
+                    for (int e = lane; e < n; e += 32)
+                        wsm[e] = base + e < a.T * a.H ? a.w[base + e] : 0.0f;
+                    __syncwarp();
+                    g_loaded = g;
+                }
+                const int b = i & 1;
+                if (!wait_all(&ctl->acc_full[b], (i >> 1) & 1, abort)) { ok = false; break; }
+                tc_fence_after();
+                const int64_t j = (int64_t)t * KT + r;
+                const uint32_t tb = tmem + (uint32_t)(b * NQ) + ((uint32_t)(sub * 32) << 16);
+                for (int tl = 0; tl < tg2; ++tl) {
+                    const int tcol = (half * tg2 + tl) * a.H;
+                    const int64_t tok = (int64_t)g * a.tg + half * tg2 + tl;
+                    const float* wr = wsm + tl * a.H;
+                    float s = 0.0f;
+                    for (int c0 = 0; c0 < a.H; c0 += 64) {
+                        uint32_t v[2][32];
+                        tmem_ld_x32(tb + (uint32_t)(tcol + c0), v[0]);
+                        if (c0 + 32 < a.H) tmem_ld_x32(tb + (uint32_t)(tcol + c0 + 32), v[1]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh) {
+                            if (c0 + hh * 32 >= a.H) break;
+#pragma unroll
+                            for (int h4 = 0; h4 < 32; h4 += 4) {
+                                if (c0 + hh * 32 + h4 >= a.H) break;   // H = 16: half a load
+                                const float4 w4 =
+                                    *reinterpret_cast<const float4*>(wr + c0 + hh * 32 + h4);
+                                s = fmaf(w4.x, fmaxf(__uint_as_float(v[hh][h4 + 0]), 0.0f), s);
+                                s = fmaf(w4.y, fmaxf(__uint_as_float(v[hh][h4 + 1]), 0.0f), s);
+                                s = fmaf(w4.z, fmaxf(__uint_as_float(v[hh][h4 + 2]), 0.0f), s);
+                                s = fmaf(w4.w, fmaxf(__uint_as_float(v[hh][h4 + 3]), 0.0f), s);
+                            }
+                        }
+                    }
+                    if (tok < a.T && j < a.L)
+                        a.scores[tok * a.L + j] = j <= a.pos0 + tok ? s : -INFINITY;
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->acc_empty[b]);
+            }
+        }
+        if (!ok && lane == 0) dsa_abort(ctl, a.status);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc(tmem, 512);
+}
+
+// Positions of each token's score row that no tile of its group covers.
+__global__ void dsa_tail_kernel(float* __restrict__ scores, int64_t T, int64_t L, int64_t pos0,
+                                int tg, int key_tiles) {
+    const int64_t t = blockIdx.y;
+    const int g = (int)(t / tg);
+    const int64_t t_last = min(T, (int64_t)(g + 1) * tg) - 1;
+    const int64_t vis = pos0 + t_last + 1;
+    const int64_t covered = vis <= 0 ? 0 : min(L, min((int64_t)key_tiles, (vis + KT - 1) / KT) * KT);
+    for (int64_t j = covered + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < L;
+         j += (int64_t)gridDim.x * blockDim.x)
+        scores[t * L + j] = -INFINITY;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn_dsa() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Row-major [rows][128] bytes as a 2-D uint8 tensor map, {128, box_rows}
+// boxes, 128-byte swizzle (one swizzle row per fp8 row).
+hmm_status_t make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int box_rows) {
+    auto fn = encode_fn_dsa();
+    if (!fn) return set_error(HMM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)DK, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)DK};
+    cuuint32_t box[2] = {(cuuint32_t)DK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(HMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return HMM_OK;
+}
+
+// Selections of keys nobody can see (score -inf: fewer visible keys than k)
+// become -1, as the reference returns only min(k, visible) indices.
+__global__ void dsa_pad_kernel(int32_t* __restrict__ idx, float* __restrict__ sc, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n && sc[i] == -INFINITY) idx[i] = -1;
+}
+
+size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace hmm
+
+using namespace hmm;
+
+extern "C" size_t hmm_dsa_indexer_fp8_workspace_size(int64_t T, int64_t H, int64_t L,
+                                                     int64_t topk) {
+    if (T < 0 || H < 1 || L < 0 || topk < 1) return 0;
+    return up256(sizeof(float) * (size_t)T * (size_t)L) + 256 +
+           up256(sizeof(float) * (size_t)T * (size_t)topk) +
+           hmm_topk_f32_workspace_size(L, T, topk);
+}
+
+extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* keys,
+                                            const float* w, int64_t T, int64_t H, int64_t L,
+                                            int64_t D, int64_t pos0, int64_t topk,
+                                            int32_t* out_idx, float* out_scores,
+                                            float* all_scores, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+    HMM_REQUIRE(D == DK, "head dim must be %d, got %lld", DK, (long long)D);
+    HMM_REQUIRE(H == 16 || H == 32 || H == 64, "heads must be 16, 32 or 64, got %lld",
+                (long long)H);
+    HMM_REQUIRE(T >= 0 && T * H < (int64_t(1) << 31), "T out of range");
+    HMM_REQUIRE(L >= 0 && L < (int64_t(1) << 31), "L out of range");
+    HMM_REQUIRE(topk >= 1 && topk <= 4096, "topk must be in [1, 4096]");
+    HMM_REQUIRE(pos0 >= -1, "pos0 must be >= -1");
+    if (T == 0) return HMM_OK;
+    HMM_REQUIRE(q && w && out_idx && (L == 0 || keys), "null pointer");
+    HMM_REQUIRE((reinterpret_cast<uintptr_t>(q) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(keys) % 16) == 0 &&
+                    (reinterpret_cast<uintptr_t>(w) % 16) == 0,
+                "q, keys and w must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    const size_t sc_bytes = all_scores ? 0 : up256(sizeof(float) * (size_t)T * (size_t)L);
+    const size_t sel_bytes = up256(sizeof(float) * (size_t)T * (size_t)topk);
+    const size_t tk_bytes = hmm_topk_f32_workspace_size(L, T, topk);
+    const size_t need = sc_bytes + 256 + sel_bytes + tk_bytes;
+    if (!ws || workspace_bytes < need)
+        return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", workspace_bytes, need);
+    float* scores = all_scores ? all_scores : reinterpret_cast<float*>(ws);
+    int* status = reinterpret_cast<int*>(ws + sc_bytes);
+    float* sel_sc = out_scores ? out_scores : reinterpret_cast<float*>(ws + sc_bytes + 256);
+    void* tk_ws = ws + sc_bytes + 256 + sel_bytes;
+
+    if (L > 0) {
+        HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
+        CUtensorMap tmK, tmQ;
+        hmm_status_t s = make_tmap_u8(&tmK, keys, L, KT);
+        if (s != HMM_OK) return s;
+        s = make_tmap_u8(&tmQ, q, T * H, NQ);
+        if (s != HMM_OK) return s;
+        DsaArgs a;
+        a.w = w;
+        a.scores = scores;
+        a.status = status;
+        a.T = T;
+        a.L = L;
+        a.pos0 = pos0;
+        a.H = (int)H;
+        a.tg = NQ / (int)H;
+        a.n_groups = (int)((T + a.tg - 1) / a.tg);
+        a.key_tiles = (int)((L + KT - 1) / KT);
+        HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_scores_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)D_SMEM));
+        const int grid = std::max(1, std::min(device_sm_count(), a.n_groups));
+        const ProfileMark pm = profile_begin(st);
+        dsa_scores_kernel<<<grid, D_THREADS, D_SMEM, st>>>(tmK, tmQ, a);
+        s = check_launch("dsa_scores_kernel");
+        profile_end(pm, st);
+        if (s != HMM_OK) return s;
+        dsa_tail_kernel<<<dim3(16, (unsigned)T), 256, 0, st>>>(scores, T, L, pos0, a.tg,
+                                                               a.key_tiles);
+        s = check_launch("dsa_tail_kernel");
+        if (s != HMM_OK) return s;
+    }
+    hmm_status_t s = hmm_topk_f32(scores, L, T, topk, out_idx, sel_sc, tk_ws, tk_bytes, st);
+    if (s != HMM_OK) return s;
+    const int64_t n_sel = T * topk;
+    dsa_pad_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(out_idx, sel_sc, n_sel);
+    s = check_launch("dsa_pad_kernel");
+    if (s != HMM_OK) return s;
+    if (L > 0) {
+        int h = 0;
+        HMM_CUDA_TRY(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, st));
+        HMM_CUDA_TRY(cudaStreamSynchronize(st));
+        if (h)
+            return set_error(HMM_ERR_TIMEOUT,
+                             "dsa_scores_kernel: a bounded pipeline wait gave up; outputs invalid");
+    }
+    return HMM_OK;
+}

@@ -327,6 +327,31 @@ hmm_status_t hmm_seer_threshold_i16(const int16_t* past, int64_t L, const int16_
                                     const int16_t* new_keys, int64_t n_queries, int64_t D,
                                     int64_t threshold, uint64_t* out_bitmap, void* stream);
 
+/* -------------------------------------------------------- DSA indexer
+ * DSA lightning indexer (reference kernels/dsa_indexer/indexer_tb.cpp:17-57,
+ * multi-head FP8 form of kernels/deepseek_engram/deepseek_v32_dsa_bench.py:
+ * 77-101) on FP8 tensor cores: for query token t (position pos0 + t) and
+ * key j <= pos0 + t, score = sum_h w[t][h] * ReLU(q[t][h] . k[j]), then the
+ * topk best keys per token (best first, ties to the lowest key, -1 past the
+ * number of visible keys).
+ *   q [T][H][128] e4m3, keys [L][128] e4m3, w [T][H] fp32 (16-byte aligned),
+ *   H in {16, 32, 64}, topk <= 4096, pos0 >= -1.
+ *   out_idx [T][topk] int32; out_scores [T][topk] fp32 or NULL;
+ *   all_scores [T][L] fp32 or NULL: every score (-inf where not visible),
+ *   kept in the caller's buffer instead of the workspace.
+ * The q . k products are exact (e4m3 x e4m3 fits fp32); their sum is the
+ * tensor core's fp32 accumulation and the head sum is fp32 FMA, so scores
+ * match the exact value to within the accumulation rounding, and selections
+ * differ from the exact ranking only among keys whose exact scores are that
+ * close to the k-th.  Waits for `stream`; HMM_ERR_TIMEOUT if a bounded
+ * device wait gave up. */
+size_t hmm_dsa_indexer_fp8_workspace_size(int64_t T, int64_t H, int64_t L, int64_t topk);
+hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* keys, const float* w,
+                                 int64_t T, int64_t H, int64_t L, int64_t D, int64_t pos0,
+                                 int64_t topk, int32_t* out_idx, float* out_scores,
+                                 float* all_scores, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
 /* ------------------------------------------------------ instrumentation
  * No reference counterpart (the reference steps are timed by their callers).
  * hmm_kernel_launches: kernels this library has launched since it was loaded.

@@ -468,6 +468,17 @@ void orc_dsa_indexer_fp8(const uint8_t* q, int64_t T, int64_t H, int64_t D,
     }
 }
 
+void orc_dsa_scores_fp8(const uint8_t* q, int64_t T, int64_t H, int64_t D, const uint8_t* keys,
+                        int64_t L, const float* w, int64_t pos0, float* out) {
+    int64_t t;
+#pragma omp parallel for schedule(dynamic)
+    for (t = 0; t < T; ++t)
+        for (int64_t j = 0; j < L; ++j)
+            out[t * L + j] = j <= pos0 + t
+                                 ? orc_dsa_score_fp8(q + t * H * D, H, D, keys + j * D, w + t * H)
+                                 : -INFINITY;
+}
+
 /* --------------------------------------------------------- a-9 / a-10 */
 
 /* Key visible at position pos to query q (indexer_lserve_tb.cpp:36-45,

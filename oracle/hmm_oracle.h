@@ -117,6 +117,11 @@ int32_t orc_e4m3_scaled(uint8_t v);
 float orc_dsa_score_fp8(const uint8_t* q_t, int64_t H, int64_t D, const uint8_t* key,
                         const float* w_t);
 
+/* Every exact score of the FP8 indexer: out [T][L], -inf where key j is not
+ * visible to token t (j > pos0 + t). */
+void orc_dsa_scores_fp8(const uint8_t* q, int64_t T, int64_t H, int64_t D, const uint8_t* keys,
+                        int64_t L, const float* w, int64_t pos0, float* out);
+
 /* a-9  kernels/lserve/indexer_lserve_tb.cpp:20-90.  Returns per query the
  * top-k 16-token blocks.  out [nq][topk] (-1 padded). */
 void orc_lserve_topk_i16(const int16_t* past, int64_t L, const int16_t* queries,

@@ -231,6 +231,17 @@ def e4m3_to_f32(v: np.ndarray) -> np.ndarray:
     return table[v].astype(np.float32)
 
 
+def dsa_scores_fp8(q, keys, w, pos0):
+    """Every exact FP8 indexer score [T, L] (-inf where not visible)."""
+    q = _c(q, np.uint8); keys = _c(keys, np.uint8); w = _c(w, np.float32)
+    T, H, D = q.shape
+    L = keys.shape[0]
+    out = np.empty((T, L), np.float32)
+    lib().orc_dsa_scores_fp8(_p(q), _I(T), _I(H), _I(D), _p(keys), _I(L), _p(w), _I(pos0),
+                             _p(out))
+    return out
+
+
 def dsa_indexer_fp8(q, keys, w, pos0, topk):
     q = _c(q, np.uint8); keys = _c(keys, np.uint8); w = _c(w, np.float32)
     T, H, D = q.shape
