@@ -150,27 +150,22 @@ def run_ours(args, rank, world, local):
     import heteromm_b200 as hmm
     from heteromm_b200 import _abi
 
+    from heteromm_b200 import shard as sharding
     dev = torch.device("cuda", local)
     hmm.load()
-    per = N_ROWS // world
-    r0 = rank * per
+    r0, r1 = sharding.shard_range(N_ROWS, rank, world)
+    per = r1 - r0
     shard = gen_rows(r0, per, dev)
     qry = gen_queries(dev)
     shard_i16 = shard.view(torch.int16)
     qry_i16 = qry.view(torch.int16)
     torch.cuda.synchronize()
 
-    gathered_s = torch.empty((world, N_QUERIES, TOP_K), dtype=torch.float32, device=dev)
-    gathered_i = torch.empty((world, N_QUERIES, TOP_K), dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream()
 
     def step(q_i16):
-        idx, sc = hmm.ip_topk_bf16(shard_i16, q_i16, TOP_K, r0)
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(gathered_s, sc)
-            torch.distributed.all_gather_into_tensor(gathered_i, idx)
-            sc, idx = hmm.shard_merge_topk(gathered_s, gathered_i, TOP_K)
-        return idx, sc
+        # local tensor-core top-k of this rank's rows, NCCL all-gather, merge
+        return sharding.sharded_ip_topk_bf16(shard_i16, q_i16, TOP_K, r0)
 
     def barrier():
         if world > 1:
