@@ -71,6 +71,8 @@ constexpr int TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
 constexpr int SEED_ROWS = 8192;
+constexpr int64_t PASS1_ROWS = int64_t(1) << 20;      // first pass of a large shard
+constexpr int64_t PASS1_MIN_ROWS = int64_t(1) << 22;  // shards from 4Mi rows on use two passes
 constexpr int POOL_CAP = 8192;
 constexpr int KMAX_TC = 128;
 constexpr int RAISE_STEP = 256;                // appends between threshold raises
@@ -656,25 +658,50 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         CUtensorMap tmB;
         s = make_tmap_bf16(&tmB, qp, nqp_pass, TC_NMAX);
         if (s != HMM_OK) return s;
-        TcArgs a;
-        a.n_rows = n;
-        a.row_begin = seed;
-        a.n_tiles = (int)((n - seed + TC_M - 1) / TC_M);
-        a.nq = nqp_pass;
-        a.k = (int)k;
-        a.pool_cap = POOL_CAP;
-        a.wm0 = std::max(256, next_pow2(2 * (int)k));
-        a.qry = qp;
-        a.mem = mem;
-        a.tau_global = tau;
-        a.pool = pool;
-        a.pool_cnt = cnt;
-        a.status = status;
-        const int grid = std::max(1, std::min(sms, a.n_tiles));
-        const ProfileMark pm = profile_begin(st);
-        tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
-        s = check_launch("tc_score_select_kernel");
-        profile_end(pm, st);
+        // One tensor-core pass over rows [r0, r1), appending to the pools.
+        auto run_pass = [&](int64_t r0, int64_t r1) -> hmm_status_t {
+            TcArgs a;
+            a.n_rows = r1;
+            a.row_begin = r0;
+            a.n_tiles = (int)((r1 - r0 + TC_M - 1) / TC_M);
+            a.nq = nqp_pass;
+            a.k = (int)k;
+            a.pool_cap = POOL_CAP;
+            a.wm0 = std::max(256, next_pow2(2 * (int)k));
+            a.qry = qp;
+            a.mem = mem;
+            a.tau_global = tau;
+            a.pool = pool;
+            a.pool_cnt = cnt;
+            a.status = status;
+            const int grid = std::max(1, std::min(sms, a.n_tiles));
+            const ProfileMark pm = profile_begin(st);
+            tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
+            const hmm_status_t ls = check_launch("tc_score_select_kernel");
+            profile_end(pm, st);
+            return ls;
+        };
+        // Large shards go in two passes.  The exact top-k of the first
+        // PASS1_ROWS rows (a pass seeded from the first SEED_ROWS) reseeds the
+        // pools for the rest: the k-th best of any subset of rows is a lower
+        // bound on the final k-th best, and a higher starting threshold means
+        // far fewer candidates to rescore and fewer threshold raises over the
+        // remaining rows.  The status word is kept across the passes, so a
+        // full pool in the first pass still sends the call to the exact path.
+        int64_t split = seed;
+        if (n >= PASS1_MIN_ROWS) {
+            split = PASS1_ROWS;
+            s = run_pass(seed, split);
+            if (s != HMM_OK) return s;
+            s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, 0, seed_idx, seed_sc, st);
+            if (s != HMM_OK) return s;
+            HMM_CUDA_TRY(cudaMemsetAsync(pool, 0, sizeof(uint64_t) * nqp_pass * POOL_CAP, st));
+            seed_pool_kernel<<<nqp_pass, 128, 0, st>>>(seed_idx, seed_sc, nqp_pass, (int)k, pool,
+                                                        POOL_CAP, cnt, tau);
+            s = check_launch("seed_pool_kernel");
+            if (s != HMM_OK) return s;
+        }
+        s = run_pass(split, n);
         if (s != HMM_OK) return s;
 
         s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, row_offset,

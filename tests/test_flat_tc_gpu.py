@@ -112,3 +112,15 @@ def test_tc_normal_call_launch_count(cuda):
     l0 = _abi.kernel_launches()
     run(cuda, mem, qry, 10)
     assert _abi.kernel_launches() - l0 == 5
+
+
+def test_tc_two_pass_shard(cuda):
+    """A shard large enough for the two-pass flow (the exact top-k of the first
+    1Mi rows reseeds the pools for the rest)."""
+    n, nq, k = (1 << 22) + 12345, 8, 100
+    mem = gen.bf16_bits(gen.normal_f32(95, (n, 128)))
+    qry = gen.bf16_bits(gen.normal_f32(96, (nq, 128)))
+    idx, sc = run(cuda, mem, qry, k, 777)
+    oidx, osc = O.ip_topk_bf16(mem, qry, k, 777)
+    assert np.array_equal(idx, oidx)
+    assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
