@@ -71,11 +71,21 @@ constexpr int TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
 constexpr int SEED_ROWS = 8192;
-constexpr int64_t PASS1_ROWS = int64_t(1) << 20;      // first pass of a large shard
-constexpr int64_t PASS1_MIN_ROWS = int64_t(1) << 22;  // shards from 4Mi rows on use two passes
+#ifndef HMM_PASS_GROWTH
+#define HMM_PASS_GROWTH 128
+#endif
+constexpr int64_t PASS_GROWTH = HMM_PASS_GROWTH;      // row-prefix growth between passes
+constexpr int64_t PASS_MIN_ROWS = int64_t(1) << 22;   // shards from 4Mi rows on use passes
 constexpr int POOL_CAP = 8192;
 constexpr int KMAX_TC = 128;
-constexpr int RAISE_STEP = 256;                // appends between threshold raises
+#ifndef HMM_RAISE_STEP
+#define HMM_RAISE_STEP 128
+#endif
+#ifndef HMM_RAISE_WINDOW
+#define HMM_RAISE_WINDOW 512
+#endif
+constexpr int RAISE_STEP = HMM_RAISE_STEP;      // appends between threshold raises
+constexpr int RAISE_WINDOW = HMM_RAISE_WINDOW;  // newest pool entries a raise selects over
 constexpr int MR_RING = 8;                     // tiles of row bounds in flight (>= STAGES + 2)
 
 struct __align__(8) Ctrl {
@@ -255,7 +265,8 @@ __device__ __noinline__ void flush_queue(Ctrl* ctl, unsigned char* FB, int ew, i
             const int W = __shfl_sync(0xffffffffu, raise, src);
             const int qq = __shfl_sync(0xffffffffu, q, src);
             const uint64_t T =
-                warp_select_threshold(a.pool + (int64_t)qq * a.pool_cap, W, a.k, ctl->hist[ew]);
+                warp_select_threshold(a.pool + (int64_t)qq * a.pool_cap + (W > RAISE_WINDOW ? W - RAISE_WINDOW : 0),
+                                      W > RAISE_WINDOW ? RAISE_WINDOW : W, a.k, ctl->hist[ew]);
             if (lane == 0) atomicAdd(&a.status[3], 1);
             if (lane == 0 && T != 0ull) {
                 atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
@@ -681,25 +692,30 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
             profile_end(pm, st);
             return ls;
         };
-        // Large shards go in two passes.  The exact top-k of the first
-        // PASS1_ROWS rows (a pass seeded from the first SEED_ROWS) reseeds the
-        // pools for the rest: the k-th best of any subset of rows is a lower
-        // bound on the final k-th best, and a higher starting threshold means
-        // far fewer candidates to rescore and fewer threshold raises over the
-        // remaining rows.  The status word is kept across the passes, so a
-        // full pool in the first pass still sends the call to the exact path.
+        // Large shards go in several passes over geometrically growing row
+        // prefixes.  The exact top-k of each prefix reseeds the pools for the
+        // next pass: the k-th best of any subset of rows is a lower bound on
+        // the final k-th best, and each pass starts from the exact threshold
+        // of everything before it, so far fewer candidates reach rescoring
+        // than when thousands of tiles run against a threshold still catching
+        // up.  The status word is kept across the passes, so a full pool in
+        // any pass still sends the call to the exact path.
         int64_t split = seed;
-        if (n >= PASS1_MIN_ROWS) {
-            split = PASS1_ROWS;
-            s = run_pass(seed, split);
-            if (s != HMM_OK) return s;
-            s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, 0, seed_idx, seed_sc, st);
-            if (s != HMM_OK) return s;
-            HMM_CUDA_TRY(cudaMemsetAsync(pool, 0, sizeof(uint64_t) * nqp_pass * POOL_CAP, st));
-            seed_pool_kernel<<<nqp_pass, 128, 0, st>>>(seed_idx, seed_sc, nqp_pass, (int)k, pool,
-                                                        POOL_CAP, cnt, tau);
-            s = check_launch("seed_pool_kernel");
-            if (s != HMM_OK) return s;
+        if (n >= PASS_MIN_ROWS) {
+            while (split * PASS_GROWTH <= n / 16) {
+                const int64_t next = split * PASS_GROWTH;
+                s = run_pass(split, next);
+                if (s != HMM_OK) return s;
+                s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, 0, seed_idx, seed_sc,
+                                      st);
+                if (s != HMM_OK) return s;
+                HMM_CUDA_TRY(cudaMemsetAsync(pool, 0, sizeof(uint64_t) * nqp_pass * POOL_CAP, st));
+                seed_pool_kernel<<<nqp_pass, 128, 0, st>>>(seed_idx, seed_sc, nqp_pass, (int)k,
+                                                            pool, POOL_CAP, cnt, tau);
+                s = check_launch("seed_pool_kernel");
+                if (s != HMM_OK) return s;
+                split = next;
+            }
         }
         s = run_pass(split, n);
         if (s != HMM_OK) return s;
