@@ -702,7 +702,7 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         // any pass still sends the call to the exact path.
         int64_t split = seed;
         if (n >= PASS_MIN_ROWS) {
-            while (split * PASS_GROWTH <= n / 16) {
+            while (split * PASS_GROWTH <= n / 4) {
                 const int64_t next = split * PASS_GROWTH;
                 s = run_pass(split, next);
                 if (s != HMM_OK) return s;
