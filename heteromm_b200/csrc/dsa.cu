@@ -61,7 +61,7 @@ constexpr size_t D_SMEM = 1024 + 2 * Q_TILE_BYTES + D_STAGES * K_TILE_BYTES + si
 struct DsaArgs {
     const float* w;       // [T][H]
     float* scores;        // [T][L]
-    int* status;          // [0] timeout
+    int* status;          // [0] timeout, [1] a row the sampled top-k could not select
     int64_t T, L, pos0;
     int H, tg;            // heads, tokens per group (NQ / H)
     int n_groups, key_tiles;
@@ -313,6 +313,99 @@ hmm_status_t make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int bo
     return HMM_OK;
 }
 
+// Exact top-k of each score row for long rows and large k (one block of 256
+// threads per row).  A strided sample of RT_SAMPLE scores gives a lower
+// threshold expected to pass ~2k scores; one read of the row gathers every
+// (score key, ~index) composite at or above it into shared memory; a radix
+// select finds the k-th composite among them and the k best are sorted.  If
+// fewer than k scores pass or more than RT_CAP do, the row is flagged
+// (status bit 1) and the caller reruns the general top-k.  The result equals
+// hmm_topk_f32's: best first, ties to the lowest index.
+constexpr int RT_THREADS = 256;
+constexpr int RT_SAMPLE = 4096;
+constexpr int RT_CAP = 8192;
+constexpr int RT_KMAX = 4096;
+constexpr size_t RT_SMEM = sizeof(uint64_t) * (RT_CAP + RT_KMAX);
+
+__global__ void __launch_bounds__(RT_THREADS) dsa_row_topk_kernel(const float* __restrict__ scores,
+                                                                  int64_t L, int k,
+                                                                  int32_t* __restrict__ out_idx,
+                                                                  float* __restrict__ out_sc,
+                                                                  int* status) {
+    extern __shared__ uint64_t rsm[];
+    uint64_t* cand = rsm;              // RT_CAP
+    uint64_t* best = rsm + RT_CAP;     // RT_KMAX: the sample, then the k best
+    __shared__ unsigned sm[300];
+    __shared__ int cnt;
+    const int64_t t = blockIdx.x;
+    const float* row = scores + t * L;
+
+    for (int i = threadIdx.x; i < RT_SAMPLE; i += RT_THREADS) {
+        const int64_t j = (int64_t)i * L / RT_SAMPLE;
+        best[i] = make_cand(f32_key(row[j]), (uint32_t)j);
+    }
+    if (threadIdx.x == 0) cnt = 0;
+    __syncthreads();
+    const int64_t r = min((int64_t)RT_SAMPLE - 1, 2 * (int64_t)k * RT_SAMPLE / L + 32);
+    const uint64_t ts = block_select_threshold(best, RT_SAMPLE, r + 1, sm);
+    const uint32_t tlo = (uint32_t)(ts >> 32);
+    __syncthreads();
+
+    auto take = [&](float v, int64_t j) {
+        const uint32_t key = f32_key(v);
+        if (key >= tlo) {
+            const int pos = atomicAdd(&cnt, 1);
+            if (pos < RT_CAP) cand[pos] = make_cand(key, (uint32_t)j);
+        }
+    };
+    if ((L & 3) == 0) {
+        const float4* row4 = reinterpret_cast<const float4*>(row);
+        const int64_t L4 = L >> 2;
+        for (int64_t b = threadIdx.x; b < L4; b += RT_THREADS * 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j4 = b + (int64_t)u * RT_THREADS;
+                v[u] = j4 < L4 ? __ldg(row4 + j4)
+                               : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j4 = b + (int64_t)u * RT_THREADS;
+                if (j4 < L4) {
+                    take(v[u].x, 4 * j4 + 0);
+                    take(v[u].y, 4 * j4 + 1);
+                    take(v[u].z, 4 * j4 + 2);
+                    take(v[u].w, 4 * j4 + 3);
+                }
+            }
+        }
+    } else {
+        for (int64_t j = threadIdx.x; j < L; j += RT_THREADS) take(__ldg(row + j), j);
+    }
+    __syncthreads();
+    const int C = cnt;
+    if (C < k || C > RT_CAP) {
+        if (threadIdx.x == 0) atomicOr(&status[1], 1);
+        return;
+    }
+    const uint64_t T = block_select_threshold(cand, C, k, sm);   // exactly k composites >= T
+    __syncthreads();
+    const int kp = next_pow2(k);
+    for (int i = threadIdx.x; i < kp; i += RT_THREADS) best[i] = 0ull;
+    if (threadIdx.x == 0) cnt = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < C; i += RT_THREADS)
+        if (cand[i] >= T) best[atomicAdd(&cnt, 1)] = cand[i];
+    __syncthreads();
+    block_bitonic_sort_desc(best, kp);
+    for (int i = threadIdx.x; i < k; i += RT_THREADS) {
+        const uint64_t c = best[i];
+        out_idx[t * k + i] = c ? (int32_t)cand_row(c) : -1;
+        out_sc[t * k + i] = c ? cand_score(c) : -INFINITY;
+    }
+}
+
 // Selections of keys nobody can see (score -inf: fewer visible keys than k)
 // become -1, as the reference returns only min(k, visible) indices.
 __global__ void dsa_pad_kernel(int32_t* __restrict__ idx, float* __restrict__ sc, int64_t n) {
@@ -368,7 +461,7 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
     void* tk_ws = ws + sc_bytes + 256 + sel_bytes;
 
     if (L > 0) {
-        HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
+        HMM_CUDA_TRY(cudaMemsetAsync(status, 0, 2 * sizeof(int), st));
         CUtensorMap tmK, tmQ;
         hmm_status_t s = make_tmap_u8(&tmK, keys, L, KT);
         if (s != HMM_OK) return s;
@@ -399,19 +492,31 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
         s = check_launch("dsa_tail_kernel");
         if (s != HMM_OK) return s;
     }
-    hmm_status_t s = hmm_topk_f32(scores, L, T, topk, out_idx, sel_sc, tk_ws, tk_bytes, st);
-    if (s != HMM_OK) return s;
     const int64_t n_sel = T * topk;
-    dsa_pad_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(out_idx, sel_sc, n_sel);
-    s = check_launch("dsa_pad_kernel");
-    if (s != HMM_OK) return s;
+    // long rows: the sampled per-row selection; otherwise (or for a row it
+    // flags) the general top-k
+    const bool row_path = L >= 16 * topk && L >= RT_SAMPLE;
+    if (row_path) {
+        HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_row_topk_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)RT_SMEM));
+        dsa_row_topk_kernel<<<(unsigned)T, RT_THREADS, RT_SMEM, st>>>(scores, L, (int)topk,
+                                                                      out_idx, sel_sc, status);
+        hmm_status_t s = check_launch("dsa_row_topk_kernel");
+        if (s != HMM_OK) return s;
+    }
+    int h[2] = {0, 0};
     if (L > 0) {
-        int h = 0;
-        HMM_CUDA_TRY(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, st));
+        HMM_CUDA_TRY(cudaMemcpyAsync(h, status, sizeof(h), cudaMemcpyDeviceToHost, st));
         HMM_CUDA_TRY(cudaStreamSynchronize(st));
-        if (h)
+        if (h[0])
             return set_error(HMM_ERR_TIMEOUT,
                              "dsa_scores_kernel: a bounded pipeline wait gave up; outputs invalid");
     }
-    return HMM_OK;
+    if (!row_path || h[1]) {
+        hmm_status_t s = hmm_topk_f32(scores, L, T, topk, out_idx, sel_sc, tk_ws, tk_bytes, st);
+        if (s != HMM_OK) return s;
+    }
+    dsa_pad_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(out_idx, sel_sc, n_sel);
+    return check_launch("dsa_pad_kernel");
 }

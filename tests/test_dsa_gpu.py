@@ -44,6 +44,7 @@ def inputs(seed, T, H, L):
     (32, 64, 2048, 2048 - 32, 256),    # the config-4 shape, scaled down
     (37, 16, 1000, -1, 64),            # early tokens see fewer keys than k; ragged group
     (24, 32, 1500, 2000, 100),         # every key visible
+    (16, 64, 8192, 8192 - 16, 256),    # long rows: the sampled per-row selection
 ])
 def test_dsa_fp8_matches_exact_within_tolerance(cuda, T, H, L, pos0, topk):
     q, k, w = inputs(800 + T, T, H, L)
@@ -71,6 +72,9 @@ def test_dsa_fp8_matches_exact_within_tolerance(cuda, T, H, L, pos0, topk):
         assert np.array_equal(sc[t, :m], full[t, got])             # reported = computed scores
         assert (np.diff(sc[t, :m]) <= 0).all()                     # best first
         assert (got <= pos0 + t).all()                              # causal
+        # the selection is exact over the kernel's own scores
+        own = np.lexsort((np.arange(L), -full[t].astype(np.float64)))[:m]
+        assert np.array_equal(got, own)
         if m == 0:
             continue
         order = np.lexsort((np.arange(L), -exact[t]))               # exact ranking, ties lowest
