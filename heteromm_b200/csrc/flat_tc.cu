@@ -65,8 +65,8 @@ constexpr int FA_BYTES = TC_M * 32;            // threshold-fold A operand: 128 
 constexpr int FB_BYTES = TC_NMAX * 32;         // threshold-fold B operand: 256 rows x 16 bf16
 constexpr int N_EPI_WARPS = 8;                 // two epilogue warpgroups (even / odd tiles)
 constexpr int NTHREADS = 32 * (8 + N_EPI_WARPS);
-constexpr int QCAP = 96;                       // per-warp rescoring queue (deferred across tiles)
-constexpr int FLUSH_MARK = 48;                 // queue fill that triggers a flush after a tile
+constexpr int RING = 128;                       // pairs per epilogue warp awaiting rescoring
+constexpr int N_RESCORERS = 2;                  // warps 2 and 3
 constexpr int TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
@@ -100,8 +100,11 @@ struct __align__(8) Ctrl {
     float l1max;                    // max over queries of sum_j |b_qj|
     float tmax;                     // max |folded threshold| ever written to the fold operand
     uint64_t tau[TC_NMAX];          // CTA copy of each query's threshold composite
-    uint64_t queue[N_EPI_WARPS][QCAP];   // (shard row << 8) | query
-    unsigned hist[N_EPI_WARPS][256];
+    uint64_t ring[N_EPI_WARPS][RING];    // (shard row << 8) | query, epilogue -> rescorer
+    int ring_head[N_EPI_WARPS];          // consumed (rescorer)
+    int ring_tail[N_EPI_WARPS];          // published (epilogue warp)
+    int epi_done[N_EPI_WARPS];           // the epilogue warp has published its last pair
+    unsigned hist[N_RESCORERS][256];
     float mrow[MR_RING][TC_M];      // EPS * max|a_r| per row of tile i
 };
 
@@ -232,52 +235,52 @@ __device__ __forceinline__ void raise_tau(Ctrl* ctl, unsigned char* FB, int q, u
     if (T > old) write_fold(FB, ctl, q, T);
 }
 
-// Rescores the warp's queued pairs exactly and appends the ones that beat
-// their query's threshold to the pools; raises thresholds at fill marks.
-__device__ __noinline__ void flush_queue(Ctrl* ctl, unsigned char* FB, int ew, int qc,
-                                         const TcArgs& a) {
+// Rescores one batch of up to 32 queued pairs exactly (lane = pair) and
+// appends the ones that beat their query's threshold to the pools; raises
+// thresholds at fill marks from the newest RAISE_WINDOW pool entries.
+__device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned char* FB, unsigned* hist,
+                                           uint64_t e, bool valid, int m, const TcArgs& a) {
     const int lane = threadIdx.x & 31;
-    if (lane == 0) atomicAdd(&a.status[2], qc);
-    for (int base = 0; base < qc; base += 32) {
-        const int i = base + lane;
-        int q = 0, raise = 0;
-        if (i < qc) {
-            const uint64_t e = ctl->queue[ew][i];
-            const int64_t row = (int64_t)(e >> 8);
-            q = (int)(e & 255u);
-            const float s = exact_dot_rows(a.mem + row * TC_DIM, a.qry + (int64_t)q * TC_DIM);
-            const uint64_t E = make_cand(f32_key(s), (uint32_t)row);
-            if (E > ctl->tau[q]) {
-                const int pos = atomicAdd(&a.pool_cnt[q], 1);
-                if (pos < a.pool_cap) {
-                    a.pool[(int64_t)q * a.pool_cap + pos] = E;
-                    const int w = pos + 1;
-                    if (w >= a.wm0 && (w % RAISE_STEP) == 0) raise = w;
-                } else {
-                    atomicExch(&a.status[1], 1);
-                }
+    if (lane == 0) atomicAdd(&a.status[2], m);
+    int q = 0, raise = 0;
+    if (valid) {
+        const int64_t row = (int64_t)(e >> 8);
+        q = (int)(e & 255u);
+        const float s = exact_dot_rows(a.mem + row * TC_DIM, a.qry + (int64_t)q * TC_DIM);
+        const uint64_t E = make_cand(f32_key(s), (uint32_t)row);
+        if (E > ctl->tau[q]) {
+            const int pos = atomicAdd(&a.pool_cnt[q], 1);
+            if (pos < a.pool_cap) {
+                a.pool[(int64_t)q * a.pool_cap + pos] = E;
+                const int w = pos + 1;
+                if (w >= a.wm0 && (w % RAISE_STEP) == 0) raise = w;
+            } else {
+                atomicExch(&a.status[1], 1);
             }
         }
-        unsigned m = __ballot_sync(0xffffffffu, raise != 0);
-        while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            const int W = __shfl_sync(0xffffffffu, raise, src);
-            const int qq = __shfl_sync(0xffffffffu, q, src);
-            const uint64_t T =
-                warp_select_threshold(a.pool + (int64_t)qq * a.pool_cap + (W > RAISE_WINDOW ? W - RAISE_WINDOW : 0),
-                                      W > RAISE_WINDOW ? RAISE_WINDOW : W, a.k, ctl->hist[ew]);
-            if (lane == 0) atomicAdd(&a.status[3], 1);
-            if (lane == 0 && T != 0ull) {
-                atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
-                          (unsigned long long)T);
-                raise_tau(ctl, FB, qq, T);
-            }
-            __syncwarp();
+    }
+    unsigned mk = __ballot_sync(0xffffffffu, raise != 0);
+    while (mk) {
+        const int src = __ffs(mk) - 1;
+        mk &= mk - 1;
+        const int W = __shfl_sync(0xffffffffu, raise, src);
+        const int qq = __shfl_sync(0xffffffffu, q, src);
+        const uint64_t T =
+            warp_select_threshold(a.pool + (int64_t)qq * a.pool_cap + (W > RAISE_WINDOW ? W - RAISE_WINDOW : 0),
+                                  W > RAISE_WINDOW ? RAISE_WINDOW : W, a.k, hist);
+        if (lane == 0) atomicAdd(&a.status[3], 1);
+        if (lane == 0 && T != 0ull) {
+            atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
+                      (unsigned long long)T);
+            raise_tau(ctl, FB, qq, T);
         }
+        __syncwarp();
     }
     __syncwarp();
 }
+
+__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+__device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
 
 // One persistent CTA per SM.  Roles (16 warps):
 //   warp 0      TMA producer: the 256 queries once, then 128-row x 128-col bf16
@@ -286,13 +289,15 @@ __device__ __noinline__ void flush_queue(Ctrl* ctl, unsigned char* FB, int ew, i
 //               queries, K = 16) plus one K = 16 MMA that adds -t'_q (each
 //               query's threshold, folded as a bf16 rounded down) into the same
 //               TMEM accumulator (two accumulators of 256 fp32 columns)
-//   warp 2      TMEM allocator
+//   warp 2      TMEM allocator, then (with warp 3) exact rescoring of the pairs
+//               the epilogue publishes to per-warp rings
 //   warps 4-7   row bounds: EPS * max|a_r| for each row of a landed tile; with
 //               the MMA commit they free the tile's stage
 //   warps 8-15  epilogue, two warpgroups (even / odd tiles): thread = row
 //               (TMEM lane); a 3-input max tree over the row's 256 folded
 //               scores s~ - t'_q against the row's margin; rows that reach it
-//               go to exact rescoring
+//               are published to the warp's ring for the rescorer warps, so
+//               rescoring never delays the accumulator release
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
@@ -323,6 +328,11 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         mbar_init(&ctl->b_full, 1);
         for (int e = 0; e < MR_RING; ++e) mbar_init(&ctl->mr_full[e], 4);
         ctl->abort = 0;
+        for (int e = 0; e < N_EPI_WARPS; ++e) {
+            ctl->ring_head[e] = 0;
+            ctl->ring_tail[e] = 0;
+            ctl->epi_done[e] = 0;
+        }
         ctl->l1max = 0.0f;
         ctl->tmax = 0.0f;
         fence_barrier_init();
@@ -446,7 +456,8 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         const int sub = warp & 3;           // TMEM lanes 32*sub .. +31
         const int r = sub * 32 + lane;      // tile row of this thread
         const int nchunks = (a.nq + 31) / 32;
-        int qc = 0;   // queued (row, query) pairs awaiting exact rescoring
+        int tail = 0;   // pairs this warp has published to its ring (warp-uniform)
+        bool ring_ok = true;
         for (int i = g; i < my_tiles; i += 2) {
             const int b = i & 1;
             // ---- off the critical path: the tile's row bounds are published
@@ -503,34 +514,108 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                         const int rem = a.nq - c * 32;
                         bits &= rem >= 32 ? 0xffffffffu : (rem > 0 ? (1u << rem) - 1u : 0u);
                     }
-                    while (__any_sync(0xffffffffu, bits != 0)) {
+                    while (ring_ok && __any_sync(0xffffffffu, bits != 0)) {
                         const bool has = bits != 0;
                         const int j = has ? __ffs(bits) - 1 : 0;
                         bits &= bits - 1;
                         const unsigned mk = __ballot_sync(0xffffffffu, has);
-                        if (has)
-                            ctl->queue[ew][qc + __popc(mk & ((1u << lane) - 1u))] =
-                                ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
-                        qc += __popc(mk);
-                        if (qc > QCAP - 32) {   // only when a tile floods the queue
+                        const int n = __popc(mk);
+                        // room in the ring: the rescorer frees slots as it goes (bounded
+                        // wait; what is queued so far is published first, or the
+                        // rescorer could not see it to free anything)
+                        if (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
                             __syncwarp();
-                            flush_queue(ctl, FB, ew, qc, a);
-                            qc = 0;
+                            if (lane == 0) {
+                                __threadfence_block();
+                                st_volatile(&ctl->ring_tail[ew], tail);
+                            }
+                            const uint64_t t0 = globaltimer_ns();
+                            while (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
+                                if (*abort || globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+                                    ring_ok = false;
+                                    break;
+                                }
+                                __nanosleep(64);
+                            }
+                            ring_ok = __all_sync(0xffffffffu, ring_ok);
+                            if (!ring_ok) break;
                         }
+                        if (has)
+                            ctl->ring[ew][(tail + __popc(mk & ((1u << lane) - 1u))) % RING] =
+                                ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
+                        tail += n;   // published once per tile, below
                     }
+                    if (!ring_ok) break;
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->acc_empty[b]);
-            // rescoring happens off the accumulator's critical path
-            if (qc >= FLUSH_MARK) {
-                flush_queue(ctl, FB, ew, qc, a);
-                qc = 0;
+            if (lane == 0) {
+                mbar_arrive(&ctl->acc_empty[b]);
+                __threadfence_block();
+                st_volatile(&ctl->ring_tail[ew], tail);   // this tile's pairs
+            }
+            if (!ring_ok) {
+                if (lane == 0) set_abort(ctl, a.status);
+                break;
             }
             if (qr < a.nq && t_new > ctl->tau[qr]) raise_tau(ctl, FB, qr, t_new);
         }
-        if (qc > 0) flush_queue(ctl, FB, ew, qc, a);
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            st_volatile(&ctl->epi_done[ew], 1);   // after its last published pair
+        }
+    } else if (warp == 2 || warp == 3) {
+        // ------------------------------------------------------- rescorers
+        // Exact rescoring of the epilogue warps' pairs, off the accumulator
+        // path: rescorer c drains the rings of epilogue warps 4c .. 4c + 3.
+        const int c = warp - 2;
+        int head[4] = {0, 0, 0, 0};   // warp-uniform
+        uint64_t last = globaltimer_ns();
+        for (;;) {
+            bool progress = false;
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+                const int e = c * 4 + e4;
+                int avail = ld_volatile(&ctl->ring_tail[e]) - head[e4];
+                __threadfence_block();   // the entries published before that tail
+                while (avail > 0) {
+                    const int m = min(avail, 32);
+                    const bool valid = lane < m;
+                    const uint64_t entry = valid ? ctl->ring[e][(head[e4] + lane) % RING] : 0ull;
+                    __syncwarp();
+                    head[e4] += m;
+                    avail -= m;
+                    if (lane == 0) {
+                        __threadfence_block();
+                        st_volatile(&ctl->ring_head[e], head[e4]);   // slots read: free them
+                    }
+                    rescore_batch(ctl, FB, ctl->hist[c], entry, valid, m, a);
+                    progress = true;
+                }
+            }
+            if (progress) {
+                last = globaltimer_ns();
+                continue;
+            }
+            // idle: done once every producer has finished and its ring is empty
+            bool done = true;
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+                const int e = c * 4 + e4;
+                const bool fin = ld_volatile(&ctl->epi_done[e]) != 0;
+                __threadfence_block();
+                done = done && fin && ld_volatile(&ctl->ring_tail[e]) == head[e4];
+            }
+            if (__all_sync(0xffffffffu, done)) break;
+            if (*abort) break;
+            if (globaltimer_ns() - last > WAIT_LIMIT_NS) {
+                if (lane == 0) set_abort(ctl, a.status);
+                break;
+            }
+            __nanosleep(256);
+        }
     }
 
     tc_fence_before();
