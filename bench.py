@@ -395,8 +395,12 @@ def run_paged(args, rank, world, local):
     torch.cuda.synchronize()
     build_ms = e0.elapsed_time(e1)
 
+    # decode loop: no per-step wait; the bounds status is checked after the loop
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
     def step(qq):
-        return hmm.block_sparse_decode_bf16(qq, summ, k16, v16, table, P_LEN, P_BLOCK, P_TOP)
+        return hmm.block_sparse_decode_bf16(qq, summ, k16, v16, table, P_LEN, P_BLOCK, P_TOP,
+                                            status=status)
 
     for _ in range(args.warmup):
         step(q16)
@@ -418,6 +422,8 @@ def run_paged(args, rank, world, local):
     k_total, k_n = _abi.profile_read()
     ms = e0.elapsed_time(e1) / args.steps
     kern_ms = k_total / args.steps   # per step, all its launches
+    from heteromm_b200.paged import check_status
+    check_status(status)
 
     # end to end: q from pinned host memory, selected blocks + outputs back
     q_host = q16.cpu().pin_memory()

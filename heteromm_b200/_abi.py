@@ -48,6 +48,9 @@ SIGNATURES = {
                                                   _P, _I, _P, _P, _S, _P]),
     "hmm_block_sparse_attention_f32": (C.c_int, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _P, _P,
                                                  _S, _P]),
+    "hmm_block_sparse_decode_bf16_async": (C.c_int, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I,
+                                                     _I, _I, _I, _P, _P, _P, _P, _S, _P]),
+    "hmm_status_read": (C.c_int, [_P, _P]),
     "hmm_block_sparse_decode_bf16": (C.c_int, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I,
                                                _I, _P, _P, _P, _S, _P]),
     "hmm_bm25_stats_host": (C.c_int, [_P, _I, _P, _I, _P, _P]),

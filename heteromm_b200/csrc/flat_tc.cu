@@ -70,7 +70,10 @@ constexpr int N_RESCORERS = 2;                  // warps 2 and 3
 constexpr int TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
-constexpr int SEED_ROWS = 8192;
+#ifndef HMM_SEED_ROWS
+#define HMM_SEED_ROWS 8192
+#endif
+constexpr int SEED_ROWS = HMM_SEED_ROWS;
 #ifndef HMM_PASS_GROWTH
 #define HMM_PASS_GROWTH 128
 #endif

@@ -916,11 +916,12 @@ extern "C" hmm_status_t hmm_block_sparse_attention_bf16(
     return read_status(status, st, "hmm_block_sparse_attention_bf16");
 }
 
-extern "C" hmm_status_t hmm_block_sparse_decode_bf16(
+extern "C" hmm_status_t hmm_block_sparse_decode_bf16_async(
     const uint16_t* q, const float* summaries, const uint16_t* k_pages, const uint16_t* v_pages,
     int64_t n_pages, const int32_t* page_table, int64_t n_seq, int64_t pages_per_seq,
     int64_t seq_len, int64_t page_tokens, int64_t block_tokens, int64_t D, int64_t top_blocks,
-    int32_t* out_blocks, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+    int32_t* out_blocks, float* out, int32_t* device_status, void* workspace,
+    size_t workspace_bytes, void* stream) {
     hmm_status_t s = bsa_common(q, k_pages, v_pages, n_pages, page_table, n_seq, pages_per_seq,
                                 seq_len, page_tokens, block_tokens, D, top_blocks, out);
     if (s != HMM_OK) return s;
@@ -945,9 +946,9 @@ extern "C" hmm_status_t hmm_block_sparse_decode_bf16(
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     if (!ws || workspace_bytes < need)
         return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", workspace_bytes, need);
-    int* status = reinterpret_cast<int*>(ws + st_off);
+    HMM_REQUIRE(device_status, "device_status is null");
+    int* status = device_status;
     int32_t* sel = out_blocks ? out_blocks : reinterpret_cast<int32_t*>(ws + sel_off);
-    HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
     const int n2 = next_pow2((int)n_blocks);
     const size_t ssm = sizeof(uint64_t) * n2 + sizeof(float) * D;
     HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel,
@@ -970,9 +971,34 @@ extern "C" hmm_status_t hmm_block_sparse_decode_bf16(
     a.block_tokens = (int)block_tokens;
     a.scale = 1.0f / sqrtf((float)D);
     a.status = status;
-    s = run_bsa(a, n_seq, D, out, ws, st_off + 256, st);
+    return run_bsa(a, n_seq, D, out, ws, st_off + 256, st);
+}
+
+extern "C" hmm_status_t hmm_block_sparse_decode_bf16(
+    const uint16_t* q, const float* summaries, const uint16_t* k_pages, const uint16_t* v_pages,
+    int64_t n_pages, const int32_t* page_table, int64_t n_seq, int64_t pages_per_seq,
+    int64_t seq_len, int64_t page_tokens, int64_t block_tokens, int64_t D, int64_t top_blocks,
+    int32_t* out_blocks, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+    // the status word sits just past the partial results of the workspace
+    const size_t st_off = up256(bsa_part_bytes(n_seq, top_blocks, block_tokens, D));
+    if (!workspace || workspace_bytes < st_off + 256)
+        return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", workspace_bytes,
+                         st_off + 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int* status = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + st_off);
+    HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
+    hmm_status_t s = hmm_block_sparse_decode_bf16_async(
+        q, summaries, k_pages, v_pages, n_pages, page_table, n_seq, pages_per_seq, seq_len,
+        page_tokens, block_tokens, D, top_blocks, out_blocks, out, status, workspace,
+        workspace_bytes, stream);
     if (s != HMM_OK) return s;
+    if (n_seq == 0 || seq_len == 0) return HMM_OK;
     return read_status(status, st, "hmm_block_sparse_decode_bf16");
+}
+
+extern "C" hmm_status_t hmm_status_read(const int32_t* device_status, void* stream) {
+    HMM_REQUIRE(device_status, "device_status is null");
+    return read_status(device_status, static_cast<cudaStream_t>(stream), "device status");
 }
 
 extern "C" hmm_status_t hmm_block_sparse_attention_f32(const float* q, const float* keys,

@@ -87,8 +87,13 @@ def block_sparse_attention_bf16(q: torch.Tensor, k_pages: torch.Tensor, v_pages:
 
 def block_sparse_decode_bf16(q: torch.Tensor, summaries: torch.Tensor, k_pages: torch.Tensor,
                              v_pages: torch.Tensor, page_table: torch.Tensor, seq_len: int,
-                             block_tokens: int, top_blocks: int):
-    """One decode step: (selected blocks [n_seq, top_blocks] int32, out [n_seq, D] fp32)."""
+                             block_tokens: int, top_blocks: int,
+                             status: torch.Tensor | None = None):
+    """One decode step: (selected blocks [n_seq, top_blocks] int32, out [n_seq, D] fp32).
+
+    With `status` (an int32 device tensor the caller zeroes) the call does not
+    wait for the stream: bad page-table entries / block ids set its bits, and
+    check_status(status) raises for them later."""
     n_pages, pt, D, n_seq, pps = _cache_dims(k_pages, page_table)
     _check(v_pages, torch.int16, "v_pages")
     _check(q, torch.int16, "q")
@@ -97,11 +102,23 @@ def block_sparse_decode_bf16(q: torch.Tensor, summaries: torch.Tensor, k_pages: 
     out = torch.empty((n_seq, D), dtype=torch.float32, device=q.device)
     ws = workspace(load().hmm_paged_workspace_size(n_seq, top_blocks, block_tokens, D),
                    q.device)
-    call("hmm_block_sparse_decode_bf16", q.data_ptr(), summaries.data_ptr(), k_pages.data_ptr(),
-         v_pages.data_ptr(), n_pages, page_table.data_ptr(), n_seq, pps, seq_len, pt,
-         block_tokens, D, top_blocks, blocks.data_ptr(), out.data_ptr(), ws.data_ptr(),
-         ws.numel(), _stream())
+    if status is None:
+        call("hmm_block_sparse_decode_bf16", q.data_ptr(), summaries.data_ptr(),
+             k_pages.data_ptr(), v_pages.data_ptr(), n_pages, page_table.data_ptr(), n_seq, pps,
+             seq_len, pt, block_tokens, D, top_blocks, blocks.data_ptr(), out.data_ptr(),
+             ws.data_ptr(), ws.numel(), _stream())
+    else:
+        _check(status, torch.int32, "status")
+        call("hmm_block_sparse_decode_bf16_async", q.data_ptr(), summaries.data_ptr(),
+             k_pages.data_ptr(), v_pages.data_ptr(), n_pages, page_table.data_ptr(), n_seq, pps,
+             seq_len, pt, block_tokens, D, top_blocks, blocks.data_ptr(), out.data_ptr(),
+             status.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
     return blocks, out
+
+
+def check_status(status: torch.Tensor) -> None:
+    """Waits for the stream and raises HmmError(HMM_ERR_BOUNDS) if `status` has bits set."""
+    call("hmm_status_read", status.data_ptr(), _stream())
 
 
 def block_sparse_attention_f32(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,

@@ -242,6 +242,20 @@ hmm_status_t hmm_block_sparse_decode_bf16(const uint16_t* q, const float* summar
                                           int32_t* out_blocks, float* out, void* workspace,
                                           size_t workspace_bytes, void* stream);
 
+/* The same step without waiting for `stream`: page-table entries outside
+ * [0, n_pages) and negative block ids set bits in *device_status (an int32
+ * in device memory the caller zeroes; bit 0 page, bit 1 block) instead of
+ * making the call return HMM_ERR_BOUNDS; the kernels never follow them.
+ * hmm_status_read waits for `stream` and turns such bits into
+ * HMM_ERR_BOUNDS.  For decode loops that check once per many steps. */
+hmm_status_t hmm_block_sparse_decode_bf16_async(
+    const uint16_t* q, const float* summaries, const uint16_t* k_pages, const uint16_t* v_pages,
+    int64_t n_pages, const int32_t* page_table, int64_t n_seq, int64_t pages_per_seq,
+    int64_t seq_len, int64_t page_tokens, int64_t block_tokens, int64_t D, int64_t top_blocks,
+    int32_t* out_blocks, float* out, int32_t* device_status, void* workspace,
+    size_t workspace_bytes, void* stream);
+hmm_status_t hmm_status_read(const int32_t* device_status, void* stream);
+
 /* ----------------------------------------------------------------- BM25
  * FusedBM25Retrieval (reference steps/example_kernel/bm25_fpga_retrieval.cpp:
  * 143-205) over a CSR inverted index: postings of term t are

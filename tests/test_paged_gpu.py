@@ -184,3 +184,23 @@ def test_block_sparse_attention_f32_contiguous(cuda, L, D, bt, nsel):
     for s in range(n_seq):
         ref = O.block_sparse_attention_f32(keys[s], vals[s], blocks[s], q[s], bt)
         np.testing.assert_allclose(out[s], ref, rtol=RTOL, atol=ATOL)
+
+
+def test_decode_async_matches_sync_and_reports_bounds(cuda):
+    from heteromm_b200.paged import check_status
+    keys, vals, kp, vp, table = make_cache(380, 3, 1000, 64, 16)
+    q = T(gen.bf16_bits(gen.normal_f32(381, (3, 64))).view(np.int16), cuda)
+    k, v, tb = dev_cache(cuda, kp, vp, table)
+    summ = hmm.paged_kv_summary_bf16(k, tb, 1000, 64)
+    b0, o0 = hmm.block_sparse_decode_bf16(q, summ, k, v, tb, 1000, 64, 6)
+    st = torch.zeros(1, dtype=torch.int32, device=cuda)
+    b1, o1 = hmm.block_sparse_decode_bf16(q, summ, k, v, tb, 1000, 64, 6, status=st)
+    check_status(st)
+    assert torch.equal(b0, b1) and torch.equal(o0, o1)
+    bad = table.copy()
+    bad[1, 3] = kp.shape[0] + 5
+    st.zero_()
+    hmm.block_sparse_decode_bf16(q, summ, k, v, T(bad, cuda), 1000, 64, 64, status=st)
+    with pytest.raises(HmmError) as e:
+        check_status(st)
+    assert e.value.status == HMM_ERR_BOUNDS
