@@ -67,6 +67,21 @@ struct DsaArgs {
     int n_groups, key_tiles;
 };
 
+// Packed fp32 pairs for fma.rn.f32x2 (sm_100a).
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 __device__ __forceinline__ int group_tiles(const DsaArgs& a, int g) {
     const int64_t t_last = min(a.T, (int64_t)(g + 1) * a.tg) - 1;
     const int64_t vis = a.pos0 + t_last + 1;            // keys visible to the group's last token
@@ -231,7 +246,9 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     const int tcol = (half * tg2 + tl) * a.H;
                     const int64_t tok = (int64_t)g * a.tg + half * tg2 + tl;
                     const float* wr = wsm + tl * a.H;
-                    float s = 0.0f;
+                    // even / odd heads in the two halves of a packed fp32 pair
+                    // (fma.rn.f32x2: one instruction per two heads)
+                    uint64_t s2 = pack_f32x2(0.0f, 0.0f);
                     for (int c0 = 0; c0 < a.H; c0 += 64) {
                         uint32_t v[2][32];
                         tmem_ld_x32(tb + (uint32_t)(tcol + c0), v[0]);
@@ -245,13 +262,20 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                                 if (c0 + hh * 32 + h4 >= a.H) break;   // H = 16: half a load
                                 const float4 w4 =
                                     *reinterpret_cast<const float4*>(wr + c0 + hh * 32 + h4);
-                                s = fmaf(w4.x, fmaxf(__uint_as_float(v[hh][h4 + 0]), 0.0f), s);
-                                s = fmaf(w4.y, fmaxf(__uint_as_float(v[hh][h4 + 1]), 0.0f), s);
-                                s = fmaf(w4.z, fmaxf(__uint_as_float(v[hh][h4 + 2]), 0.0f), s);
-                                s = fmaf(w4.w, fmaxf(__uint_as_float(v[hh][h4 + 3]), 0.0f), s);
+                                s2 = fma_f32x2(pack_f32x2(w4.x, w4.y),
+                                               pack_f32x2(fmaxf(__uint_as_float(v[hh][h4 + 0]), 0.0f),
+                                                          fmaxf(__uint_as_float(v[hh][h4 + 1]), 0.0f)),
+                                               s2);
+                                s2 = fma_f32x2(pack_f32x2(w4.z, w4.w),
+                                               pack_f32x2(fmaxf(__uint_as_float(v[hh][h4 + 2]), 0.0f),
+                                                          fmaxf(__uint_as_float(v[hh][h4 + 3]), 0.0f)),
+                                               s2);
                             }
                         }
                     }
+                    float s_lo, s_hi;
+                    unpack_f32x2(s2, s_lo, s_hi);
+                    const float s = s_lo + s_hi;
                     if (tok < a.T && j < a.L)
                         a.scores[tok * a.L + j] = j <= a.pos0 + tok ? s : -INFINITY;
                 }
