@@ -64,9 +64,10 @@ constexpr int Q_BYTES = 2 * Q_BOX;             // 64 KiB
 constexpr int FA_BYTES = TC_M * 32;            // threshold-fold A operand: 128 rows x 16 bf16
 constexpr int FB_BYTES = TC_NMAX * 32;         // threshold-fold B operand: 256 rows x 16 bf16
 constexpr int N_EPI_WARPS = 8;                 // two epilogue warpgroups (even / odd tiles)
-constexpr int NTHREADS = 32 * (8 + N_EPI_WARPS);
+constexpr int NTHREADS = 32 * (10 + N_EPI_WARPS);   // + TMA, MMA, 4 rescorers, 4 row-bound warps
 constexpr int RING = 128;                       // pairs per epilogue warp awaiting rescoring
-constexpr int N_RESCORERS = 2;                  // warps 2 and 3
+constexpr int N_RESCORERS = 4;                  // warps 2, 3, 16 and 17
+constexpr int RPR = N_EPI_WARPS / N_RESCORERS;  // rings per rescorer
 constexpr int TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
@@ -90,6 +91,7 @@ constexpr int KMAX_TC = 128;
 constexpr int RAISE_STEP = HMM_RAISE_STEP;      // appends between threshold raises
 constexpr int RAISE_WINDOW = HMM_RAISE_WINDOW;  // newest pool entries a raise selects over
 constexpr int MR_RING = 8;                     // tiles of row bounds in flight (>= STAGES + 2)
+constexpr uint64_t REFRESH_NS = 2000;          // cadence of the rescorers' shared-threshold refresh
 
 struct __align__(8) Ctrl {
     uint64_t a_full[STAGES];        // tile landed (TMA tx)
@@ -170,12 +172,14 @@ __device__ __forceinline__ uint32_t neg_fold_pair(uint64_t T, float* mag) {
 // Writes query q's folded threshold into the fold B operand (row q, K
 // columns 0-1 as one 4-byte store, so a concurrent MMA sees the old or the
 // new pair, both <= the current threshold; 32-byte swizzle: 16-byte chunk c
-// of row q sits at c ^ ((q >> 2) & 1)).
+// of row q sits at c ^ ((q >> 2) & 1)).  The fold bound tmax is raised
+// first, so no MMA can read a fold that the epilogue's margin does not cover.
 __device__ __forceinline__ void write_fold(unsigned char* FB, Ctrl* ctl, int q, uint64_t T) {
     float mag;
     const uint32_t bits = neg_fold_pair(T, &mag);
-    *reinterpret_cast<uint32_t*>(FB + q * 32 + ((((q >> 2) & 1)) << 4)) = bits;
     atomicMax(reinterpret_cast<int*>(&ctl->tmax), __float_as_int(__fmul_ru(mag, 1.0f + 1.0f / 1024.0f)));
+    __threadfence_block();
+    *reinterpret_cast<uint32_t*>(FB + q * 32 + ((((q >> 2) & 1)) << 4)) = bits;
     fence_proxy_async_smem();
 }
 
@@ -285,15 +289,16 @@ __device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned char* FB, unsigne
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 __device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
 
-// One persistent CTA per SM.  Roles (16 warps):
+// One persistent CTA per SM.  Roles (18 warps):
 //   warp 0      TMA producer: the 256 queries once, then 128-row x 128-col bf16
 //               tiles (two 64-column boxes, 128-byte swizzle) into a 4-stage ring
 //   warp 1      MMA issuer: per tile, 8 x tcgen05.mma (M = 128 rows, N = 256
 //               queries, K = 16) plus one K = 16 MMA that adds -t'_q (each
 //               query's threshold, folded as a bf16 rounded down) into the same
 //               TMEM accumulator (two accumulators of 256 fp32 columns)
-//   warp 2      TMEM allocator, then (with warp 3) exact rescoring of the pairs
-//               the epilogue publishes to per-warp rings
+//   warp 2      TMEM allocator, then (with warps 3, 16, 17) exact rescoring of
+//               the pairs the epilogue publishes to per-warp rings, and the
+//               refolding of thresholds that other CTAs raised
 //   warps 4-7   row bounds: EPS * max|a_r| for each row of a landed tile; with
 //               the MMA commit they free the tile's stage
 //   warps 8-15  epilogue, two warpgroups (even / odd tiles): thread = row
@@ -452,14 +457,15 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctl->mr_full[i % MR_RING]);
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 8 && warp < 16) {
         // --------------------------------------------------------- epilogue
         const int ew = warp - 8;            // 0..7
         const int g = ew >> 2;              // warpgroup: tiles with i % 2 == g
         const int sub = warp & 3;           // TMEM lanes 32*sub .. +31
         const int r = sub * 32 + lane;      // tile row of this thread
         const int nchunks = (a.nq + 31) / 32;
-        int tail = 0;   // pairs this warp has published to its ring (warp-uniform)
+        int tail = 0;        // pairs this warp has queued in its ring (warp-uniform)
+        int published = 0;   // of those, pairs whose tail the rescorers can see
         bool ring_ok = true;
         for (int i = g; i < my_tiles; i += 2) {
             const int b = i & 1;
@@ -470,10 +476,6 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             }
             const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
             const bool valid = tile_row0 + r < a.n_rows;
-            // start the load of this warp's 32 shared thresholds; applied after the filter
-            const int qr = ew * 32 + lane;
-            uint64_t t_new = 0;
-            if (qr < a.nq) t_new = *reinterpret_cast<volatile uint64_t*>(&a.tau_global[qr]);
             const float er = ctl->mrow[i % MR_RING][r];
 
             // ---- critical path: accumulator ready -> filter -> release
@@ -487,116 +489,155 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             const float margin = __fmaf_ru(er, ctl->l1max, __fmul_ru(EPS, ctl->tmax));
             const float neg = valid ? -margin : INFINITY;   // rows past the end never pass
             const uint32_t tbase = tmem + (uint32_t)(b * TC_NMAX) + ((uint32_t)(sub * 32) << 16);
+            // one 32-column chunk per tcgen05.wait::ld: measured faster than two
 #pragma unroll 1
-            for (int c0 = 0; c0 < nchunks; c0 += 2) {
-                uint32_t v[2][32];
-                tmem_ld_x32(tbase + (uint32_t)(c0 * 32), v[0]);
-                if (c0 + 1 < nchunks) tmem_ld_x32(tbase + (uint32_t)(c0 * 32 + 32), v[1]);
+            for (int c = 0; c < nchunks; ++c) {
+                uint32_t v[32];
+                tmem_ld_x32(tbase + (uint32_t)(c * 32), v);
                 tmem_wait_ld();
+                float m[11];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int c = c0 + h;
-                    float m[11];
+                for (int j = 0; j < 10; ++j)
+                    m[j] = max3_nan(__uint_as_float(v[3 * j]), __uint_as_float(v[3 * j + 1]),
+                                    __uint_as_float(v[3 * j + 2]));
+                m[10] = max3_nan(__uint_as_float(v[30]), __uint_as_float(v[31]), __uint_as_float(v[31]));
+                const float m0 = max3_nan(m[0], m[1], m[2]), m1 = max3_nan(m[3], m[4], m[5]);
+                const float m2 = max3_nan(m[6], m[7], m[8]), m3 = max3_nan(m[9], m[10], m[10]);
+                const float mx = max3_nan(max3_nan(m0, m1, m2), m3, m3);
+                const bool hit = !(mx < neg);   // NaN passes
+                if (!__any_sync(0xffffffffu, hit)) continue;
+                // rare: queue the (row, query) pairs of this chunk that reach -margin
+                uint32_t bits = 0;
+                if (hit) {
 #pragma unroll
-                    for (int j = 0; j < 10; ++j)
-                        m[j] = max3_nan(__uint_as_float(v[h][3 * j]), __uint_as_float(v[h][3 * j + 1]),
-                                        __uint_as_float(v[h][3 * j + 2]));
-                    m[10] = max3_nan(__uint_as_float(v[h][30]), __uint_as_float(v[h][31]),
-                                     __uint_as_float(v[h][31]));
-                    const float m0 = max3_nan(m[0], m[1], m[2]), m1 = max3_nan(m[3], m[4], m[5]);
-                    const float m2 = max3_nan(m[6], m[7], m[8]), m3 = max3_nan(m[9], m[10], m[10]);
-                    const float mx = max3_nan(max3_nan(m0, m1, m2), m3, m3);
-                    const bool hit = c < nchunks && !(mx < neg);   // NaN passes
-                    if (!__any_sync(0xffffffffu, hit)) continue;
-                    // rare: queue the (row, query) pairs of this chunk that reach -margin
-                    uint32_t bits = 0;
-                    if (hit) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            bits |= (uint32_t)(!(__uint_as_float(v[h][j]) < neg)) << j;
-                        const int rem = a.nq - c * 32;
-                        bits &= rem >= 32 ? 0xffffffffu : (rem > 0 ? (1u << rem) - 1u : 0u);
-                    }
-                    while (ring_ok && __any_sync(0xffffffffu, bits != 0)) {
-                        const bool has = bits != 0;
-                        const int j = has ? __ffs(bits) - 1 : 0;
-                        bits &= bits - 1;
-                        const unsigned mk = __ballot_sync(0xffffffffu, has);
-                        const int n = __popc(mk);
-                        // room in the ring: the rescorer frees slots as it goes (bounded
-                        // wait; what is queued so far is published first, or the
-                        // rescorer could not see it to free anything)
-                        if (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
-                            __syncwarp();
-                            if (lane == 0) {
-                                __threadfence_block();
-                                st_volatile(&ctl->ring_tail[ew], tail);
-                            }
-                            const uint64_t t0 = globaltimer_ns();
-                            while (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
-                                if (*abort || globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-                                    ring_ok = false;
-                                    break;
-                                }
-                                __nanosleep(64);
-                            }
-                            ring_ok = __all_sync(0xffffffffu, ring_ok);
-                            if (!ring_ok) break;
-                        }
-                        if (has)
-                            ctl->ring[ew][(tail + __popc(mk & ((1u << lane) - 1u))) % RING] =
-                                ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
-                        tail += n;   // published once per tile, below
-                    }
-                    if (!ring_ok) break;
+                    for (int j = 0; j < 32; ++j)
+                        bits |= (uint32_t)(!(__uint_as_float(v[j]) < neg)) << j;
+                    const int rem = a.nq - c * 32;
+                    bits &= rem >= 32 ? 0xffffffffu : (1u << rem) - 1u;
                 }
+                while (ring_ok && __any_sync(0xffffffffu, bits != 0)) {
+                    const bool has = bits != 0;
+                    const int j = has ? __ffs(bits) - 1 : 0;
+                    bits &= bits - 1;
+                    const unsigned mk = __ballot_sync(0xffffffffu, has);
+                    const int n = __popc(mk);
+                    // room in the ring: the rescorer frees slots as it goes (bounded
+                    // wait; what is queued so far is published first, or the
+                    // rescorer could not see it to free anything)
+                    if (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
+                        __syncwarp();
+                        if (lane == 0) {
+                            __threadfence_block();
+                            st_volatile(&ctl->ring_tail[ew], tail);
+                        }
+                        published = tail;
+                        const uint64_t t0 = globaltimer_ns();
+                        while (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
+                            if (*abort || globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+                                ring_ok = false;
+                                break;
+                            }
+                            __nanosleep(64);
+                        }
+                        ring_ok = __all_sync(0xffffffffu, ring_ok);
+                        if (!ring_ok) break;
+                    }
+                    if (has)
+                        ctl->ring[ew][(tail + __popc(mk & ((1u << lane) - 1u))) % RING] =
+                            ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
+                    tail += n;   // published once per tile, below
+                }
+                if (!ring_ok) break;
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&ctl->acc_empty[b]);
-                __threadfence_block();
-                st_volatile(&ctl->ring_tail[ew], tail);   // this tile's pairs
+            if (lane == 0) mbar_arrive(&ctl->acc_empty[b]);
+            if (tail != published) {   // this tile's pairs
+                if (lane == 0) {
+                    __threadfence_block();
+                    st_volatile(&ctl->ring_tail[ew], tail);
+                }
+                published = tail;
             }
             if (!ring_ok) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
-            if (qr < a.nq && t_new > ctl->tau[qr]) raise_tau(ctl, FB, qr, t_new);
         }
         __syncwarp();
         if (lane == 0) {
             __threadfence_block();
             st_volatile(&ctl->epi_done[ew], 1);   // after its last published pair
         }
-    } else if (warp == 2 || warp == 3) {
+    } else if (warp == 2 || warp == 3 || warp >= 16) {
         // ------------------------------------------------------- rescorers
         // Exact rescoring of the epilogue warps' pairs, off the accumulator
-        // path: rescorer c drains the rings of epilogue warps 4c .. 4c + 3.
-        const int c = warp - 2;
-        int head[4] = {0, 0, 0, 0};   // warp-uniform
-        uint64_t last = globaltimer_ns();
-        for (;;) {
-            bool progress = false;
+        // path: rescorer c drains the rings of epilogue warps RPR*c .. RPR*c + RPR-1,
+        // gathering up to 32 pairs across them into one batch (lane = pair), so
+        // that sparse hits do not pay a batch's memory latency each.
+        const int c = warp < 16 ? warp - 2 : warp - 14;
+        int head[RPR];   // warp-uniform
 #pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-                const int e = c * 4 + e4;
-                int avail = ld_volatile(&ctl->ring_tail[e]) - head[e4];
-                __threadfence_block();   // the entries published before that tail
-                while (avail > 0) {
-                    const int m = min(avail, 32);
-                    const bool valid = lane < m;
-                    const uint64_t entry = valid ? ctl->ring[e][(head[e4] + lane) % RING] : 0ull;
-                    __syncwarp();
-                    head[e4] += m;
-                    avail -= m;
-                    if (lane == 0) {
-                        __threadfence_block();
-                        st_volatile(&ctl->ring_head[e], head[e4]);   // slots read: free them
+        for (int e4 = 0; e4 < RPR; ++e4) head[e4] = 0;
+        uint64_t last = globaltimer_ns();
+        uint64_t refreshed = 0;
+        for (;;) {
+            // thresholds raised by other CTAs (shared through tau_global), refolded
+            // here every REFRESH_NS so that the epilogue never waits on them
+            const uint64_t now = globaltimer_ns();
+            if (now - refreshed > REFRESH_NS) {
+                refreshed = now;
+#pragma unroll
+                for (int j = 0; j < TC_NMAX / (32 * N_RESCORERS); ++j) {
+                    const int q = c * (TC_NMAX / N_RESCORERS) + j * 32 + lane;
+                    if (q < a.nq) {
+                        const uint64_t t = *reinterpret_cast<volatile uint64_t*>(&a.tau_global[q]);
+                        if (t > ctl->tau[q]) raise_tau(ctl, FB, q, t);
                     }
-                    rescore_batch(ctl, FB, ctl->hist[c], entry, valid, m, a);
-                    progress = true;
                 }
+            }
+            int avail[RPR];
+            int total = 0;
+#pragma unroll
+            for (int e4 = 0; e4 < RPR; ++e4) {
+                // one lane's read, shared: every lane sees the same count
+                avail[e4] = __shfl_sync(0xffffffffu, ld_volatile(&ctl->ring_tail[c * RPR + e4]), 0) -
+                            head[e4];
+                total += avail[e4];
+            }
+            __threadfence_block();   // the entries published before those tails
+            bool progress = false;
+            if (total > 0) {
+                const int m = min(total, 32);
+                // lane l takes the l-th pending pair in ring order
+                int off = lane, er = 0;
+#pragma unroll
+                for (int e4 = 0; e4 < RPR - 1; ++e4)
+                    if (er == e4 && off >= avail[e4]) {
+                        off -= avail[e4];
+                        er = e4 + 1;
+                    }
+                const bool valid = lane < m;
+                uint64_t entry = 0ull;
+#pragma unroll
+                for (int e4 = 0; e4 < RPR; ++e4)
+                    if (valid && er == e4) entry = ctl->ring[c * RPR + e4][(head[e4] + off) % RING];
+                __syncwarp();
+                int rem = m;
+#pragma unroll
+                for (int e4 = 0; e4 < RPR; ++e4) {
+                    const int take = min(avail[e4], rem);
+                    rem -= take;
+                    if (take > 0) {
+                        head[e4] += take;
+                        if (lane == 0) {
+                            __threadfence_block();
+                            st_volatile(&ctl->ring_head[c * RPR + e4], head[e4]);   // slots read: free them
+                        }
+                    }
+                }
+                rescore_batch(ctl, FB, ctl->hist[c], entry, valid, m, a);
+                progress = true;
             }
             if (progress) {
                 last = globaltimer_ns();
@@ -605,8 +646,8 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             // idle: done once every producer has finished and its ring is empty
             bool done = true;
 #pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-                const int e = c * 4 + e4;
+            for (int e4 = 0; e4 < RPR; ++e4) {
+                const int e = c * RPR + e4;
                 const bool fin = ld_volatile(&ctl->epi_done[e]) != 0;
                 __threadfence_block();
                 done = done && fin && ld_volatile(&ctl->ring_tail[e]) == head[e4];
