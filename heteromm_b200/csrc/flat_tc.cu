@@ -489,7 +489,9 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             const float margin = __fmaf_ru(er, ctl->l1max, __fmul_ru(EPS, ctl->tmax));
             const float neg = valid ? -margin : INFINITY;   // rows past the end never pass
             const uint32_t tbase = tmem + (uint32_t)(b * TC_NMAX) + ((uint32_t)(sub * 32) << 16);
-            // one 32-column chunk per tcgen05.wait::ld: measured faster than two
+            // filter: one 32-column chunk per tcgen05.wait::ld (measured faster than
+            // two), kept free of the rare hit path, which would slow every chunk
+            unsigned hitmask = 0;   // warp-uniform: chunks where some pair reaches -margin
 #pragma unroll 1
             for (int c = 0; c < nchunks; ++c) {
                 uint32_t v[32];
@@ -504,26 +506,30 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                 const float m0 = max3_nan(m[0], m[1], m[2]), m1 = max3_nan(m[3], m[4], m[5]);
                 const float m2 = max3_nan(m[6], m[7], m[8]), m3 = max3_nan(m[9], m[10], m[10]);
                 const float mx = max3_nan(max3_nan(m0, m1, m2), m3, m3);
-                const bool hit = !(mx < neg);   // NaN passes
-                if (!__any_sync(0xffffffffu, hit)) continue;
-                // rare: queue the (row, query) pairs of this chunk that reach -margin
+                if (__any_sync(0xffffffffu, !(mx < neg))) hitmask |= 1u << c;   // NaN passes
+            }
+            // rare: re-read the hit chunks and queue their (row, query) pairs
+            while (hitmask != 0u && ring_ok) {
+                const int c = __ffs(hitmask) - 1;
+                hitmask &= hitmask - 1u;
+                uint32_t v[32];
+                tmem_ld_x32(tbase + (uint32_t)(c * 32), v);
+                tmem_wait_ld();
                 uint32_t bits = 0;
-                if (hit) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        bits |= (uint32_t)(!(__uint_as_float(v[j]) < neg)) << j;
-                    const int rem = a.nq - c * 32;
-                    bits &= rem >= 32 ? 0xffffffffu : (1u << rem) - 1u;
-                }
+                for (int j = 0; j < 32; ++j)
+                    bits |= (uint32_t)(!(__uint_as_float(v[j]) < neg)) << j;
+                const int rem = a.nq - c * 32;
+                bits &= rem >= 32 ? 0xffffffffu : (1u << rem) - 1u;
                 while (ring_ok && __any_sync(0xffffffffu, bits != 0)) {
                     const bool has = bits != 0;
                     const int j = has ? __ffs(bits) - 1 : 0;
                     bits &= bits - 1;
                     const unsigned mk = __ballot_sync(0xffffffffu, has);
                     const int n = __popc(mk);
-                    // room in the ring: the rescorer frees slots as it goes (bounded
+                    // room in the ring: the rescorers free slots as they go (bounded
                     // wait; what is queued so far is published first, or the
-                    // rescorer could not see it to free anything)
+                    // rescorers could not see it to free anything)
                     if (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
                         __syncwarp();
                         if (lane == 0) {
@@ -547,7 +553,6 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                             ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
                     tail += n;   // published once per tile, below
                 }
-                if (!ring_ok) break;
             }
             tc_fence_before();
             __syncwarp();
