@@ -63,7 +63,7 @@ constexpr int Q_BOX = TC_NMAX * 128;           // 256 queries x 64 columns = 32 
 constexpr int Q_BYTES = 2 * Q_BOX;             // 64 KiB
 constexpr int FA_BYTES = TC_M * 32;            // threshold-fold A operand: 128 rows x 16 bf16
 constexpr int FB_BYTES = TC_NMAX * 32;         // threshold-fold B operand: 256 rows x 16 bf16
-constexpr int N_EPI_WARPS = 8;                 // two epilogue warpgroups (even / odd tiles)
+constexpr int N_EPI_WARPS = 8;                 // two epilogue warpgroups (query halves)
 constexpr int NTHREADS = 32 * (10 + N_EPI_WARPS);   // + TMA, MMA, 4 rescorers, 4 row-bound warps
 constexpr int RING = 128;                       // pairs per epilogue warp awaiting rescoring
 constexpr int N_RESCORERS = 4;                  // warps 2, 3, 16 and 17
@@ -301,11 +301,12 @@ __device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<v
 //               refolding of thresholds that other CTAs raised
 //   warps 4-7   row bounds: EPS * max|a_r| for each row of a landed tile; with
 //               the MMA commit they free the tile's stage
-//   warps 8-15  epilogue, two warpgroups (even / odd tiles): thread = row
-//               (TMEM lane); a 3-input max tree over the row's 256 folded
-//               scores s~ - t'_q against the row's margin; rows that reach it
-//               are published to the warp's ring for the rescorer warps, so
-//               rescoring never delays the accumulator release
+//   warps 8-15  epilogue, two warpgroups on every tile, each over half of the
+//               256 query columns (measured faster than one warpgroup per
+//               tile): thread = row (TMEM lane); a 3-input max tree over the
+//               row's 128 folded scores s~ - t'_q against the row's margin;
+//               pairs that reach it are published to the warp's ring for the
+//               rescorer warps, so rescoring never delays the accumulator release
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
@@ -331,7 +332,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->acc_full[b], 1);
-            mbar_init(&ctl->acc_empty[b], 4);        // the 4 warps of a warpgroup
+            mbar_init(&ctl->acc_empty[b], N_EPI_WARPS);   // every epilogue warp
         }
         mbar_init(&ctl->b_full, 1);
         for (int e = 0; e < MR_RING; ++e) mbar_init(&ctl->mr_full[e], 4);
@@ -460,14 +461,14 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
     } else if (warp >= 8 && warp < 16) {
         // --------------------------------------------------------- epilogue
         const int ew = warp - 8;            // 0..7
-        const int g = ew >> 2;              // warpgroup: tiles with i % 2 == g
+        const int g = ew >> 2;              // warpgroup: query columns 128g .. 128g + 127
         const int sub = warp & 3;           // TMEM lanes 32*sub .. +31
         const int r = sub * 32 + lane;      // tile row of this thread
-        const int nchunks = (a.nq + 31) / 32;
+        const int nchunks = min((a.nq + 31) / 32, 4 * g + 4);
         int tail = 0;        // pairs this warp has queued in its ring (warp-uniform)
         int published = 0;   // of those, pairs whose tail the rescorers can see
         bool ring_ok = true;
-        for (int i = g; i < my_tiles; i += 2) {
+        for (int i = 0; i < my_tiles; ++i) {
             const int b = i & 1;
             // ---- off the critical path: the tile's row bounds are published
             if (!warp_wait(&ctl->mr_full[i % MR_RING], (i / MR_RING) & 1, abort)) {
@@ -493,7 +494,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             // two), kept free of the rare hit path, which would slow every chunk
             unsigned hitmask = 0;   // warp-uniform: chunks where some pair reaches -margin
 #pragma unroll 1
-            for (int c = 0; c < nchunks; ++c) {
+            for (int c = 4 * g; c < nchunks; ++c) {
                 uint32_t v[32];
                 tmem_ld_x32(tbase + (uint32_t)(c * 32), v);
                 tmem_wait_ld();
