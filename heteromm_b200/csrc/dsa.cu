@@ -99,9 +99,11 @@ __device__ __forceinline__ void dsa_abort(DsaCtrl* c, int* status) {
     atomicExch(&status[0], 1);
 }
 
+template <int H>   // heads: 16, 32 or 64; the epilogue loops unroll fully
 __global__ void __launch_bounds__(D_THREADS, 1)
 dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                   const DsaArgs a) {
+    constexpr int TG2 = NQ / H / 2;   // tokens per epilogue warp and tile
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* Qs = smem;                                  // 2 x 32 KB
@@ -219,7 +221,6 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         const int half = wg >> 1;              // tokens [half * tg / 2, (half + 1) * tg / 2)
         const int sub = warp & 3;              // TMEM lanes 32*sub .. +31
         const int r = sub * 32 + lane;         // key within the tile
-        const int tg2 = a.tg >> 1;
         float* wsm = ctl->wsm[ew];   // per warp: no cross-warp barrier on any path
         int i = 0, g_loaded = -1;
         bool ok = true;
@@ -230,10 +231,10 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 if (g_loaded != g) {
                     // this warp's tokens' weights for group g
                     __syncwarp();
-                    const int n = tg2 * a.H;
-                    const int64_t base = ((int64_t)g * a.tg + half * tg2) * a.H;
+                    const int n = TG2 * H;
+                    const int64_t base = ((int64_t)g * (2 * TG2) + half * TG2) * H;
                     for (int e = lane; e < n; e += 32)
-                        wsm[e] = base + e < a.T * a.H ? a.w[base + e] : 0.0f;
+                        wsm[e] = base + e < a.T * H ? a.w[base + e] : 0.0f;
                     __syncwarp();
                     g_loaded = g;
                 }
@@ -242,35 +243,33 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 tc_fence_after();
                 const int64_t j = (int64_t)t * KT + r;
                 const uint32_t tb = tmem + (uint32_t)(b * NQ) + ((uint32_t)(sub * 32) << 16);
-                for (int tl = 0; tl < tg2; ++tl) {
-                    const int tcol = (half * tg2 + tl) * a.H;
-                    const int64_t tok = (int64_t)g * a.tg + half * tg2 + tl;
-                    const float* wr = wsm + tl * a.H;
+#pragma unroll
+                for (int tl = 0; tl < TG2; ++tl) {
+                    const int tcol = (half * TG2 + tl) * H;
+                    const int64_t tok = (int64_t)g * (2 * TG2) + half * TG2 + tl;
+                    const float* wr = wsm + tl * H;
                     // even / odd heads in the two halves of a packed fp32 pair
-                    // (fma.rn.f32x2: one instruction per two heads)
+                    // (fma.rn.f32x2: one instruction per two heads); one TMEM load
+                    // of up to 32 heads per wait
                     uint64_t s2 = pack_f32x2(0.0f, 0.0f);
-                    for (int c0 = 0; c0 < a.H; c0 += 64) {
-                        uint32_t v[2][32];
-                        tmem_ld_x32(tb + (uint32_t)(tcol + c0), v[0]);
-                        if (c0 + 32 < a.H) tmem_ld_x32(tb + (uint32_t)(tcol + c0 + 32), v[1]);
+#pragma unroll
+                    for (int c0 = 0; c0 < H; c0 += 32) {
+                        constexpr int CW = H < 32 ? H : 32;
+                        uint32_t v[CW];
+                        if constexpr (CW == 32) tmem_ld_x32(tb + (uint32_t)(tcol + c0), v);
+                        else tmem_ld_x16(tb + (uint32_t)(tcol + c0), v);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {
-                            if (c0 + hh * 32 >= a.H) break;
-#pragma unroll
-                            for (int h4 = 0; h4 < 32; h4 += 4) {
-                                if (c0 + hh * 32 + h4 >= a.H) break;   // H = 16: half a load
-                                const float4 w4 =
-                                    *reinterpret_cast<const float4*>(wr + c0 + hh * 32 + h4);
-                                s2 = fma_f32x2(pack_f32x2(w4.x, w4.y),
-                                               pack_f32x2(fmaxf(__uint_as_float(v[hh][h4 + 0]), 0.0f),
-                                                          fmaxf(__uint_as_float(v[hh][h4 + 1]), 0.0f)),
-                                               s2);
-                                s2 = fma_f32x2(pack_f32x2(w4.z, w4.w),
-                                               pack_f32x2(fmaxf(__uint_as_float(v[hh][h4 + 2]), 0.0f),
-                                                          fmaxf(__uint_as_float(v[hh][h4 + 3]), 0.0f)),
-                                               s2);
-                            }
+                        for (int h4 = 0; h4 < CW; h4 += 4) {
+                            const float4 w4 = *reinterpret_cast<const float4*>(wr + c0 + h4);
+                            s2 = fma_f32x2(pack_f32x2(w4.x, w4.y),
+                                           pack_f32x2(fmaxf(__uint_as_float(v[h4 + 0]), 0.0f),
+                                                      fmaxf(__uint_as_float(v[h4 + 1]), 0.0f)),
+                                           s2);
+                            s2 = fma_f32x2(pack_f32x2(w4.z, w4.w),
+                                           pack_f32x2(fmaxf(__uint_as_float(v[h4 + 2]), 0.0f),
+                                                      fmaxf(__uint_as_float(v[h4 + 3]), 0.0f)),
+                                           s2);
                         }
                     }
                     float s_lo, s_hi;
@@ -502,12 +501,13 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
         a.tg = NQ / (int)H;
         a.n_groups = (int)((T + a.tg - 1) / a.tg);
         a.key_tiles = (int)((L + KT - 1) / KT);
-        HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_scores_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+        auto kern = H == 64 ? dsa_scores_kernel<64> : H == 32 ? dsa_scores_kernel<32>
+                                                              : dsa_scores_kernel<16>;
+        HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)D_SMEM));
         const int grid = std::max(1, std::min(device_sm_count(), a.n_groups));
         const ProfileMark pm = profile_begin(st);
-        dsa_scores_kernel<<<grid, D_THREADS, D_SMEM, st>>>(tmK, tmQ, a);
+        kern<<<grid, D_THREADS, D_SMEM, st>>>(tmK, tmQ, a);
         s = check_launch("dsa_scores_kernel");
         profile_end(pm, st);
         if (s != HMM_OK) return s;
