@@ -336,19 +336,83 @@ hmm_status_t make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int bo
     return HMM_OK;
 }
 
-// Exact top-k of each score row for long rows and large k (one block of 256
-// threads per row).  A strided sample of RT_SAMPLE scores gives a lower
+// Exact top-k of each score row for long rows and large k (one block of 512
+// threads per row: twice the loads in flight of 256, at the same shared memory).  A strided sample of RT_SAMPLE scores gives a lower
 // threshold expected to pass ~2k scores; one read of the row gathers every
 // (score key, ~index) composite at or above it into shared memory; a radix
 // select finds the k-th composite among them and the k best are sorted.  If
 // fewer than k scores pass or more than RT_CAP do, the row is flagged
 // (status bit 1) and the caller reruns the general top-k.  The result equals
 // hmm_topk_f32's: best first, ties to the lowest index.
-constexpr int RT_THREADS = 256;
+constexpr int RT_THREADS = 512;
 constexpr int RT_SAMPLE = 4096;
 constexpr int RT_CAP = 8192;
 constexpr int RT_KMAX = 4096;
 constexpr size_t RT_SMEM = sizeof(uint64_t) * (RT_CAP + RT_KMAX);
+
+// Block-wide inclusive scan of one value per thread for NT threads (a
+// multiple of 32, at most 1024); warp_tot holds NT / 32 words.
+template <int NT>
+__device__ __forceinline__ unsigned rt_scan_incl(unsigned v, unsigned* warp_tot) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    if (lane == 31) warp_tot[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        unsigned t = lane < NT / 32 ? warp_tot[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned u = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += u;
+        }
+        if (lane < NT / 32) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const unsigned r = v + (w > 0 ? warp_tot[w - 1] : 0u);
+    __syncthreads();
+    return r;
+}
+
+// block_select_threshold for NT threads (a multiple of 256): the threshold T
+// such that exactly min(k, M) keys are >= T among keys[0, M) (0 if k >= M).
+// sm holds >= 256 + 32 + 3 words.
+template <int NT>
+__device__ __forceinline__ uint64_t rt_select_threshold(const uint64_t* keys, int64_t M, int64_t k,
+                                                        unsigned* sm) {
+    unsigned* hist = sm;          // 256
+    unsigned* wt = sm + 256;      // NT / 32
+    unsigned* res = sm + 288;     // 3
+    if (k >= M) return 0ull;
+    uint64_t prefix = 0, mask = 0;
+    unsigned need = (unsigned)k;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        if (threadIdx.x < 256) hist[threadIdx.x] = 0;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < M; i += NT) {
+            const uint64_t key = keys[i];
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1u);
+        }
+        __syncthreads();
+        const unsigned c = threadIdx.x < 256 ? hist[255 - threadIdx.x] : 0u;
+        const unsigned incl = rt_scan_incl<NT>(c, wt);
+        const unsigned excl = incl - c;
+        if (threadIdx.x < 256 && excl < need && need <= incl) {
+            res[0] = 255 - threadIdx.x; res[1] = excl; res[2] = c;
+        }
+        __syncthreads();
+        const unsigned bucket = res[0], before = res[1], cnt = res[2];
+        need -= before;
+        prefix |= (uint64_t)bucket << shift;
+        mask |= (uint64_t)0xff << shift;
+        __syncthreads();
+        if (cnt == need) break;
+    }
+    return prefix;
+}
 
 __global__ void __launch_bounds__(RT_THREADS) dsa_row_topk_kernel(const float* __restrict__ scores,
                                                                   int64_t L, int k,
@@ -358,7 +422,7 @@ __global__ void __launch_bounds__(RT_THREADS) dsa_row_topk_kernel(const float* _
     extern __shared__ uint64_t rsm[];
     uint64_t* cand = rsm;              // RT_CAP
     uint64_t* best = rsm + RT_CAP;     // RT_KMAX: the sample, then the k best
-    __shared__ unsigned sm[300];
+    __shared__ unsigned sm[320];
     __shared__ int cnt;
     const int64_t t = blockIdx.x;
     const float* row = scores + t * L;
@@ -370,7 +434,7 @@ __global__ void __launch_bounds__(RT_THREADS) dsa_row_topk_kernel(const float* _
     if (threadIdx.x == 0) cnt = 0;
     __syncthreads();
     const int64_t r = min((int64_t)RT_SAMPLE - 1, 2 * (int64_t)k * RT_SAMPLE / L + 32);
-    const uint64_t ts = block_select_threshold(best, RT_SAMPLE, r + 1, sm);
+    const uint64_t ts = rt_select_threshold<RT_THREADS>(best, RT_SAMPLE, r + 1, sm);
     const uint32_t tlo = (uint32_t)(ts >> 32);
     __syncthreads();
 
@@ -412,7 +476,7 @@ __global__ void __launch_bounds__(RT_THREADS) dsa_row_topk_kernel(const float* _
         if (threadIdx.x == 0) atomicOr(&status[1], 1);
         return;
     }
-    const uint64_t T = block_select_threshold(cand, C, k, sm);   // exactly k composites >= T
+    const uint64_t T = rt_select_threshold<RT_THREADS>(cand, C, k, sm);   // exactly k composites >= T
     __syncthreads();
     const int kp = next_pow2(k);
     for (int i = threadIdx.x; i < kp; i += RT_THREADS) best[i] = 0ull;
