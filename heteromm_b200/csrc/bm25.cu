@@ -162,11 +162,14 @@ __global__ void __launch_bounds__(BM_THREADS) bm25_range_kernel(const BmArgs a) 
     const int nd = (int)min((int64_t)BM_RANGE, a.n_docs - d0);
 
     for (int i = threadIdx.x; i < BM_RANGE; i += BM_THREADS) sc[i] = 0.0;
+    __shared__ int32_t raw[BM_MAX_QLEN];
+    if (threadIdx.x < a.qlen) raw[threadIdx.x] = __ldg(a.qterms + (int64_t)q * a.qlen + threadIdx.x);
+    __syncthreads();
     if (threadIdx.x == 0) {
         // the query's distinct in-vocabulary terms, ascending
         int n = 0;
         for (int i = 0; i < a.qlen; ++i) {
-            const int32_t t = a.qterms[(int64_t)q * a.qlen + i];
+            const int32_t t = raw[i];
             if (t < 0 || t >= a.n_terms) continue;
             int j = n;
             while (j > 0 && terms[j - 1] > t) { terms[j] = terms[j - 1]; --j; }
@@ -257,18 +260,31 @@ __global__ void __launch_bounds__(BM_THREADS) bm25_range_kernel(const BmArgs a) 
     }
     __syncthreads();
     const uint64_t tau = tau_s;
+    // candidates: the documents at or above tau (at least kk of them).  When
+    // there are few, ranking them by (key desc, doc asc) settles ties at tau
+    // too; otherwise only those above tau are candidates and the ties at tau
+    // are filled in document order below.
     unsigned g = 0;
 #pragma unroll
-    for (int j = 0; j < BM_PER_THREAD; ++j) g += key[j] > tau;
-    const unsigned g_incl = block_scan_incl_256(g, wt);
-    const unsigned G = wt[7];
+    for (int j = 0; j < BM_PER_THREAD; ++j) g += key[j] >= tau && key[j] != 0ull;
+    unsigned g_incl = block_scan_incl_256(g, wt);
+    unsigned G = wt[7];
+    const bool with_ties = G <= BM_THREADS;
+    if (!with_ties) {
+        __syncthreads();   // every read of wt[7] is done before the scan reuses it
+        g = 0;
+#pragma unroll
+        for (int j = 0; j < BM_PER_THREAD; ++j) g += key[j] > tau;
+        g_incl = block_scan_incl_256(g, wt);
+        G = wt[7];
+    }
     uint64_t* ck = reinterpret_cast<uint64_t*>(arena);
     int32_t* cdoc = reinterpret_cast<int32_t*>(arena + 2048 * sizeof(uint64_t));
     {
         unsigned pos = g_incl - g;
 #pragma unroll
         for (int j = 0; j < BM_PER_THREAD; ++j)
-            if (key[j] > tau) {
+            if (with_ties ? (key[j] >= tau && key[j] != 0ull) : key[j] > tau) {
                 ck[pos] = key[j];
                 cdoc[pos] = threadIdx.x + BM_THREADS * j;
                 ++pos;
@@ -307,7 +323,7 @@ __global__ void __launch_bounds__(BM_THREADS) bm25_range_kernel(const BmArgs a) 
             od[i] = (int32_t)(d0 + cdoc[i]);
         }
     }
-    if ((int)G < kk) {
+    if (!with_ties && (int)G < kk) {
         // the rest from the documents tied at tau, lowest doc first: rank =
         // ties in earlier rows + ties earlier in this row (warp ballots)
         unsigned* cnt = tie_cnt;   // [16 rows][8 warps]
