@@ -724,7 +724,8 @@ def run_dsa(args, rank, world, local):
                 "d2h_bytes_per_step": T * D_TOPK * 4},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None, "kernel": "dsa_scores_kernel",
+                     "frac": achieved / peak, "traffic": traffic_per_launch("dsa_scores_kernel", T),
+                     "kernel": "dsa_scores_kernel",
                      "kernel_ms": kern_ms, "kernel_launches_per_step": k_n / args.steps,
                      "peak_kind": "measured here: cuBLAS e4m3 GEMM 8192^3 (torch._scaled_mm), "
                                   "1 s back to back"},
