@@ -237,7 +237,31 @@ __global__ void __launch_bounds__(BM_THREADS) bm25_range_kernel(const BmArgs a) 
     tmax[warp * 32 + lane] = mx;   // warp w's maxima, descending
     __syncthreads();               // also: every read of the scores is done
     const int kk = min(a.k, nd);
-    if (warp == 0) {
+    if (kk <= 32) {
+        // merge tree: pairs of descending lists -> the top 32 of their union
+        // (the larger of a[l] and b[31 - l] is a bitonic sequence holding it),
+        // sorted again with shuffles; three rounds leave the top 32 in list 0
+        for (int span_w = 1; span_w < 8; span_w <<= 1) {
+            uint64_t v = 0ull;
+            const bool act = (warp % (2 * span_w)) == 0;
+            if (act) {
+                const uint64_t x = tmax[warp * 32 + lane];
+                const uint64_t y = tmax[(warp + span_w) * 32 + (31 - lane)];
+                v = x > y ? x : y;
+#pragma unroll
+                for (int stride = 16; stride > 0; stride >>= 1) {
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, v, stride);
+                    const bool keep_max = (lane & stride) == 0;
+                    v = keep_max ? (o > v ? o : v) : (o < v ? o : v);
+                }
+            }
+            __syncthreads();
+            if (act) tmax[warp * 32 + lane] = v;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) tau_s = kk > 0 ? tmax[kk - 1] : 0ull;
+    } else if (warp == 0) {
+        // larger k: warp 0 merges the 8 sorted lists one element at a time
         int ptr = 0;
         uint64_t head = lane < 8 ? tmax[lane * 32] : 0ull, t = 0ull;
         for (int i = 0; i < kk; ++i) {
