@@ -144,7 +144,8 @@ __device__ __forceinline__ void sort_pairs_desc(uint64_t* key, int32_t* idx, int
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(BM_THREADS) bm25_range_kernel(const BmArgs a) {
+// 5 CTAs per SM: the extra latency hiding outweighs a few spilled registers
+__global__ void __launch_bounds__(BM_THREADS, 5) bm25_range_kernel(const BmArgs a) {
     // fp64 scores of the range; reused as the candidate scratch afterwards
     __shared__ __align__(16) unsigned char arena[BM_RANGE * sizeof(double)];
     __shared__ uint64_t tmax[BM_THREADS];
