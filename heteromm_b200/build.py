@@ -5,6 +5,9 @@
   lib/libheteromm_steps.so  the C++17 heteromm step API (include/heteromm/dev),
                             CPU bodies and GPU adapters (src/*.cpp), linked
                             to the former
+  lib/heteromm_cpp_kernels<ext>  Python bindings of the steps under the names the
+                            reference's pipeline generator calls
+                            (src/py/heteromm_cpp_kernels.cpp, pybind11)
 
 nvcc cross-compiles for sm_100a without a GPU; the built .so files travel with
 the repository snapshot to the GPU machine.
@@ -67,9 +70,35 @@ def build_steps(force: bool = False) -> str:
     return STEPS_LIB
 
 
+def py_kernels_path() -> str:
+    import sysconfig
+    return os.path.join(LIB_DIR, "heteromm_cpp_kernels" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_py_kernels(force: bool = False) -> str:
+    """The pybind11 module heteromm_cpp_kernels, linked to the step library."""
+    import sysconfig
+    try:
+        import pybind11
+    except ImportError:   # bindings are optional; the C ABI and step API stand alone
+        return ""
+    src = os.path.join(PKG, "src", "py", "heteromm_cpp_kernels.cpp")
+    out = py_kernels_path()
+    deps = [src, STEPS_LIB, os.path.join(PKG, "src", "packed.h")] + \
+        glob.glob(os.path.join(INC, "heteromm", "**", "*.h"), recursive=True)
+    if force or _newer(out, deps):
+        cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-fvisibility=hidden",
+               f"-I{pybind11.get_include()}", f"-I{sysconfig.get_paths()['include']}",
+               f"-I{INC}", f"-I{os.path.join(PKG, 'src')}", "-o", out, src, f"-L{LIB_DIR}",
+               "-lheteromm_steps", "-Wl,-rpath,$ORIGIN"]
+        _run(cmd)
+    return out
+
+
 def build(force: bool = False) -> None:
     build_cuda(force)
     build_steps(force)
+    build_py_kernels(force)
 
 
 if __name__ == "__main__":

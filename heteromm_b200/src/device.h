@@ -71,6 +71,13 @@ T* upload(Slot s, const std::vector<T>& host) {
 }
 
 template <typename T>
+T* upload(Slot s, const T* host, size_t n) {
+    T* d = static_cast<T*>(scratch(s).get(sizeof(T) * (n ? n : 1)));
+    if (n) check_cuda(cudaMemcpy(d, host, sizeof(T) * n, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+    return d;
+}
+
+template <typename T>
 void download(std::vector<T>& host, const T* dev) {
     if (!host.empty())
         check_cuda(cudaMemcpy(host.data(), dev, sizeof(T) * host.size(), cudaMemcpyDeviceToHost),

@@ -10,6 +10,7 @@
 #include <numeric>
 
 #include "device.h"
+#include "packed.h"
 #include "heteromm/dev/steps/compute_score.h"
 #include "heteromm/dev/steps/fused_steps/template.h"
 #include "heteromm/dev/steps/memory_retrieval.h"
@@ -76,18 +77,9 @@ void InnerProductCompute::run_gpu_kernel(const data_type::FlatIndexMemory<float>
     const auto& rows = memory.data_ref();
     const auto& q = query.data_ref();
     const size_t n = rows.size(), d = q.size();
-    std::vector<float> out(n);
-    if (n > 0 && d > 0) {
-        const float* dm = gpu::upload(gpu::kMem, gpu::pack_rows(rows, d, "InnerProductCompute"));
-        const float* dq = gpu::upload(gpu::kQuery, q);
-        float* ds = static_cast<float*>(gpu::scratch(gpu::kOut).get(sizeof(float) * n));
-        gpu::check(hmm_ip_score_f32(dm, (int64_t)n, (int64_t)d, dq, 1, ds, nullptr),
-                   "InnerProductCompute GPU kernel");
-        gpu::download(out, ds);
-    } else {
-        std::fill(out.begin(), out.end(), 0.0f);
-    }
-    score.set_data(out);
+    const std::vector<float> packed =
+        n > 0 && d > 0 ? gpu::pack_rows(rows, d, "InnerProductCompute") : std::vector<float>();
+    score.set_data(gpu::ip_scores(packed.data(), n, d, q.data()));
 }
 
 void InnerProductCompute::run_fpga_kernel(const data_type::FlatIndexMemory<float>&,
@@ -178,22 +170,10 @@ void InnerProductTopKRetrieval::run_gpu_kernel(const data_type::FlatIndexMemory<
                                                data_type::TopKIndex& index) {
     const auto& rows = memory.data_ref();
     const auto& q = query.data_ref();
-    const size_t n = rows.size(), d = q.size(), m = std::min(k_, n);
-    std::vector<int> out(m);
-    if (m > 0 && d > 0) {
-        const float* dm = gpu::upload(gpu::kMem, gpu::pack_rows(rows, d, "InnerProductTopK"));
-        const float* dq = gpu::upload(gpu::kQuery, q);
-        int32_t* di = static_cast<int32_t*>(gpu::scratch(gpu::kIdx).get(sizeof(int32_t) * m));
-        const size_t ws = hmm_ip_topk_f32_workspace_size((int64_t)n, (int64_t)d, 1, (int64_t)m);
-        void* w = gpu::scratch(gpu::kWork).get(ws);
-        gpu::check(hmm_ip_topk_f32(dm, (int64_t)n, (int64_t)d, dq, 1, (int64_t)m, di, nullptr,
-                                   0.0f, nullptr, w, ws, nullptr),
-                   "InnerProductTopKRetrieval GPU kernel");
-        gpu::download(out, di);
-    } else if (m > 0) {
-        std::iota(out.begin(), out.end(), 0);   // all scores 0: the lowest indices
-    }
-    index.set_data(out);
+    const size_t n = rows.size(), d = q.size();
+    const std::vector<float> packed =
+        std::min(k_, n) > 0 && d > 0 ? gpu::pack_rows(rows, d, "InnerProductTopK") : std::vector<float>();
+    index.set_data(gpu::ip_topk(packed.data(), n, d, q.data(), k_));
 }
 
 void InnerProductTopKRetrieval::run_fpga_kernel(const data_type::FlatIndexMemory<float>&,
@@ -203,4 +183,42 @@ void InnerProductTopKRetrieval::run_fpga_kernel(const data_type::FlatIndexMemory
 }
 
 }  // namespace step
+}  // namespace heteromm
+
+namespace heteromm {
+namespace gpu {
+
+std::vector<float> ip_scores(const float* rows, size_t n, size_t d, const float* q) {
+    std::vector<float> out(n, 0.0f);
+    if (n > 0 && d > 0) {
+        const float* dm = upload(kMem, rows, n * d);
+        const float* dq = upload(kQuery, q, d);
+        float* ds = static_cast<float*>(scratch(kOut).get(sizeof(float) * n));
+        check(hmm_ip_score_f32(dm, (int64_t)n, (int64_t)d, dq, 1, ds, nullptr),
+              "InnerProductCompute GPU kernel");
+        download(out, ds);
+    }
+    return out;
+}
+
+std::vector<int> ip_topk(const float* rows, size_t n, size_t d, const float* q, size_t k) {
+    const size_t m = std::min(k, n);
+    std::vector<int> out(m);
+    if (m > 0 && d > 0) {
+        const float* dm = upload(kMem, rows, n * d);
+        const float* dq = upload(kQuery, q, d);
+        int32_t* di = static_cast<int32_t*>(scratch(kIdx).get(sizeof(int32_t) * m));
+        const size_t ws = hmm_ip_topk_f32_workspace_size((int64_t)n, (int64_t)d, 1, (int64_t)m);
+        void* w = scratch(kWork).get(ws);
+        check(hmm_ip_topk_f32(dm, (int64_t)n, (int64_t)d, dq, 1, (int64_t)m, di, nullptr, 0.0f,
+                              nullptr, w, ws, nullptr),
+              "InnerProductTopKRetrieval GPU kernel");
+        download(out, di);
+    } else if (m > 0) {
+        std::iota(out.begin(), out.end(), 0);   // all scores 0: the lowest indices
+    }
+    return out;
+}
+
+}  // namespace gpu
 }  // namespace heteromm

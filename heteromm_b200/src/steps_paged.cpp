@@ -7,6 +7,7 @@
 #include <iostream>
 
 #include "device.h"
+#include "packed.h"
 #include "heteromm/dev/steps/apply_memory.h"
 #include "heteromm/dev/steps/build_memory.h"
 
@@ -78,14 +79,9 @@ void PagedKVIndexBuilder::run_gpu_kernel(const data_type::KVCacheData<float>& ra
     }
     const size_t L = keys.size(), D = keys[0].size(), out_dim = weight_.size();
     const size_t pages = (L + (size_t)page_size_ - 1) / (size_t)page_size_;
-    const float* dk = gpu::upload(gpu::kMem, gpu::pack_rows(keys, D, "PagedKVIndexBuilder keys"));
-    const float* dw = gpu::upload(gpu::kAux, gpu::pack_rows(weight_, D, "PagedKVIndexBuilder weight"));
-    float* dout = static_cast<float*>(gpu::scratch(gpu::kOut).get(sizeof(float) * pages * out_dim));
-    gpu::check(hmm_paged_kv_summary_f32(dk, 1, (int64_t)L, (int64_t)D, dw, (int64_t)out_dim,
-                                        page_size_, dout, nullptr),
-               "PagedKVIndexBuilder GPU kernel");
-    std::vector<float> flat(pages * out_dim);
-    gpu::download(flat, dout);
+    const std::vector<float> pk = gpu::pack_rows(keys, D, "PagedKVIndexBuilder keys");
+    const std::vector<float> pw = gpu::pack_rows(weight_, D, "PagedKVIndexBuilder weight");
+    const std::vector<float> flat = gpu::paged_summary(pk.data(), L, D, pw.data(), out_dim, page_size_);
     std::vector<std::vector<float>> result(pages);
     for (size_t p = 0; p < pages; ++p)
         result[p].assign(flat.begin() + (std::ptrdiff_t)(p * out_dim),
@@ -168,20 +164,12 @@ void BlockSparseAttention::run_gpu_kernel(const data_type::KVCacheData<float>& r
         output.set_data(out);
         return;
     }
-    const float* dk = gpu::upload(gpu::kMem, gpu::pack_rows(kv.keys, D, "BlockSparseAttention keys"));
-    const float* dv = gpu::upload(gpu::kAux, gpu::pack_rows(kv.values, D, "BlockSparseAttention values"));
-    const float* dq = gpu::upload(gpu::kQuery, q);
-    const int32_t* db = gpu::upload(gpu::kIdx, blocks);
-    float* dout = static_cast<float*>(gpu::scratch(gpu::kOut).get(sizeof(float) * D));
-    const size_t ws = hmm_paged_workspace_size(1, (int64_t)blocks.size(), (int64_t)page_size_,
-                                               (int64_t)D);
-    void* w = gpu::scratch(gpu::kWork).get(ws);
-    gpu::check(hmm_block_sparse_attention_f32(dq, dk, dv, 1, (int64_t)L, (int64_t)D,
-                                              (int64_t)page_size_, db, (int64_t)blocks.size(),
-                                              dout, w, ws, nullptr),
-               "BlockSparseAttention GPU kernel");
-    gpu::download(out, dout);
-    output.set_data(out);
+    if (kv.values.size() != L)
+        throw std::invalid_argument("BlockSparseAttention: keys and values differ in length");
+    const std::vector<float> pk = gpu::pack_rows(kv.keys, D, "BlockSparseAttention keys");
+    const std::vector<float> pv = gpu::pack_rows(kv.values, D, "BlockSparseAttention values");
+    output.set_data(gpu::block_sparse_attention(pk.data(), pv.data(), L, D, q.data(), blocks.data(),
+                                                blocks.size(), page_size_));
 }
 
 void BlockSparseAttention::run_fpga_kernel(const data_type::KVCacheData<float>&,
@@ -192,4 +180,42 @@ void BlockSparseAttention::run_fpga_kernel(const data_type::KVCacheData<float>&,
 }
 
 }  // namespace step
+}  // namespace heteromm
+
+namespace heteromm {
+namespace gpu {
+
+std::vector<float> paged_summary(const float* keys, size_t L, size_t D, const float* weight,
+                                 size_t out_dim, int page) {
+    const size_t pages = (L + (size_t)page - 1) / (size_t)page;
+    const float* dk = upload(kMem, keys, L * D);
+    const float* dw = upload(kAux, weight, out_dim * D);
+    float* dout = static_cast<float*>(scratch(kOut).get(sizeof(float) * pages * out_dim));
+    check(hmm_paged_kv_summary_f32(dk, 1, (int64_t)L, (int64_t)D, dw, (int64_t)out_dim, page,
+                                   dout, nullptr),
+          "PagedKVIndexBuilder GPU kernel");
+    std::vector<float> flat(pages * out_dim);
+    download(flat, dout);
+    return flat;
+}
+
+std::vector<float> block_sparse_attention(const float* keys, const float* values, size_t L,
+                                          size_t D, const float* q, const int* blocks, size_t nb,
+                                          size_t page) {
+    const float* dk = upload(kMem, keys, L * D);
+    const float* dv = upload(kAux, values, L * D);
+    const float* dq = upload(kQuery, q, D);
+    const int32_t* db = upload(kIdx, reinterpret_cast<const int32_t*>(blocks), nb);
+    float* dout = static_cast<float*>(scratch(kOut).get(sizeof(float) * D));
+    const size_t ws = hmm_paged_workspace_size(1, (int64_t)nb, (int64_t)page, (int64_t)D);
+    void* w = scratch(kWork).get(ws);
+    check(hmm_block_sparse_attention_f32(dq, dk, dv, 1, (int64_t)L, (int64_t)D, (int64_t)page, db,
+                                         (int64_t)nb, dout, w, ws, nullptr),
+          "BlockSparseAttention GPU kernel");
+    std::vector<float> out(D);
+    download(out, dout);
+    return out;
+}
+
+}  // namespace gpu
 }  // namespace heteromm
