@@ -500,6 +500,46 @@ B_DOCS, B_VOCAB, B_MEAN, B_NQ, B_QLEN, B_K = 1_000_000, 30522, 60.0, 1024, 8, 10
 SEED_CORPUS, SEED_BQ = 6, 8
 
 
+def bm25_csr_build(tp, pd, tf, dl, dev, n_docs):
+    """The index's CSR rebuilt from per-document term counts (the reference's
+    term_freq.bin layout): on the device by hmm_bm25_csr_from_docs (inputs
+    resident, CUDA events, checked against the original CSR), and on the host
+    as a NumPy stable sort by term, for comparison."""
+    import numpy as np
+
+    from heteromm_b200.bm25 import csr_from_docs
+    n_terms = tp.size - 1
+    term = np.repeat(np.arange(n_terms, dtype=np.int32), np.diff(tp))
+    order = np.argsort(pd, kind="stable")              # document major
+    terms_dm = term[order]
+    counts_dm = tf[order].astype(np.uint32)
+    doc_ptr = np.zeros(n_docs + 1, np.int64)
+    doc_ptr[1:] = np.cumsum(np.bincount(pd, minlength=n_docs))
+    t0 = time.perf_counter()
+    o2 = np.argsort(terms_dm, kind="stable")
+    h_doc = np.repeat(np.arange(n_docs, dtype=np.int32), np.diff(doc_ptr))[o2]
+    h_tf = counts_dm[o2].astype(np.uint16)
+    h_ptr = np.zeros(n_terms + 1, np.int64)
+    h_ptr[1:] = np.cumsum(np.bincount(terms_dm, minlength=n_terms))
+    host_s = time.perf_counter() - t0
+    d = [torch.from_numpy(a).to(dev) for a in (doc_ptr, terms_dm, counts_dm.view(np.int32))]
+    out = csr_from_docs(*d, n_terms, dev)   # warm-up
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        out = csr_from_docs(*d, n_terms, dev)
+    e1.record()
+    torch.cuda.synchronize()
+    ok = (np.array_equal(out[0].cpu().numpy(), tp) and np.array_equal(out[1].cpu().numpy(), pd)
+          and np.array_equal(out[2].cpu().numpy().view(np.uint16), tf)
+          and np.array_equal(out[3].cpu().numpy(), dl) and np.array_equal(h_ptr, tp)
+          and np.array_equal(h_doc, pd) and np.array_equal(h_tf, tf))
+    return {"entries": int(doc_ptr[-1]), "device_ms": e0.elapsed_time(e1) / reps,
+            "host_numpy_s": host_s, "equal": bool(ok)}
+
+
 def run_bm25(args, rank, world, local):
     """BM25 top-10 over a 1M-doc CSR index (Zipf(1.1) terms over 30,522,
     Poisson(60) lengths), 1,024 queries of 8 distinct Zipf terms.  Queries are
@@ -520,6 +560,7 @@ def run_bm25(args, rank, world, local):
     index = hmm.BM25Index(tp, pd, tf, dl, dev)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
+    csr_build = bm25_csr_build(tp, pd, tf, dl, dev, n_docs) if rank == 0 else None
     q = torch.from_numpy(q_np).to(dev)
     for _ in range(args.warmup):
         index.topk(q, B_K)
@@ -579,6 +620,7 @@ def run_bm25(args, rank, world, local):
                                f"{n_q} queries x {B_QLEN} terms, top-{B_K}",
                    "parallelism": f"query split x{world}",
                    "postings_per_step": post, "index_prepare_s": build_s,
+                   "csr_from_docs": csr_build,
                    "l2": "inputs larger than L2 (postings read per step > 126 MB)"},
         "e2e": {"value": n_q / (e2e_ms * 1e-3), "unit": "queries/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": per * B_QLEN * 4,

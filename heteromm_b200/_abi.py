@@ -58,6 +58,8 @@ SIGNATURES = {
     "hmm_bm25_prepare": (C.c_int, [_P, _P, _P, _I, _P, _I, _P, C.c_double, _P, _P, _P, _S,
                                    _P]),
     "hmm_bm25_topk_workspace_size": (_S, [_I, _I, _I]),
+    "hmm_bm25_csr_workspace_size": (_S, [_I, _I]),
+    "hmm_bm25_csr_from_docs": (C.c_int, [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _S, _P]),
     "hmm_bm25_topk_csr": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P, _P, _S,
                                     _P]),
     "hmm_indexer_workspace_size": (_S, [_I, _I]),

@@ -304,6 +304,25 @@ hmm_status_t hmm_bm25_topk_csr(const int32_t* post_doc, const double* impact,
                                int64_t qlen, int64_t k, int32_t* out_idx, double* out_scores,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* The inverted index built on the device from per-document term counts
+ * (replaces the CPU index build behind BuildMemory<TextDBData, BM25IndexMemory>,
+ * steps/build_memory.h:183-247, over the reference's term_freq.bin layout,
+ * rag_test/export_bm25_data.py:13-27): document d's entries are
+ * [doc_ptr[d], doc_ptr[d+1]) of terms (vocabulary index in [0, n_terms)) and
+ * counts (in [1, 65535]), each term at most once per document.  Writes
+ * term_ptr [n_terms+1] int64, post_doc / post_tf [doc_ptr[n_docs]] with the
+ * documents of every term ascending, and doc_len [n_docs] = the sum of each
+ * document's counts.  Waits for `stream` to check the inputs: bad doc_ptr or
+ * counts give HMM_ERR_INVALID, a term outside the vocabulary HMM_ERR_BOUNDS.
+ * Workspace: hmm_bm25_csr_workspace_size bytes (4 B per term per 1,024
+ * documents). */
+size_t hmm_bm25_csr_workspace_size(int64_t n_docs, int64_t n_terms);
+hmm_status_t hmm_bm25_csr_from_docs(const int64_t* doc_ptr, const int32_t* terms,
+                                    const uint32_t* counts, int64_t n_docs, int64_t n_terms,
+                                    int64_t* term_ptr, int32_t* post_doc, uint16_t* post_tf,
+                                    int32_t* doc_len, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
 /* ------------------------------------------------------------ indexers
  * int16 sparse-attention indexers of one index head (the CPU references in
  * kernels/lserve/indexer_lserve_tb.cpp:20-92,
