@@ -43,6 +43,9 @@ SIGNATURES = {
     "hmm_paged_workspace_size": (_S, [_I, _I, _I, _I]),
     "hmm_paged_kv_summary_bf16": (C.c_int, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S,
                                             _P]),
+    "hmm_paged_kv_minmax_bf16": (C.c_int, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _S,
+                                           _P]),
+    "hmm_block_select_minmax": (C.c_int, [_P, _P, _I, _I, _I, _I, _P, _P]),
     "hmm_block_pages": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _P]),
     "hmm_block_sparse_attention_bf16": (C.c_int, [_P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _I,
                                                   _P, _I, _P, _P, _S, _P]),

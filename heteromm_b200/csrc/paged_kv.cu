@@ -165,6 +165,78 @@ __global__ void __launch_bounds__(256) paged_summary_kernel(PagedCache c, int bl
     }
 }
 
+// Min/max page summaries (the reference's MinMaxIndexMemory, types/memory.h:
+// 127-230: per block a min vector then a max vector): per (sequence, block) and
+// column, the smallest and largest key of the block's tokens (fminf / fmaxf:
+// NaN ignored unless all are).  Same walk as paged_summary_kernel; out is
+// [unit][2][D].
+template <int NG>
+__global__ void __launch_bounds__(256) paged_minmax_kernel(PagedCache c, int block_tokens,
+                                                           int n_blocks, int64_t n_units,
+                                                           float* __restrict__ out,
+                                                           int* status) {
+    constexpr int U = 16 / NG;
+    const int64_t unit = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (unit >= n_units) return;
+    const int s = (int)(unit / n_blocks), b = (int)(unit % n_blocks);
+    const int t0 = b * block_tokens;
+    const int t1 = min(t0 + block_tokens, c.seq_len);
+    const int ng = c.D >> 2;
+    float mn[NG][4], mx[NG][4];
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            mn[g][i] = __int_as_float(0x7fc00000);   // NaN: replaced by the first key
+            mx[g][i] = __int_as_float(0x7fc00000);
+        }
+    bool bad = false;
+    for (int t = t0, n = 0; t < t1; t += n) {
+        const uint16_t* row = token_row(c, c.pages, s, t, status);
+        if (!row) { bad = true; break; }
+        n = min(c.page_tokens - (t % c.page_tokens), t1 - t);
+        for (int j0 = 0; j0 < n; j0 += U) {
+            uint2 v[U][NG];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int g = 0; g < NG; ++g) {
+                    const int gi = lane + 32 * g;
+                    v[u][g] = (j0 + u < n && gi < ng)
+                                  ? __ldg(reinterpret_cast<const uint2*>(row + (int64_t)(j0 + u) * c.D) + gi)
+                                  : make_uint2(0u, 0u);
+                }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                if (j0 + u >= n) break;
+#pragma unroll
+                for (int g = 0; g < NG; ++g) {
+                    const float x[4] = {bf16_lo(v[u][g].x), bf16_hi(v[u][g].x),
+                                        bf16_lo(v[u][g].y), bf16_hi(v[u][g].y)};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        mn[g][i] = fminf(mn[g][i], x[i]);
+                        mx[g][i] = fmaxf(mx[g][i], x[i]);
+                    }
+                }
+            }
+        }
+    }
+    float* omin = out + unit * 2 * c.D;
+    float* omax = omin + c.D;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+        const int gi = lane + 32 * g;
+        if (gi < ng) {
+            reinterpret_cast<float4*>(omin)[gi] =
+                bad ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(mn[g][0], mn[g][1], mn[g][2], mn[g][3]);
+            reinterpret_cast<float4*>(omax)[gi] =
+                bad ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(mx[g][0], mx[g][1], mx[g][2], mx[g][3]);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ a-7
 // Logical pages [b*ppb, (b+1)*ppb) of each selected block b, in selection
 // order, clipped to [0, pages_per_seq), through the page table; one block per
@@ -604,6 +676,10 @@ __global__ void bsa_combine_kernel(const float* __restrict__ part, int splits, i
 // Per sequence: score each block summary against q (fp32, d ascending,
 // fl(fl(S*q) + acc), inner_product_compute.cpp:23-29), then keep the best
 // `top` (topk_retrieval.cpp:13-31; ties to the lowest block id).
+// MINMAX: summ rows are [block][2][D] (min, max) and a block's score is the
+// upper bound of q.k over its keys, sum_j max(q_j * min_j, q_j * max_j) in j
+// order; otherwise rows are [block][D] and the score is q . summary.
+template <bool MINMAX>
 __global__ void __launch_bounds__(256) block_select_kernel(const float* __restrict__ summ,
                                                            int n_blocks, int D,
                                                            const uint16_t* __restrict__ q,
@@ -616,10 +692,25 @@ __global__ void __launch_bounds__(256) block_select_kernel(const float* __restri
     for (int d = threadIdx.x; d < D; d += blockDim.x)
         qf[d] = bf16_bits_to_f32(q[(int64_t)s * D + d]);
     __syncthreads();
-    const float* S = summ + (int64_t)s * n_blocks * D;
+    const float* S = summ + (int64_t)s * n_blocks * D * (MINMAX ? 2 : 1);
     for (int b = threadIdx.x; b < n2; b += blockDim.x) {
         uint64_t key = 0ull;
-        if (b < n_blocks) {
+        if (MINMAX && b < n_blocks) {
+            const float4* lo = reinterpret_cast<const float4*>(S + (int64_t)b * 2 * D);
+            const float4* hi = lo + (D >> 2);
+            float acc = 0.0f;
+            for (int d4 = 0; d4 < (D >> 2); ++d4) {
+                const float4 a = __ldg(lo + d4), z = __ldg(hi + d4);
+                const float av[4] = {a.x, a.y, a.z, a.w}, zv[4] = {z.x, z.y, z.z, z.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float l = __fmul_rn(qf[4 * d4 + i], av[i]);
+                    const float h = __fmul_rn(qf[4 * d4 + i], zv[i]);
+                    acc = __fadd_rn(acc, l > h ? l : h);
+                }
+            }
+            key = make_cand(f32_key(acc), (uint32_t)b);
+        } else if (b < n_blocks) {
             const float4* r = reinterpret_cast<const float4*>(S + (int64_t)b * D);
             float acc = 0.0f;
             for (int d4 = 0; d4 < (D >> 2); ++d4) {
@@ -844,6 +935,63 @@ extern "C" hmm_status_t hmm_paged_kv_summary_bf16(const uint16_t* k_pages, int64
     return read_status(status, st, "hmm_paged_kv_summary_bf16");
 }
 
+extern "C" hmm_status_t hmm_paged_kv_minmax_bf16(const uint16_t* k_pages, int64_t n_pages,
+                                                 const int32_t* page_table, int64_t n_seq,
+                                                 int64_t pages_per_seq, int64_t seq_len,
+                                                 int64_t page_tokens, int64_t block_tokens,
+                                                 int64_t D, float* out, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+    hmm_status_t s = check_cache(k_pages, n_pages, page_table, n_seq, pages_per_seq, seq_len,
+                                 page_tokens, D);
+    if (s != HMM_OK) return s;
+    HMM_REQUIRE(block_tokens >= 1, "block_tokens must be >= 1");
+    if (n_seq == 0 || seq_len == 0) return HMM_OK;
+    HMM_REQUIRE(out, "out is null");
+    HMM_REQUIRE(workspace && workspace_bytes >= 256, "workspace must hold >= 256 bytes");
+    HMM_REQUIRE((reinterpret_cast<uintptr_t>(out) % 16) == 0, "out must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int* status = static_cast<int*>(workspace);
+    HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
+    PagedCache c{k_pages, page_table, n_pages, (int)pages_per_seq, (int)seq_len,
+                 (int)page_tokens, (int)D, false};
+    const int n_blocks = (int)((seq_len + block_tokens - 1) / block_tokens);
+    const int64_t units = n_seq * n_blocks;
+    const unsigned grid = (unsigned)((units + 7) / 8);
+    if (D <= 128)
+        paged_minmax_kernel<1><<<grid, 256, 0, st>>>(c, (int)block_tokens, n_blocks, units, out,
+                                                      status);
+    else if (D <= 256)
+        paged_minmax_kernel<2><<<grid, 256, 0, st>>>(c, (int)block_tokens, n_blocks, units, out,
+                                                      status);
+    else
+        paged_minmax_kernel<4><<<grid, 256, 0, st>>>(c, (int)block_tokens, n_blocks, units, out,
+                                                      status);
+    s = check_launch("paged_minmax_kernel");
+    if (s != HMM_OK) return s;
+    return read_status(status, st, "hmm_paged_kv_minmax_bf16");
+}
+
+extern "C" hmm_status_t hmm_block_select_minmax(const uint16_t* q, const float* minmax,
+                                                int64_t n_seq, int64_t n_blocks, int64_t D,
+                                                int64_t top_blocks, int32_t* out_blocks,
+                                                void* stream) {
+    HMM_REQUIRE(n_seq >= 0 && n_seq <= 65535, "n_seq must be in [0, 65535]");
+    HMM_REQUIRE(n_blocks >= 0 && n_blocks <= 16384, "n_blocks must be in [0, 16384]");
+    HMM_REQUIRE(D >= 4 && D % 4 == 0 && D <= 1024, "D must be a multiple of 4 in [4, 1024]");
+    HMM_REQUIRE(top_blocks >= 1, "top_blocks must be >= 1");
+    if (n_seq == 0) return HMM_OK;
+    HMM_REQUIRE(q && out_blocks && (minmax || n_blocks == 0), "null pointer");
+    HMM_REQUIRE((reinterpret_cast<uintptr_t>(minmax) % 16) == 0, "minmax must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int n2 = next_pow2((int)std::max<int64_t>(n_blocks, 1));
+    const size_t ssm = sizeof(uint64_t) * n2 + sizeof(float) * D;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel<true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm));
+    block_select_kernel<true><<<(unsigned)n_seq, 256, ssm, st>>>(minmax, (int)n_blocks, (int)D, q,
+                                                                 (int)top_blocks, out_blocks);
+    return check_launch("block_select_kernel");
+}
+
 extern "C" hmm_status_t hmm_block_pages(const int32_t* page_table, int64_t n_seq,
                                         int64_t pages_per_seq, const int32_t* blocks,
                                         int64_t n_sel, int64_t pages_per_block,
@@ -951,10 +1099,10 @@ extern "C" hmm_status_t hmm_block_sparse_decode_bf16_async(
     int32_t* sel = out_blocks ? out_blocks : reinterpret_cast<int32_t*>(ws + sel_off);
     const int n2 = next_pow2((int)n_blocks);
     const size_t ssm = sizeof(uint64_t) * n2 + sizeof(float) * D;
-    HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel,
+    HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel<false>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm));
-    block_select_kernel<<<(unsigned)n_seq, 256, ssm, st>>>(summaries, (int)n_blocks, (int)D, q,
-                                                           (int)top_blocks, sel);
+    block_select_kernel<false><<<(unsigned)n_seq, 256, ssm, st>>>(summaries, (int)n_blocks, (int)D,
+                                                                  q, (int)top_blocks, sel);
     s = check_launch("block_select_kernel");
     if (s != HMM_OK) return s;
     // slots past the number of blocks hold -1: treat them as absent by

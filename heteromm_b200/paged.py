@@ -54,6 +54,33 @@ def paged_kv_summary_bf16(k_pages: torch.Tensor, page_table: torch.Tensor, seq_l
     return out
 
 
+def paged_kv_minmax_bf16(k_pages: torch.Tensor, page_table: torch.Tensor, seq_len: int,
+                         block_tokens: int) -> torch.Tensor:
+    """[n_seq, n_blocks, 2, D] fp32 per-block min and max keys (MinMaxIndexMemory:
+    for every block its min vector, then its max vector)."""
+    n_pages, pt, D, n_seq, pps = _cache_dims(k_pages, page_table)
+    nb = (seq_len + block_tokens - 1) // block_tokens
+    out = torch.empty((n_seq, nb, 2, D), dtype=torch.float32, device=k_pages.device)
+    ws = workspace(load().hmm_paged_workspace_size(n_seq, 0, block_tokens, D), k_pages.device)
+    call("hmm_paged_kv_minmax_bf16", k_pages.data_ptr(), n_pages, page_table.data_ptr(), n_seq,
+         pps, seq_len, pt, block_tokens, D, out.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    return out
+
+
+def block_select_minmax(q: torch.Tensor, minmax: torch.Tensor, top: int) -> torch.Tensor:
+    """[n_seq, top] int32: the blocks with the largest upper bound of q.k over their
+    keys, sum_j max(q_j min_j, q_j max_j); best first, ties to the lower block, -1
+    past the block count.  q [n_seq, D] bf16 bits (int16), minmax
+    [n_seq, n_blocks, 2, D] fp32."""
+    _check(q, torch.int16, "q")
+    _check(minmax, torch.float32, "minmax")
+    n_seq, nb, _, D = minmax.shape
+    out = torch.empty((n_seq, top), dtype=torch.int32, device=q.device)
+    call("hmm_block_select_minmax", q.data_ptr(), minmax.data_ptr(), n_seq, nb, D, top,
+         out.data_ptr(), _stream())
+    return out
+
+
 def block_pages(page_table: torch.Tensor, blocks: torch.Tensor, pages_per_block: int):
     """(pages [n_seq, n_sel*ppb] int32, -1 padded; counts [n_seq] int32)."""
     _check(page_table, torch.int32, "page_table")

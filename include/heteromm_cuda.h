@@ -187,6 +187,27 @@ hmm_status_t hmm_paged_kv_summary_bf16(const uint16_t* k_pages, int64_t n_pages,
                                        float* out, void* workspace, size_t workspace_bytes,
                                        void* stream);
 
+/* Min/max page summaries of the paged key cache, the reference's
+ * MinMaxIndexMemory (types/memory.h:127-230; no reference step computes them):
+ * out [n_seq][ceil(seq_len/block_tokens)][2][D] fp32, per block and column the
+ * smallest then the largest key (fminf / fmaxf).  Arguments and checks as
+ * hmm_paged_kv_summary_bf16. */
+hmm_status_t hmm_paged_kv_minmax_bf16(const uint16_t* k_pages, int64_t n_pages,
+                                      const int32_t* page_table, int64_t n_seq,
+                                      int64_t pages_per_seq, int64_t seq_len,
+                                      int64_t page_tokens, int64_t block_tokens, int64_t D,
+                                      float* out, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
+/* The min/max-bound block selector over those summaries: per sequence, the
+ * top_blocks blocks with the largest u_b = sum_j max(q_j * min_bj, q_j * max_bj)
+ * (j ascending, each product rounded before the add), an upper bound of q.k for
+ * every key of block b; best first, ties to the lower block, -1 past n_blocks.
+ * q [n_seq][D] bf16; the selection feeds hmm_block_sparse_attention_bf16. */
+hmm_status_t hmm_block_select_minmax(const uint16_t* q, const float* minmax, int64_t n_seq,
+                                     int64_t n_blocks, int64_t D, int64_t top_blocks,
+                                     int32_t* out_blocks, void* stream);
+
 /* Physical pages of the selected blocks (the reference has no page table; this
  * is the paged form of the token list of block_sparse_attention.cpp:53-63):
  * for each sequence, logical pages [b*pages_per_block, (b+1)*pages_per_block)

@@ -306,6 +306,59 @@ int64_t orc_block_mean_f32(const float* keys, int64_t L, int64_t D, int64_t page
     return pages;
 }
 
+/* Min/max page summaries of the reference's MinMaxIndexMemory
+ * (types/memory.h:127-230: for every block a min vector and a max vector,
+ * stored min then max): per block of `page_size` tokens and column, the
+ * smallest and the largest key (fminf / fmaxf: NaN ignored unless all are). */
+int64_t orc_block_minmax_f32(const float* keys, int64_t L, int64_t D, int64_t page_size,
+                             float* out) {
+    int64_t pages, p;
+    if (L == 0 || D == 0 || page_size <= 0) return 0;
+    pages = (L + page_size - 1) / page_size;
+    for (p = 0; p < pages; ++p) {
+        int64_t start = p * page_size;
+        int64_t end = start + page_size < L ? start + page_size : L;
+        for (int64_t d = 0; d < D; ++d) {
+            float mn = keys[start * D + d], mx = mn;
+            for (int64_t t = start + 1; t < end; ++t) {
+                mn = fminf(mn, keys[t * D + d]);
+                mx = fmaxf(mx, keys[t * D + d]);
+            }
+            out[(2 * p) * D + d] = mn;
+            out[(2 * p + 1) * D + d] = mx;
+        }
+    }
+    return pages;
+}
+
+/* Top-`top` blocks by the upper bound of q.k over each block's keys,
+ * u_b = sum_j max(q_j * min_bj, q_j * max_bj), j ascending, each product
+ * rounded before the add; best first, ties to the lower block, -1 past nb. */
+void orc_block_select_minmax(const float* q, const float* minmax, int64_t nb, int64_t D,
+                             int64_t top, int32_t* out) {
+    float* u = (float*)malloc(sizeof(float) * (size_t)(nb ? nb : 1));
+    for (int64_t b = 0; b < nb; ++b) {
+        float acc = 0.0f;
+        for (int64_t j = 0; j < D; ++j) {
+            const float lo = q[j] * minmax[(2 * b) * D + j];
+            const float hi = q[j] * minmax[(2 * b + 1) * D + j];
+            acc = acc + (lo > hi ? lo : hi);
+        }
+        u[b] = acc;
+    }
+    for (int64_t i = 0; i < top; ++i) {
+        int64_t best = -1;
+        for (int64_t b = 0; b < nb; ++b) {
+            int taken = 0;
+            for (int64_t j = 0; j < i; ++j) taken |= out[j] == (int32_t)b;
+            if (taken) continue;
+            if (best < 0 || orc_f32_key(u[b]) > orc_f32_key(u[best])) best = b;
+        }
+        out[i] = (int32_t)best;
+    }
+    free(u);
+}
+
 /* ------------------------------------------------------------------ a-6 */
 
 /* block_sparse_attention.cpp:50-123 */

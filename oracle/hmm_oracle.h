@@ -84,6 +84,10 @@ int64_t orc_paged_kv_summary_f32(const float* keys, int64_t L, int64_t D,
  * exactly: 1*x + 0*y summed in order is x). */
 int64_t orc_block_mean_f32(const float* keys, int64_t L, int64_t D, int64_t page_size,
                            float* out);
+int64_t orc_block_minmax_f32(const float* keys, int64_t L, int64_t D, int64_t page_size,
+                             float* out);
+void orc_block_select_minmax(const float* q, const float* minmax, int64_t nb, int64_t D,
+                             int64_t top, int32_t* out);
 
 /* a-6  steps/example_kernel/block_sparse_attention.cpp:21-126
  * keys/values [L][D], blocks [nb] (block ids, top-k order), q [D]; out [D]. */

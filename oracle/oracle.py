@@ -194,6 +194,24 @@ def block_mean_f32(keys, page_size):
     return out
 
 
+def block_minmax_f32(keys, page_size):
+    """[pages][2][D]: per block the min row then the max row (MinMaxIndexMemory)."""
+    keys = _c(keys, np.float32)
+    L, D = keys.shape
+    out = np.empty(((L + page_size - 1) // page_size, 2, D), np.float32)
+    lib().orc_block_minmax_f32(_p(keys), _I(L), _I(D), _I(page_size), _p(out))
+    return out
+
+
+def block_select_minmax(q, minmax, top):
+    """Top blocks by the min/max upper bound of q.k (-1 past the block count)."""
+    q = _c(q, np.float32); mm = _c(minmax, np.float32)
+    nb, _, D = mm.shape
+    out = np.empty(top, np.int32)
+    lib().orc_block_select_minmax(_p(q), _p(mm), _I(nb), _I(D), _I(top), _p(out))
+    return out
+
+
 def block_sparse_attention_f32(keys, values, blocks, q, page_size):
     keys = _c(keys, np.float32); values = _c(values, np.float32)
     blocks = _c(blocks, np.int32); q = _c(q, np.float32)
