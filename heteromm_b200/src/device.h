@@ -84,6 +84,38 @@ void download(std::vector<T>& host, const T* dev) {
                    "cudaMemcpy D2H");
 }
 
+// Device copies of recently used memories, per thread: up to kMirrors,
+// keyed by the memory's generation (renewed by every change of its contents)
+// and the packed shape; the least recently used is replaced.  A hit skips the
+// packing and the upload of an unchanged memory.
+struct Mirror {
+    uint64_t gen = 0;
+    size_t n = 0, d = 0;
+    uint64_t used = 0;
+    DeviceBuffer buf;
+};
+constexpr int kMirrors = 4;
+
+// The mirror of (gen, n, d); *hit tells whether it already holds the data.
+inline Mirror& mirror(uint64_t gen, size_t n, size_t d, bool* hit) {
+    thread_local Mirror m[kMirrors];
+    thread_local uint64_t clock = 0;
+    ++clock;
+    for (auto& x : m)
+        if (x.gen != 0 && x.gen == gen && x.n == n && x.d == d) {
+            x.used = clock;
+            *hit = true;
+            return x;
+        }
+    Mirror* lru = &m[0];
+    for (auto& x : m)
+        if (x.used < lru->used) lru = &x;
+    lru->gen = 0;   // claimed; valid once the caller has uploaded
+    lru->used = clock;
+    *hit = false;
+    return *lru;
+}
+
 // Rows of a vector-of-vectors packed into one row-major array; every row
 // must have `cols` values.
 template <typename T>

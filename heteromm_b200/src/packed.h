@@ -19,6 +19,10 @@ std::vector<float> ip_scores(const float* rows, size_t n, size_t d, const float*
 // index (0, 1, ... if d is 0: every score is 0).
 std::vector<int> ip_topk(const float* rows, size_t n, size_t d, const float* q, size_t k);
 
+// The same two with the rows already on the device (n, d > 0).
+std::vector<float> ip_scores_dev(const float* d_rows, size_t n, size_t d, const float* q);
+std::vector<int> ip_topk_dev(const float* d_rows, size_t n, size_t d, const float* q, size_t k);
+
 // Page summaries [ceil(L/page)][out_dim] (flat) of keys[L][D] projected by
 // weight[out_dim][D]; the caller has checked L, D, out_dim and page > 0.
 std::vector<float> paged_summary(const float* keys, size_t L, size_t D, const float* weight,

@@ -53,6 +53,28 @@ std::vector<unsigned long long> cpu_bitmap(const std::vector<float>& s, float th
     return bm;
 }
 
+// The memory's first d columns on the device: its cached mirror when the
+// memory is unchanged since an earlier call on this thread, else packed and
+// uploaded into one.
+const float* device_rows(const data_type::FlatIndexMemory<float>& memory, size_t d,
+                         const char* what) {
+    const auto& rows = memory.data_ref();
+    const size_t n = rows.size();
+    bool hit = false;
+    gpu::Mirror& m = gpu::mirror(memory.generation(), n, d, &hit);
+    float* dev = static_cast<float*>(m.buf.get(sizeof(float) * n * d));
+    if (!hit) {
+        const std::vector<float> packed = gpu::pack_rows(rows, d, what);
+        gpu::check_cuda(cudaMemcpy(dev, packed.data(), sizeof(float) * n * d,
+                                   cudaMemcpyHostToDevice),
+                        "cudaMemcpy H2D");
+        m.gen = memory.generation();
+        m.n = n;
+        m.d = d;
+    }
+    return dev;
+}
+
 void fpga_stub(const char* step) {
     std::clog << "[" << step << "] FPGA kernel not implemented. exiting." << std::endl;
 }
@@ -77,9 +99,11 @@ void InnerProductCompute::run_gpu_kernel(const data_type::FlatIndexMemory<float>
     const auto& rows = memory.data_ref();
     const auto& q = query.data_ref();
     const size_t n = rows.size(), d = q.size();
-    const std::vector<float> packed =
-        n > 0 && d > 0 ? gpu::pack_rows(rows, d, "InnerProductCompute") : std::vector<float>();
-    score.set_data(gpu::ip_scores(packed.data(), n, d, q.data()));
+    if (n == 0 || d == 0) {
+        score.set_data(std::vector<float>(n, 0.0f));
+        return;
+    }
+    score.set_data(gpu::ip_scores_dev(device_rows(memory, d, "InnerProductCompute"), n, d, q.data()));
 }
 
 void InnerProductCompute::run_fpga_kernel(const data_type::FlatIndexMemory<float>&,
@@ -171,9 +195,11 @@ void InnerProductTopKRetrieval::run_gpu_kernel(const data_type::FlatIndexMemory<
     const auto& rows = memory.data_ref();
     const auto& q = query.data_ref();
     const size_t n = rows.size(), d = q.size();
-    const std::vector<float> packed =
-        std::min(k_, n) > 0 && d > 0 ? gpu::pack_rows(rows, d, "InnerProductTopK") : std::vector<float>();
-    index.set_data(gpu::ip_topk(packed.data(), n, d, q.data(), k_));
+    if (std::min(k_, n) == 0 || d == 0) {
+        index.set_data(gpu::ip_topk(nullptr, n, d, q.data(), k_));   // no device work
+        return;
+    }
+    index.set_data(gpu::ip_topk_dev(device_rows(memory, d, "InnerProductTopK"), n, d, q.data(), k_));
 }
 
 void InnerProductTopKRetrieval::run_fpga_kernel(const data_type::FlatIndexMemory<float>&,
@@ -189,23 +215,31 @@ namespace heteromm {
 namespace gpu {
 
 std::vector<float> ip_scores(const float* rows, size_t n, size_t d, const float* q) {
+    if (n == 0 || d == 0) return std::vector<float>(n, 0.0f);
+    return ip_scores_dev(upload(kMem, rows, n * d), n, d, q);
+}
+
+std::vector<float> ip_scores_dev(const float* dm, size_t n, size_t d, const float* q) {
     std::vector<float> out(n, 0.0f);
-    if (n > 0 && d > 0) {
-        const float* dm = upload(kMem, rows, n * d);
-        const float* dq = upload(kQuery, q, d);
-        float* ds = static_cast<float*>(scratch(kOut).get(sizeof(float) * n));
-        check(hmm_ip_score_f32(dm, (int64_t)n, (int64_t)d, dq, 1, ds, nullptr),
-              "InnerProductCompute GPU kernel");
-        download(out, ds);
-    }
+    const float* dq = upload(kQuery, q, d);
+    float* ds = static_cast<float*>(scratch(kOut).get(sizeof(float) * n));
+    check(hmm_ip_score_f32(dm, (int64_t)n, (int64_t)d, dq, 1, ds, nullptr),
+          "InnerProductCompute GPU kernel");
+    download(out, ds);
     return out;
 }
 
 std::vector<int> ip_topk(const float* rows, size_t n, size_t d, const float* q, size_t k) {
+    if (std::min(k, n) > 0 && d > 0) return ip_topk_dev(upload(kMem, rows, n * d), n, d, q, k);
+    std::vector<int> out(std::min(k, n));
+    std::iota(out.begin(), out.end(), 0);   // all scores 0: the lowest indices
+    return out;
+}
+
+std::vector<int> ip_topk_dev(const float* dm, size_t n, size_t d, const float* q, size_t k) {
     const size_t m = std::min(k, n);
     std::vector<int> out(m);
-    if (m > 0 && d > 0) {
-        const float* dm = upload(kMem, rows, n * d);
+    {
         const float* dq = upload(kQuery, q, d);
         int32_t* di = static_cast<int32_t*>(scratch(kIdx).get(sizeof(int32_t) * m));
         const size_t ws = hmm_ip_topk_f32_workspace_size((int64_t)n, (int64_t)d, 1, (int64_t)m);
@@ -214,8 +248,6 @@ std::vector<int> ip_topk(const float* rows, size_t n, size_t d, const float* q, 
                               nullptr, w, ws, nullptr),
               "InnerProductTopKRetrieval GPU kernel");
         download(out, di);
-    } else if (m > 0) {
-        std::iota(out.begin(), out.end(), 0);   // all scores 0: the lowest indices
     }
     return out;
 }

@@ -53,16 +53,19 @@ public:
         if (row.size() != memory_size_)
             throw std::invalid_argument("FlatIndexMemory: row size does not match memory_size");
         this->data.push_back(row);
+        this->touch();
         ++num_entries_;
     }
     void pop_last_memory() {
         if (num_entries_ == 0) throw std::out_of_range("FlatIndexMemory: memory is empty");
         this->data.pop_back();
+        this->touch();
         --num_entries_;
     }
     void delete_memory(size_t idx) {
         if (idx >= num_entries_) throw std::out_of_range("FlatIndexMemory: index out of range");
         this->data.erase(this->data.begin() + (std::ptrdiff_t)idx);
+        this->touch();
         --num_entries_;
     }
     std::vector<S> get_memory(size_t idx) const {
@@ -109,6 +112,7 @@ public:
 
     void insert_document(const std::unordered_map<int, int>& doc) {
         this->data.doc_freqs.push_back(doc);
+        this->touch();
         for (const auto& tf : doc) {
             ++this->data.df_map[tf.first];
             num_tokens_ += (size_t)tf.second;

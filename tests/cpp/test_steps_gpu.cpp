@@ -1,6 +1,7 @@
 // GPU arms of the C++ step API against their CPU arms (same inputs, same
 // step objects, KernelType::GPU vs KernelType::CPU).  Exits nonzero on the
 // first mismatch.  Built and run by tests/test_step_api_gpu.py.
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -151,6 +152,62 @@ int main() {
             s.execute(mem, q, gpu);
             EXPECT(cpu.export_data() == gpu.export_data(), "FusedBM25Retrieval query %d differs", t);
         }
+    }
+    {   // device copies of unchanged memories are reused; every change is seen
+        data_type::FlatIndexMemory<float> mem(matrix(g, 2000, 32));
+        data_type::VectorQuery<float> q(vec(g, 32));
+        auto agree = [&](data_type::FlatIndexMemory<float>& m, const char* what) {
+            data_type::TopKIndex cpu, gpu;
+            data_type::VectorScore<float> sc_cpu, sc_gpu;
+            step::InnerProductTopKRetrieval s(20);
+            s.execute(m, q, cpu);
+            s.set_kernel(KernelType::GPU);
+            s.execute(m, q, gpu);
+            step::InnerProductCompute c;
+            c.execute(m, q, sc_cpu);
+            c.set_current_kernel(KernelType::GPU);
+            c.execute(m, q, sc_gpu);
+            EXPECT(cpu.export_data() == gpu.export_data(), "cached top-k after %s", what);
+            EXPECT(sc_cpu.export_data() == sc_gpu.export_data(), "cached scores after %s", what);
+        };
+        agree(mem, "first use");
+        agree(mem, "reuse");
+        std::vector<float> big = vec(g, 32);
+        for (auto& v : big) v *= 100.0f;   // a row that wins every query
+        mem.insert_memory(big);
+        agree(mem, "insert_memory");
+        mem.delete_memory(0);
+        agree(mem, "delete_memory");
+        mem.pop_last_memory();
+        agree(mem, "pop_last_memory");
+        mem.set_data(matrix(g, 1500, 32));
+        agree(mem, "set_data");
+        data_type::FlatIndexMemory<float> copy = mem;
+        copy.insert_memory(big);
+        agree(copy, "a modified copy");
+        agree(mem, "its unchanged original");
+        // more memories in turn than the cache holds
+        std::vector<data_type::FlatIndexMemory<float>> many;
+        for (int i = 0; i < 6; ++i) many.emplace_back(matrix(g, 300 + i, 32));
+        for (int r = 0; r < 2; ++r)
+            for (auto& m : many) agree(m, "cycling memories");
+    }
+    {   // the cost the cache saves, at the flat-retrieval shape of config 1
+        data_type::FlatIndexMemory<float> mem(matrix(g, 65536, 128));
+        data_type::VectorQuery<float> q(vec(g, 128));
+        step::InnerProductTopKRetrieval s(64);
+        s.set_kernel(KernelType::GPU);
+        data_type::TopKIndex out;
+        auto ms = [&]() {
+            const auto t0 = std::chrono::steady_clock::now();
+            s.execute(mem, q, out);
+            return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        };
+        const double first = ms();
+        double again = 0.0;
+        for (int i = 0; i < 10; ++i) again += ms() / 10;
+        std::printf("InnerProductTopKRetrieval GPU, 65536 x 128: first call %.3f ms, "
+                    "unchanged memory %.3f ms per call\n", first, again);
     }
     std::printf("%s (%d failures)\n", failures ? "FAILED" : "PASSED", failures);
     return failures ? 1 : 0;
