@@ -60,7 +60,8 @@ def build_steps(force: bool = False) -> str:
     srcs = sorted(glob.glob(os.path.join(PKG, "src", "*.cpp")))
     if not srcs:
         return ""
-    deps = srcs + glob.glob(os.path.join(INC, "heteromm", "**", "*.h"), recursive=True) + [CUDA_LIB]
+    deps = srcs + glob.glob(os.path.join(PKG, "src", "*.h")) + \
+        glob.glob(os.path.join(INC, "heteromm", "**", "*.h"), recursive=True) + [CUDA_LIB]
     if force or _newer(STEPS_LIB, deps):
         cmd = ["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-Wall",
                "-Wextra", f"-I{INC}",

@@ -395,6 +395,144 @@ hmm_status_t check_common(const void* mem, int64_t n, int64_t dim, const void* q
     return HMM_OK;
 }
 
+// Score + top-k of a small memory (n <= SMALL_N rows), one CTA per query.
+// Columns [c0, c0 + SMALL_KC) of every row are staged in shared memory by
+// 16-byte cp.async copies, all of a chunk in flight at once; rows are padded to
+// 16 bytes past the chunk, so the 16-byte reads of a quarter-warp (8 rows)
+// fall in distinct banks.  Each thread then extends its rows' sums by those
+// columns in index order, as the fused kernel does.  The scores' composites go
+// to shared memory and one bitonic sort orders them.  Writes what
+// fused_ip_topk_kernel + merge_candidates_kernel write, in one launch and
+// without radix passes: the one-query-per-call shapes of the reference's API (a
+// few hundred page summaries) are set by those two launches' selection passes,
+// not by memory traffic.
+constexpr int SMALL_N = 1024;
+constexpr int SMALL_NT = 512;
+constexpr int SMALL_R = SMALL_N / SMALL_NT;   // rows per thread
+constexpr int SMALL_NQ = 64;
+constexpr int SMALL_KC = 32;                   // columns per staged chunk
+
+template <typename T>
+__host__ __device__ constexpr int small_ld() { return SMALL_KC + 16 / (int)sizeof(T); }   // padded row stride (elements)
+
+template <typename In>
+size_t small_smem_bytes(int64_t n, int64_t dim) {
+    return sizeof(float) * (size_t)((dim + 3) & ~int64_t(3)) +
+           sizeof(typename In::T) * (size_t)(n * small_ld<typename In::T>());
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+template <typename In, typename IdxT>
+__global__ void __launch_bounds__(SMALL_NT)
+small_ip_topk_kernel(const typename In::T* __restrict__ mem, int n, int dim,
+                     const typename In::T* __restrict__ qry, int k, int64_t row_offset, float thr,
+                     uint32_t* __restrict__ bitmap32, float* __restrict__ full_scores,
+                     IdxT* __restrict__ out_idx, float* __restrict__ out_scores, bool vec_ok) {
+    using T = typename In::T;
+    constexpr int LDT = small_ld<T>();
+    __shared__ uint64_t keys[SMALL_N];
+    extern __shared__ __align__(16) float sdyn[];
+    float* sqv = sdyn;                                              // the query, dim values
+    T* tile = reinterpret_cast<T*>(sdyn + ((dim + 3) & ~3));        // [n][LDT]
+    const int q = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int j = tid; j < dim; j += SMALL_NT) sqv[j] = In::widen1(qry + (int64_t)q * dim + j);
+
+    float acc[SMALL_R];
+#pragma unroll
+    for (int r = 0; r < SMALL_R; ++r) acc[r] = 0.0f;
+    for (int c0 = 0; c0 < dim; c0 += SMALL_KC) {
+        const int w = min(SMALL_KC, dim - c0);
+        __syncthreads();   // the previous chunk is consumed (and the query written)
+        if (vec_ok) {      // dim % VEC == 0 and 16-byte aligned rows, so w % VEC == 0
+            const int per_row = w / In::VEC;
+            for (int idx = tid; idx < n * per_row; idx += SMALL_NT) {
+                const int r = idx / per_row, v = (idx - r * per_row) * In::VEC;
+                cp_async16(tile + r * LDT + v, mem + (int64_t)r * dim + c0 + v);
+            }
+            cp_async_wait_all();
+        } else {
+            for (int idx = tid; idx < n * w; idx += SMALL_NT) {
+                const int r = idx / w, j = idx - r * w;
+                tile[r * LDT + j] = mem[(int64_t)r * dim + c0 + j];
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < SMALL_R; ++r) {
+            const int i = tid + r * SMALL_NT;
+            if (i >= n) continue;
+            const T* t = tile + i * LDT;
+            if (vec_ok) {
+                for (int v = 0; v < w; v += In::VEC) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(t + v);
+                    if constexpr (In::VEC == 4) {
+                        acc[r] = In::mac(acc[r], __uint_as_float(u.x), sqv[c0 + v]);
+                        acc[r] = In::mac(acc[r], __uint_as_float(u.y), sqv[c0 + v + 1]);
+                        acc[r] = In::mac(acc[r], __uint_as_float(u.z), sqv[c0 + v + 2]);
+                        acc[r] = In::mac(acc[r], __uint_as_float(u.w), sqv[c0 + v + 3]);
+                    } else {
+                        const uint32_t h[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            acc[r] = In::mac(acc[r], bf16_bits_to_f32((uint16_t)(h[e] & 0xffffu)),
+                                             sqv[c0 + v + 2 * e]);
+                            acc[r] = In::mac(acc[r], bf16_bits_to_f32((uint16_t)(h[e] >> 16)),
+                                             sqv[c0 + v + 2 * e + 1]);
+                        }
+                    }
+                }
+            } else {
+                for (int j = 0; j < w; ++j) acc[r] = In::mac(acc[r], In::widen1(t + j), sqv[c0 + j]);
+            }
+        }
+    }
+
+    const int n2 = next_pow2(n);
+    const int64_t words32 = 2 * (((int64_t)n + 63) / 64);
+    const int cover = max(n2, (int)(32 * words32));   // rows whose key slot or bitmap bit is written
+#pragma unroll
+    for (int r = 0; r < SMALL_R; ++r) {
+        const int base = r * SMALL_NT;
+        if (base >= cover) break;   // uniform: the ballot below sees whole warps
+        const int i = base + tid;
+        const float sc = acc[r];
+        if (i < n && full_scores) full_scores[(int64_t)q * n + i] = sc;
+        if (bitmap32) {
+            const unsigned bits = __ballot_sync(0xffffffffu, i < n && sc >= thr);
+            const int64_t w32 = (base >> 5) + warp;
+            if (lane == 0 && w32 < words32) bitmap32[(int64_t)q * words32 + w32] = bits;
+        }
+        if (i < n2) keys[i] = i < n ? make_cand(f32_key(sc), (uint32_t)i) : 0ull;
+    }
+    block_bitonic_sort_desc(keys, n2);   // synchronises before and after
+    for (int i = tid; i < k; i += SMALL_NT) {
+        const uint64_t c = i < n2 ? keys[i] : 0ull;
+        const bool ok = c != 0ull;
+        out_idx[(int64_t)q * k + i] = ok ? (IdxT)((int64_t)cand_row(c) + row_offset) : (IdxT)-1;
+        if (out_scores) out_scores[(int64_t)q * k + i] = ok ? cand_score(c) : -INFINITY;
+    }
+}
+
+// Sets the small kernel's dynamic shared-memory limit (on the current device)
+// to the largest any call can need: SMALL_N rows of the widest rows
+// check_common accepts, so calls of different shapes never lower it.
+template <typename In, typename IdxT>
+hmm_status_t prepare_small_kernel() {
+    const cudaError_t e = cudaFuncSetAttribute(
+        small_ip_topk_kernel<In, IdxT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        (int)small_smem_bytes<In>(SMALL_N, 1024));
+    if (e != cudaSuccess)
+        return set_error(HMM_ERR_CUDA, "cudaFuncSetAttribute(small_ip_topk_kernel): %s",
+                         cudaGetErrorString(e));
+    return HMM_OK;
+}
+
 template <typename In, typename IdxT>
 hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const typename In::T* qry,
                        int64_t nq, int64_t k, int64_t row_offset, IdxT* out_idx,
@@ -406,13 +544,21 @@ hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const 
     if (nq == 0) return HMM_OK;
     if (ws_bytes < need || !ws)
         return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu bytes", ws_bytes, need);
+    const bool vec_ok = (dim % In::VEC) == 0 &&
+                        (reinterpret_cast<uintptr_t>(mem) % 16) == 0;
+    if (n >= 1 && n <= SMALL_N && nq <= SMALL_NQ) {
+        const hmm_status_t ps = prepare_small_kernel<In, IdxT>();
+        if (ps != HMM_OK) return ps;
+        small_ip_topk_kernel<In, IdxT><<<(unsigned)nq, SMALL_NT, small_smem_bytes<In>(n, dim), st>>>(
+            mem, (int)n, (int)dim, qry, (int)k, row_offset, thr,
+            reinterpret_cast<uint32_t*>(out_bitmap), full_scores, out_idx, out_scores, vec_ok);
+        return check_launch("small_ip_topk_kernel");
+    }
     const Plan p = plan_fused(n, nq);
     uint64_t* cand = static_cast<uint64_t*>(ws);
     const size_t smem = fused_smem_bytes((int)dim);
     auto kern = fused_ip_topk_kernel<In>;
     HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const bool vec_ok = (dim % In::VEC) == 0 &&
-                        (reinterpret_cast<uintptr_t>(mem) % 16) == 0;
     dim3 grid(p.n_parts, p.n_qgroups);
     if (n > 0) {
         kern<<<grid, NT, smem, st>>>(mem, n, (int)dim, qry, (int)nq, (int)k, p.rows_per_part, thr,

@@ -32,6 +32,12 @@ constexpr int BSA_THREADS = 256;
 constexpr int BSA_WARPS = BSA_THREADS / 32;
 constexpr int BSA_MAX_SEL = 4096;       // selected blocks per sequence
 constexpr int BSA_MAX_SPLIT_TOKENS = 8192;
+// Smallest share of the token list one block takes when the sequences are too
+// few to fill the GPU: one pass of its warps (4 tokens each) in the token-
+// granular kernel, one page per warp in the page-granular one.  A single
+// decode sequence then spreads over ~n_list / 32 blocks instead of a handful.
+constexpr int BSA_MIN_SPLIT_TOKENS = BSA_WARPS * 4;
+constexpr int BSA_MIN_SPLIT_PAGES = BSA_WARPS;
 constexpr int SEL_MAX_BLOCKS = 8192;    // summaries per sequence for the fused selection
 
 struct PagedCache {
@@ -650,25 +656,78 @@ __global__ void __launch_bounds__(BSA_THREADS) bsa_page_kernel(const BsaArgs a) 
 }
 
 // out[d] = sum_s e^(m_s - M) acc_s[d] / sum_s e^(m_s - M) l_s; zeros for an
-// empty token list (block_sparse_attention.cpp:42-47, 67-71).
-__global__ void bsa_combine_kernel(const float* __restrict__ part, int splits, int D,
-                                   float* __restrict__ out) {
-    const int s = blockIdx.x;
-    const float* p = part + (int64_t)s * splits * (2 + D);
-    float M = -INFINITY;
-    for (int i = 0; i < splits; ++i) M = fmaxf(M, p[i * (2 + D)]);
-    float L = 0.0f;
-    for (int i = 0; i < splits; ++i) {
-        const float mi = p[i * (2 + D)];
-        if (mi != -INFINITY) L += expf(mi - M) * p[i * (2 + D) + 1];
+// empty token list (block_sparse_attention.cpp:42-47, 67-71).  One block per
+// sequence.  The max reduces over the splits in parallel; then, a chunk of
+// CMB_CHUNK splits at a time, the weights f_s = e^(m_s - M) (0 for an empty
+// split) go to shared memory, thread (g, d) adds f_s acc_s[d] over splits g,
+// g + G, ... of the chunk (G = CMB_THREADS / D groups, eight loads in flight per
+// batch), and each thread adds f_s l_s over its own splits.  Partial sums are
+// combined in group / warp order, so results repeat bit for bit.
+constexpr int CMB_THREADS = 512;
+constexpr int CMB_WARPS = CMB_THREADS / 32;
+constexpr int CMB_CHUNK = 2048;
+static_assert(PK_MAX_D <= CMB_THREADS, "one column per thread at least");
+
+template <bool IS_MAX>
+__device__ __forceinline__ float cmb_reduce(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float u = __shfl_xor_sync(0xffffffffu, v, o);
+        v = IS_MAX ? fmaxf(v, u) : v + u;
     }
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float t = 0.0f;
-        for (int i = 0; i < splits; ++i) {
-            const float mi = p[i * (2 + D)];
-            if (mi != -INFINITY) t += expf(mi - M) * p[i * (2 + D) + 2 + d];
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int w = 1; w < CMB_WARPS; ++w) r = IS_MAX ? fmaxf(r, red[w]) : r + red[w];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(CMB_THREADS) bsa_combine_kernel(const float* __restrict__ part,
+                                                                   int splits, int D,
+                                                                   float* __restrict__ out) {
+    __shared__ float red[CMB_WARPS];
+    __shared__ float tsum[CMB_THREADS];
+    __shared__ float fs[CMB_CHUNK];
+    const int s = blockIdx.x;
+    const int64_t stride = 2 + D;
+    const float* p = part + (int64_t)s * splits * stride;
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < splits; i += CMB_THREADS) m = fmaxf(m, p[i * stride]);
+    const float M = cmb_reduce<true>(m, red);
+    const int G = CMB_THREADS / D;
+    const int g = threadIdx.x / D, d = threadIdx.x % D;
+    float l = 0.0f, t = 0.0f;
+    for (int c0 = 0; c0 < splits; c0 += CMB_CHUNK) {
+        const int cn = min(CMB_CHUNK, splits - c0);
+        for (int i = threadIdx.x; i < cn; i += CMB_THREADS) {
+            const float* pi = p + (c0 + i) * stride;
+            const float f = pi[0] != -INFINITY ? expf(pi[0] - M) : 0.0f;
+            fs[i] = f;
+            l += f * pi[1];
         }
-        out[(int64_t)s * D + d] = M == -INFINITY ? 0.0f : t / L;
+        __syncthreads();
+        if (g < G) {
+            const float* col = p + (int64_t)c0 * stride + 2 + d;
+            int i = g;
+            for (; i + 7 * G < cn; i += 8 * G) {
+                float x[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) x[u] = col[(i + u * G) * stride];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) t += fs[i + u * G] * x[u];
+            }
+            for (; i < cn; i += G) t += fs[i] * col[i * stride];
+        }
+        __syncthreads();   // fs is rewritten by the next chunk
+    }
+    const float L = cmb_reduce<false>(l, red);
+    if (g < G) tsum[threadIdx.x] = t;
+    __syncthreads();
+    if (threadIdx.x < D) {
+        float o = 0.0f;
+        for (int h = 0; h < G; ++h) o += tsum[h * D + threadIdx.x];
+        out[(int64_t)s * D + threadIdx.x] = M == -INFINITY ? 0.0f : o / L;
     }
 }
 
@@ -741,7 +800,7 @@ BsaPlan bsa_plan(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_t D) 
     const int64_t max_tokens = std::max<int64_t>(1, n_sel * block_tokens);
     const int64_t sms = device_sm_count();
     int64_t want = (8 * sms + n_seq - 1) / std::max<int64_t>(1, n_seq);
-    int64_t by_tokens = (max_tokens + 255) / 256;
+    int64_t by_tokens = (max_tokens + BSA_MIN_SPLIT_TOKENS - 1) / BSA_MIN_SPLIT_TOKENS;
     int64_t sp = std::max<int64_t>(1, std::min(want, by_tokens));
     sp = std::max<int64_t>(sp, (max_tokens + BSA_MAX_SPLIT_TOKENS - 1) / BSA_MAX_SPLIT_TOKENS);
     p.splits = (int)sp;
@@ -758,8 +817,8 @@ BsaPlan bsa_page_plan(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_
                       int64_t D);
 
 // Partial-result bytes that cover both the token-granular and the
-// page-granular plans (page_tokens >= 1: the page plan never has more splits
-// than one per 16 pages, the token plan one per 256 tokens).
+// page-granular plans (the page path has 16-token pages, so its plan is
+// computed for page_tokens 16; both plans cap their splits at 8 per SM).
 size_t bsa_part_bytes(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_t D) {
     const BsaPlan t = bsa_plan(n_seq, n_sel, block_tokens, D);
     const BsaPlan g = bsa_page_plan(n_seq, n_sel, block_tokens, 16, D);
@@ -800,7 +859,7 @@ BsaPlan bsa_page_plan(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_
     const int64_t max_pages = std::max<int64_t>(1, n_sel * (block_tokens / page_tokens));
     const int64_t sms = device_sm_count();
     const int64_t want = (8 * sms + n_seq - 1) / std::max<int64_t>(1, n_seq);
-    const int64_t by_pages = (max_pages + 15) / 16;
+    const int64_t by_pages = (max_pages + BSA_MIN_SPLIT_PAGES - 1) / BSA_MIN_SPLIT_PAGES;
     const int64_t sp = std::max<int64_t>(1, std::min(want, by_pages));
     p.splits = (int)sp;
     p.split_tokens = (int)((max_pages + sp - 1) / sp);   // pages per split
@@ -843,7 +902,7 @@ hmm_status_t run_bsa(const BsaArgs& a0, int64_t n_seq, int64_t D, float* out, un
                                     : launch_page_kernel<256, 16>(a, p, n_seq, st);
         profile_end(pm, st);
         if (s != HMM_OK) return s;
-        bsa_combine_kernel<<<(unsigned)n_seq, 128, 0, st>>>(a.part, p.splits, (int)D, out);
+        bsa_combine_kernel<<<(unsigned)n_seq, CMB_THREADS, 0, st>>>(a.part, p.splits, (int)D, out);
         return check_launch("bsa_combine_kernel");
     }
     const BsaPlan p = bsa_plan(n_seq, a0.n_sel, a0.block_tokens, D);
@@ -863,7 +922,7 @@ hmm_status_t run_bsa(const BsaArgs& a0, int64_t n_seq, int64_t D, float* out, un
     hmm_status_t s = check_launch("bsa_split_kernel");
     profile_end(pm, st);
     if (s != HMM_OK) return s;
-    bsa_combine_kernel<<<(unsigned)n_seq, 128, 0, st>>>(a.part, p.splits, (int)D, out);
+    bsa_combine_kernel<<<(unsigned)n_seq, CMB_THREADS, 0, st>>>(a.part, p.splits, (int)D, out);
     return check_launch("bsa_combine_kernel");
 }
 

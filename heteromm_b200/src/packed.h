@@ -7,6 +7,7 @@
 #define HETEROMM_B200_SRC_PACKED_H_
 
 #include <cstddef>
+#include <cstdint>
 #include <vector>
 
 namespace heteromm {
@@ -28,11 +29,22 @@ std::vector<int> ip_topk_dev(const float* d_rows, size_t n, size_t d, const floa
 std::vector<float> paged_summary(const float* keys, size_t L, size_t D, const float* weight,
                                  size_t out_dim, int page);
 
+// The same with the keys on the device; the summaries stay on the device
+// (this thread's output scratch, valid until its next GPU call) and the
+// returned pointer addresses them.
+const float* paged_summary_dev(const float* d_keys, size_t L, size_t D, const float* weight,
+                               size_t out_dim, int page);
+
 // Attention output [D] of q over the tokens of the selected blocks of `page`
 // tokens of keys/values [L][D]; the caller has checked L, D, nb and page > 0.
 std::vector<float> block_sparse_attention(const float* keys, const float* values, size_t L,
                                           size_t D, const float* q, const int* blocks, size_t nb,
                                           size_t page);
+
+// The same with keys, values and the block ids on the device.
+std::vector<float> block_sparse_attention_dev(const float* d_keys, const float* d_values,
+                                              size_t L, size_t D, const float* q,
+                                              const int32_t* d_blocks, size_t nb, size_t page);
 
 }  // namespace gpu
 }  // namespace heteromm

@@ -53,26 +53,11 @@ std::vector<unsigned long long> cpu_bitmap(const std::vector<float>& s, float th
     return bm;
 }
 
-// The memory's first d columns on the device: its cached mirror when the
-// memory is unchanged since an earlier call on this thread, else packed and
-// uploaded into one.
+// The memory's first d columns on the device (its cached mirror when the
+// memory is unchanged since an earlier call on this thread).
 const float* device_rows(const data_type::FlatIndexMemory<float>& memory, size_t d,
                          const char* what) {
-    const auto& rows = memory.data_ref();
-    const size_t n = rows.size();
-    bool hit = false;
-    gpu::Mirror& m = gpu::mirror(memory.generation(), n, d, &hit);
-    float* dev = static_cast<float*>(m.buf.get(sizeof(float) * n * d));
-    if (!hit) {
-        const std::vector<float> packed = gpu::pack_rows(rows, d, what);
-        gpu::check_cuda(cudaMemcpy(dev, packed.data(), sizeof(float) * n * d,
-                                   cudaMemcpyHostToDevice),
-                        "cudaMemcpy H2D");
-        m.gen = memory.generation();
-        m.n = n;
-        m.d = d;
-    }
-    return dev;
+    return gpu::device_rows(memory.data_ref(), memory.generation(), gpu::kRows, d, what);
 }
 
 void fpga_stub(const char* step) {

@@ -1,7 +1,8 @@
 // steps_paged.cpp — PagedKVIndexBuilder and BlockSparseAttention: CPU bodies
 // (the reference's arithmetic, steps/example_kernel/paged_kv_index_builder.cpp:18-85
 // and block_sparse_attention.cpp:21-126) and GPU adapters onto
-// hmm_paged_kv_summary_f32 / hmm_block_sparse_attention_f32.
+// hmm_paged_kv_summary_f32 / hmm_block_sparse_attention_f32, reading the KV
+// cache through the per-thread device mirrors (device.h).
 #include <algorithm>
 #include <cmath>
 #include <iostream>
@@ -79,14 +80,20 @@ void PagedKVIndexBuilder::run_gpu_kernel(const data_type::KVCacheData<float>& ra
     }
     const size_t L = keys.size(), D = keys[0].size(), out_dim = weight_.size();
     const size_t pages = (L + (size_t)page_size_ - 1) / (size_t)page_size_;
-    const std::vector<float> pk = gpu::pack_rows(keys, D, "PagedKVIndexBuilder keys");
+    const float* dk = gpu::device_rows(keys, raw_data.generation(), gpu::kKeys, D,
+                                       "PagedKVIndexBuilder keys");
     const std::vector<float> pw = gpu::pack_rows(weight_, D, "PagedKVIndexBuilder weight");
-    const std::vector<float> flat = gpu::paged_summary(pk.data(), L, D, pw.data(), out_dim, page_size_);
+    const float* dsum = gpu::paged_summary_dev(dk, L, D, pw.data(), out_dim, page_size_);
+    std::vector<float> flat(pages * out_dim);
+    gpu::download(flat, dsum);
     std::vector<std::vector<float>> result(pages);
     for (size_t p = 0; p < pages; ++p)
         result[p].assign(flat.begin() + (std::ptrdiff_t)(p * out_dim),
                          flat.begin() + (std::ptrdiff_t)((p + 1) * out_dim));
     memory.set_data(result);
+    // the summaries stay on the device as the new memory's mirror: a GPU
+    // ComputeScore on this memory reads them without an upload
+    gpu::adopt_rows(memory.generation(), gpu::kRows, pages, out_dim, dsum);
 }
 
 void PagedKVIndexBuilder::run_fpga_kernel(const data_type::KVCacheData<float>&,
@@ -166,10 +173,14 @@ void BlockSparseAttention::run_gpu_kernel(const data_type::KVCacheData<float>& r
     }
     if (kv.values.size() != L)
         throw std::invalid_argument("BlockSparseAttention: keys and values differ in length");
-    const std::vector<float> pk = gpu::pack_rows(kv.keys, D, "BlockSparseAttention keys");
-    const std::vector<float> pv = gpu::pack_rows(kv.values, D, "BlockSparseAttention values");
-    output.set_data(gpu::block_sparse_attention(pk.data(), pv.data(), L, D, q.data(), blocks.data(),
-                                                blocks.size(), page_size_));
+    const float* dk = gpu::device_rows(kv.keys, retrieved_data.generation(), gpu::kKeys, D,
+                                       "BlockSparseAttention keys");
+    const float* dv = gpu::device_rows(kv.values, retrieved_data.generation(), gpu::kValues, D,
+                                       "BlockSparseAttention values");
+    const int32_t* db = gpu::upload(gpu::kIdx, reinterpret_cast<const int32_t*>(blocks.data()),
+                                    blocks.size());
+    output.set_data(gpu::block_sparse_attention_dev(dk, dv, L, D, q.data(), db, blocks.size(),
+                                                    page_size_));
 }
 
 void BlockSparseAttention::run_fpga_kernel(const data_type::KVCacheData<float>&,
@@ -188,15 +199,21 @@ namespace gpu {
 std::vector<float> paged_summary(const float* keys, size_t L, size_t D, const float* weight,
                                  size_t out_dim, int page) {
     const size_t pages = (L + (size_t)page - 1) / (size_t)page;
-    const float* dk = upload(kMem, keys, L * D);
+    const float* dsum = paged_summary_dev(upload(kMem, keys, L * D), L, D, weight, out_dim, page);
+    std::vector<float> flat(pages * out_dim);
+    download(flat, dsum);
+    return flat;
+}
+
+const float* paged_summary_dev(const float* dk, size_t L, size_t D, const float* weight,
+                               size_t out_dim, int page) {
+    const size_t pages = (L + (size_t)page - 1) / (size_t)page;
     const float* dw = upload(kAux, weight, out_dim * D);
     float* dout = static_cast<float*>(scratch(kOut).get(sizeof(float) * pages * out_dim));
     check(hmm_paged_kv_summary_f32(dk, 1, (int64_t)L, (int64_t)D, dw, (int64_t)out_dim, page,
                                    dout, nullptr),
           "PagedKVIndexBuilder GPU kernel");
-    std::vector<float> flat(pages * out_dim);
-    download(flat, dout);
-    return flat;
+    return dout;
 }
 
 std::vector<float> block_sparse_attention(const float* keys, const float* values, size_t L,
@@ -204,9 +221,15 @@ std::vector<float> block_sparse_attention(const float* keys, const float* values
                                           size_t page) {
     const float* dk = upload(kMem, keys, L * D);
     const float* dv = upload(kAux, values, L * D);
-    const float* dq = upload(kQuery, q, D);
     const int32_t* db = upload(kIdx, reinterpret_cast<const int32_t*>(blocks), nb);
-    float* dout = static_cast<float*>(scratch(kOut).get(sizeof(float) * D));
+    return block_sparse_attention_dev(dk, dv, L, D, q, db, nb, page);
+}
+
+std::vector<float> block_sparse_attention_dev(const float* dk, const float* dv, size_t L, size_t D,
+                                              const float* q, const int32_t* db, size_t nb,
+                                              size_t page) {
+    const float* dq = upload(kAux2, q, D);
+    float* dout = static_cast<float*>(scratch(kOut2).get(sizeof(float) * D));
     const size_t ws = hmm_paged_workspace_size(1, (int64_t)nb, (int64_t)page, (int64_t)D);
     void* w = scratch(kWork).get(ws);
     check(hmm_block_sparse_attention_f32(dq, dk, dv, 1, (int64_t)L, (int64_t)D, (int64_t)page, db,

@@ -79,6 +79,10 @@ public:
     BlockSparseAttention(size_t page_size) : page_size_(page_size) {}
     ~BlockSparseAttention() override = default;
 
+    // Tokens per block (an accessor of this build; the device-resident
+    // pipeline of deploy/paged_attention.h reads it).
+    size_t page_size() const { return page_size_; }
+
 protected:
     void run_test_kernel(const data_type::KVCacheData<float>& retrieved_data,
                          const data_type::TopKIndex& index,

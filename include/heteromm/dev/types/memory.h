@@ -38,6 +38,15 @@ public:
 
     std::string type_name() const override { return "FlatIndexMemory"; }
     size_t get_size() const override { return num_entries_ * memory_size_ * sizeof(S); }
+
+    // Replaces the rows and keeps num_entries / memory_size in step with them
+    // (the reference's set_data is the base's, which leaves the counts of the
+    // previous contents, types/base_types.h:68-70 and memory.h:78).
+    void set_data(const content_type& rows) {
+        Memory<content_type>::set_data(rows);
+        num_entries_ = rows.size();
+        memory_size_ = rows.empty() ? 0 : rows[0].size();
+    }
     size_t get_num_entries() const { return num_entries_; }
     size_t get_memory_size() const { return memory_size_; }
 

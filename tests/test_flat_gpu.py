@@ -23,6 +23,14 @@ def dev(a, device):
     (1000, 37, 3, 10),        # dim not a multiple of 4, n not a multiple of 64
     (257, 64, 17, 256),       # k > n/2, a partial query group
     (50, 16, 2, 100),         # k > n
+    # the one-CTA path for small memories (n <= 1024 rows, <= 64 queries) and its edges
+    (1, 128, 1, 5),           # one row
+    (512, 128, 1, 64),        # one (batch, head) of page summaries, one query
+    (64, 8, 5, 64),           # k == n, short rows
+    (1024, 128, 64, 256),     # largest n, largest query count, largest k
+    (1025, 128, 64, 100),     # one row over: the multi-CTA path
+    (1024, 128, 65, 10),      # one query over: the multi-CTA path
+    (700, 3, 2, 9),           # dim below one vector load
 ])
 def test_ip_topk_f32_matches_oracle(cuda, n, d, nq, k):
     mem = gen.normal_f32(1000 + n, (n, d))
@@ -82,6 +90,19 @@ def test_ties_nan_and_signed_zero(cuda):
     assert np.array_equal(bm.cpu().numpy().view(np.uint64), obm)
 
 
+def test_ties_nan_small_bf16(cuda):
+    """bf16 rows on the one-CTA path: ties to the lower row, NaN last."""
+    mem = np.zeros((200, 128), np.float32)
+    mem[::5, 0] = 1.0
+    mem[7, 0] = np.nan
+    mem = gen.bf16_bits(mem)
+    qry = gen.bf16_bits(np.ones((2, 128), np.float32))
+    idx, sc = hmm.ip_topk_bf16(dev(mem.view(np.int16), cuda), dev(qry.view(np.int16), cuda), 50, 0)
+    oidx, osc = O.ip_topk_bf16(mem, qry, 50, 0)
+    assert np.array_equal(idx.cpu().numpy(), oidx)
+    assert np.array_equal(sc.cpu().numpy().view(np.uint32), osc.view(np.uint32))
+
+
 def test_empty_memory(cuda):
     mem = torch.empty((0, 16), dtype=torch.float32, device=cuda)
     qry = torch.ones((2, 16), dtype=torch.float32, device=cuda)
@@ -90,7 +111,8 @@ def test_empty_memory(cuda):
     assert bm.numel() == 0
 
 
-@pytest.mark.parametrize("n,nq,k,off", [(20000, 16, 100, 0), (7777, 33, 100, 123456789)])
+@pytest.mark.parametrize("n,nq,k,off", [(20000, 16, 100, 0), (7777, 33, 100, 123456789),
+                                        (600, 3, 100, 77), (1024, 64, 256, 0)])
 def test_ip_topk_bf16_matches_oracle(cuda, n, nq, k, off):
     mem = gen.bf16_bits(gen.normal_f32(31 + n, (n, 128)))
     qry = gen.bf16_bits(gen.normal_f32(32 + n, (nq, 128)))
