@@ -41,8 +41,6 @@ float elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
 }
 }  // namespace
 
-uint64_t h2d_bytes() { return h2d_counter(); }
-
 std::vector<float> paged_attention_chain(const data_type::KVCacheData<float>& kv,
                                          const data_type::FlatIndexMemory<float>& memory,
                                          const std::vector<float>& query, size_t k,
@@ -56,7 +54,7 @@ std::vector<float> paged_attention_chain(const data_type::KVCacheData<float>& kv
     const size_t n = rows.size(), d = query.size(), m = std::min(k, n);
     int32_t* dblocks = static_cast<int32_t*>(scratch(kIdx).get(sizeof(int32_t) * (m ? m : 1)));
     if (m > 0 && d > 0) {
-        const float* dm = device_rows(rows, memory.generation(), kRows, d, "InnerProductCompute");
+        const float* dm = device_flat_rows(memory, d, "InnerProductCompute");
         const float* dq = upload(kQuery, query.data(), d);
         const size_t ws = hmm_ip_topk_f32_workspace_size((int64_t)n, (int64_t)d, 1, (int64_t)m);
         void* w = scratch(kWork).get(ws);
@@ -79,9 +77,11 @@ std::vector<float> paged_attention_chain(const data_type::KVCacheData<float>& kv
     if (m > 0 && L > 0 && D > 0 && page > 0) {
         if (values.size() != L)
             throw std::invalid_argument("BlockSparseAttention: keys and values differ in length");
-        const float* dk = device_rows(keys, kv.generation(), kKeys, D, "BlockSparseAttention keys");
+        const bool held = kv.get_device() == data_type::DataLocation::GPU_MEM;
+        const float* dk =
+            device_rows(keys, kv.generation(), kKeys, D, "BlockSparseAttention keys", held);
         const float* dv =
-            device_rows(values, kv.generation(), kValues, D, "BlockSparseAttention values");
+            device_rows(values, kv.generation(), kValues, D, "BlockSparseAttention values", held);
         out = block_sparse_attention_dev(dk, dv, L, D, input.data(), dblocks, m, page);
     }
     check_cuda(cudaEventRecord(ev.e[2], nullptr), "cudaEventRecord");

@@ -53,11 +53,12 @@ std::vector<unsigned long long> cpu_bitmap(const std::vector<float>& s, float th
     return bm;
 }
 
-// The memory's first d columns on the device (its cached mirror when the
-// memory is unchanged since an earlier call on this thread).
+// The memory's first d columns on the device: its cached mirror when the
+// memory is unchanged since an earlier call on this thread, or that mirror
+// brought up to date from the memory's row log after inserts and deletes.
 const float* device_rows(const data_type::FlatIndexMemory<float>& memory, size_t d,
                          const char* what) {
-    return gpu::device_rows(memory.data_ref(), memory.generation(), gpu::kRows, d, what);
+    return gpu::device_flat_rows(memory, d, what);
 }
 
 void fpga_stub(const char* step) {

@@ -81,7 +81,8 @@ void PagedKVIndexBuilder::run_gpu_kernel(const data_type::KVCacheData<float>& ra
     const size_t L = keys.size(), D = keys[0].size(), out_dim = weight_.size();
     const size_t pages = (L + (size_t)page_size_ - 1) / (size_t)page_size_;
     const float* dk = gpu::device_rows(keys, raw_data.generation(), gpu::kKeys, D,
-                                       "PagedKVIndexBuilder keys");
+                                       "PagedKVIndexBuilder keys",
+                                       raw_data.get_device() == data_type::DataLocation::GPU_MEM);
     const std::vector<float> pw = gpu::pack_rows(weight_, D, "PagedKVIndexBuilder weight");
     const float* dsum = gpu::paged_summary_dev(dk, L, D, pw.data(), out_dim, page_size_);
     std::vector<float> flat(pages * out_dim);
@@ -173,10 +174,11 @@ void BlockSparseAttention::run_gpu_kernel(const data_type::KVCacheData<float>& r
     }
     if (kv.values.size() != L)
         throw std::invalid_argument("BlockSparseAttention: keys and values differ in length");
+    const bool held = retrieved_data.get_device() == data_type::DataLocation::GPU_MEM;
     const float* dk = gpu::device_rows(kv.keys, retrieved_data.generation(), gpu::kKeys, D,
-                                       "BlockSparseAttention keys");
+                                       "BlockSparseAttention keys", held);
     const float* dv = gpu::device_rows(kv.values, retrieved_data.generation(), gpu::kValues, D,
-                                       "BlockSparseAttention values");
+                                       "BlockSparseAttention values", held);
     const int32_t* db = gpu::upload(gpu::kIdx, reinterpret_cast<const int32_t*>(blocks.data()),
                                     blocks.size());
     output.set_data(gpu::block_sparse_attention_dev(dk, dv, L, D, q.data(), db, blocks.size(),

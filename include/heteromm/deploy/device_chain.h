@@ -22,6 +22,7 @@
 
 #include "../dev/types/memory.h"
 #include "../dev/types/retrieved_data.h"
+#include "../residency.h"
 
 namespace heteromm {
 namespace gpu {
@@ -44,10 +45,6 @@ std::vector<float> paged_attention_chain(const data_type::KVCacheData<float>& kv
                                          const std::vector<float>& query, size_t k,
                                          const std::vector<float>& input, size_t page_size,
                                          ChainTimes* times = nullptr);
-
-// Bytes the calling thread has copied host -> device through the step
-// adapters and the chains so far (a monotone counter, for tests and benches).
-uint64_t h2d_bytes();
 
 }  // namespace gpu
 }  // namespace heteromm

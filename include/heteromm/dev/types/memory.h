@@ -7,6 +7,7 @@
 #ifndef HETEROMM_B200_DEV_TYPES_MEMORY_H_
 #define HETEROMM_B200_DEV_TYPES_MEMORY_H_
 
+#include <deque>
 #include <stdexcept>
 #include <unordered_map>
 #include <vector>
@@ -46,7 +47,25 @@ public:
         Memory<content_type>::set_data(rows);
         num_entries_ = rows.size();
         memory_size_ = rows.empty() ? 0 : rows[0].size();
+        deltas_.clear();
     }
+
+    // Row changes made by insert_memory / pop_last_memory / delete_memory,
+    // oldest first, at most kMaxRowDeltas (an addition of this build).  Each
+    // names the generation it was made on and the one it produced, so a copy of
+    // the rows taken at generation `from` (a device copy, say) can be brought up
+    // to date by replaying the changes after it instead of being taken again.
+    // set_data clears the log; a copy of the memory has a generation of its own,
+    // so the log it inherits never ends at it and is never replayed for it.
+    struct RowDelta {
+        enum Kind { Append, PopLast, Erase };
+        uint64_t from, to;
+        Kind kind;
+        size_t index;          // Append: the new row's position; Erase: the erased row's
+        std::vector<S> row;    // Append: the appended row
+    };
+    static constexpr size_t kMaxRowDeltas = 1024;
+    const std::deque<RowDelta>& row_deltas() const { return deltas_; }
     size_t get_num_entries() const { return num_entries_; }
     size_t get_memory_size() const { return memory_size_; }
 
@@ -62,19 +81,19 @@ public:
         if (row.size() != memory_size_)
             throw std::invalid_argument("FlatIndexMemory: row size does not match memory_size");
         this->data.push_back(row);
-        this->touch();
+        record(RowDelta::Append, num_entries_, &row);
         ++num_entries_;
     }
     void pop_last_memory() {
         if (num_entries_ == 0) throw std::out_of_range("FlatIndexMemory: memory is empty");
         this->data.pop_back();
-        this->touch();
+        record(RowDelta::PopLast, num_entries_ - 1, nullptr);
         --num_entries_;
     }
     void delete_memory(size_t idx) {
         if (idx >= num_entries_) throw std::out_of_range("FlatIndexMemory: index out of range");
         this->data.erase(this->data.begin() + (std::ptrdiff_t)idx);
-        this->touch();
+        record(RowDelta::Erase, idx, nullptr);
         --num_entries_;
     }
     std::vector<S> get_memory(size_t idx) const {
@@ -83,8 +102,18 @@ public:
     }
 
 private:
+    // Renews the generation and logs the change that produced it.
+    void record(typename RowDelta::Kind kind, size_t index, const std::vector<S>* row) {
+        const uint64_t from = this->generation();
+        this->touch();
+        deltas_.push_back(RowDelta{from, this->generation(), kind, index,
+                                   row ? *row : std::vector<S>()});
+        if (deltas_.size() > kMaxRowDeltas) deltas_.pop_front();
+    }
+
     size_t num_entries_ = 0;
     size_t memory_size_ = 0;
+    std::deque<RowDelta> deltas_;
 };
 
 // Inverted BM25 statistics: document frequency per token and the token
