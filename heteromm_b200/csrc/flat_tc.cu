@@ -75,11 +75,6 @@ constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summatio
 #define HMM_SEED_ROWS 8192
 #endif
 constexpr int SEED_ROWS = HMM_SEED_ROWS;
-#ifndef HMM_PASS_GROWTH
-#define HMM_PASS_GROWTH 128
-#endif
-constexpr int64_t PASS_GROWTH = HMM_PASS_GROWTH;      // row-prefix growth between passes
-constexpr int64_t PASS_MIN_ROWS = int64_t(1) << 22;   // shards from 4Mi rows on use passes
 constexpr int POOL_CAP = 8192;
 constexpr int KMAX_TC = 128;
 #ifndef HMM_RAISE_STEP
@@ -804,12 +799,16 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         CUtensorMap tmB;
         s = make_tmap_bf16(&tmB, qp, nqp_pass, TC_NMAX);
         if (s != HMM_OK) return s;
-        // One tensor-core pass over rows [r0, r1), appending to the pools.
-        auto run_pass = [&](int64_t r0, int64_t r1) -> hmm_status_t {
+        // One tensor-core pass over rows [seed, n), appending to the pools.  The
+        // pools start from the seed's exact top-k, and the rescorers refresh the
+        // shared threshold as candidates arrive, so one pass keeps hits sparse;
+        // passes over growing row prefixes, each reseeded from the exact top-k
+        // of the last, measured no faster at 8Mi-64Mi rows (slower below 32Mi).
+        {
             TcArgs a;
-            a.n_rows = r1;
-            a.row_begin = r0;
-            a.n_tiles = (int)((r1 - r0 + TC_M - 1) / TC_M);
+            a.n_rows = n;
+            a.row_begin = seed;
+            a.n_tiles = (int)((n - seed + TC_M - 1) / TC_M);
             a.nq = nqp_pass;
             a.k = (int)k;
             a.pool_cap = POOL_CAP;
@@ -823,37 +822,10 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
             const int grid = std::max(1, std::min(sms, a.n_tiles));
             const ProfileMark pm = profile_begin(st);
             tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
-            const hmm_status_t ls = check_launch("tc_score_select_kernel");
+            s = check_launch("tc_score_select_kernel");
             profile_end(pm, st);
-            return ls;
-        };
-        // Large shards go in several passes over geometrically growing row
-        // prefixes.  The exact top-k of each prefix reseeds the pools for the
-        // next pass: the k-th best of any subset of rows is a lower bound on
-        // the final k-th best, and each pass starts from the exact threshold
-        // of everything before it, so far fewer candidates reach rescoring
-        // than when thousands of tiles run against a threshold still catching
-        // up.  The status word is kept across the passes, so a full pool in
-        // any pass still sends the call to the exact path.
-        int64_t split = seed;
-        if (n >= PASS_MIN_ROWS) {
-            while (split * PASS_GROWTH <= n / 4) {
-                const int64_t next = split * PASS_GROWTH;
-                s = run_pass(split, next);
-                if (s != HMM_OK) return s;
-                s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, 0, seed_idx, seed_sc,
-                                      st);
-                if (s != HMM_OK) return s;
-                HMM_CUDA_TRY(cudaMemsetAsync(pool, 0, sizeof(uint64_t) * nqp_pass * POOL_CAP, st));
-                seed_pool_kernel<<<nqp_pass, 128, 0, st>>>(seed_idx, seed_sc, nqp_pass, (int)k,
-                                                            pool, POOL_CAP, cnt, tau);
-                s = check_launch("seed_pool_kernel");
-                if (s != HMM_OK) return s;
-                split = next;
-            }
+            if (s != HMM_OK) return s;
         }
-        s = run_pass(split, n);
-        if (s != HMM_OK) return s;
 
         s = launch_pool_merge(pool, POOL_CAP, cnt, nqp_pass, (int)k, row_offset,
                               out_idx + q0 * k, out_scores + q0 * k, st);

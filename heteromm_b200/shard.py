@@ -2,7 +2,8 @@
 
 Rank r of P owns the contiguous rows [r*N/P, (r+1)*N/P) (the last rank takes
 the remainder), scores them locally with global row indices, and one
-all-gather of the (score, index) candidates lets every rank merge the same
+all-gather of the (score, index) candidates (packed into one byte buffer per
+rank, so one collective carries both) lets every rank merge the same
 global top-k (score desc, global index asc).  The reference has no
 multi-device path; this is the exchange its single-device top-k implies.
 
@@ -35,14 +36,17 @@ def gather_merge(scores: torch.Tensor, idx: torch.Tensor, k: int,
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     if world == 1:
         return scores, idx
-    gs = torch.empty((world,) + tuple(scores.shape), dtype=scores.dtype, device=scores.device)
-    gi = torch.empty((world,) + tuple(idx.shape), dtype=idx.dtype, device=idx.device)
-    if scores.is_cuda:
-        dist.all_gather_into_tensor(gs, scores.contiguous(), group=group)
-        dist.all_gather_into_tensor(gi, idx.contiguous(), group=group)
+    # one collective: each rank's scores and indices packed as bytes, side by side
+    ns = scores.numel() * scores.element_size()
+    mine = torch.cat([scores.contiguous().reshape(-1).view(torch.uint8),
+                      idx.contiguous().reshape(-1).view(torch.uint8)])
+    g = torch.empty((world, mine.numel()), dtype=torch.uint8, device=mine.device)
+    if mine.is_cuda:
+        dist.all_gather_into_tensor(g, mine, group=group)
     else:   # gloo: list form
-        dist.all_gather(list(gs.unbind(0)), scores.contiguous(), group=group)
-        dist.all_gather(list(gi.unbind(0)), idx.contiguous(), group=group)
+        dist.all_gather(list(g.unbind(0)), mine, group=group)
+    gs = g[:, :ns].contiguous().view(scores.dtype).reshape((world,) + tuple(scores.shape))
+    gi = g[:, ns:].contiguous().view(idx.dtype).reshape((world,) + tuple(idx.shape))
     return merge(gs, gi, k)
 
 
