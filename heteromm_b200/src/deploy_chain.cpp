@@ -17,7 +17,7 @@ namespace heteromm {
 namespace gpu {
 
 namespace {
-// Three events on the legacy default stream, created on first use by a thread.
+// Three events on the legacy default stream, per thread and device.
 struct ChainEvents {
     cudaEvent_t e[3] = {nullptr, nullptr, nullptr};
     ChainEvents() {
@@ -29,10 +29,7 @@ struct ChainEvents {
     }
 };
 
-ChainEvents& chain_events() {
-    thread_local ChainEvents ev;
-    return ev;
-}
+ChainEvents& chain_events() { return per_device<ChainEvents>(); }
 
 float elapsed_ms(cudaEvent_t a, cudaEvent_t b) {
     float ms = 0.0f;

@@ -1,6 +1,6 @@
 // device.h — shared plumbing of the GPU adapters behind the step classes:
-// status -> exception mapping, a grow-only per-thread device scratch and
-// per-thread device mirrors of unchanged host rows.
+// status -> exception mapping, a grow-only device scratch and device mirrors
+// of unchanged host rows, both per thread and GPU.
 // Adapters are synchronous, like the reference steps: upload, run on the
 // legacy default stream, copy results back.
 #ifndef HETEROMM_B200_SRC_DEVICE_H_
@@ -11,6 +11,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -77,12 +78,31 @@ private:
     size_t n_ = 0;
 };
 
-// Named scratch slots of the calling thread.
-enum Slot { kMem, kQuery, kOut, kOut2, kIdx, kWork, kAux, kAux2, kAux3, kSlots };
-inline DeviceBuffer& scratch(Slot s) {
-    thread_local DeviceBuffer buf[kSlots];
-    return buf[s];
+// The calling thread's instance of T for the current device, created on
+// first use there.  Device buffers, the events recorded on a device's streams
+// and the copies of data held on a device live in these, so a thread that
+// moves between GPUs (cudaSetDevice) never hands one device's memory or
+// events to another's kernels.
+inline int current_device() {
+    int d = 0;
+    check_cuda(cudaGetDevice(&d), "cudaGetDevice");
+    return d;
 }
+template <typename T>
+T& per_device() {
+    thread_local std::vector<std::unique_ptr<T>> v;
+    const int d = current_device();
+    if ((size_t)d >= v.size()) v.resize((size_t)d + 1);
+    if (!v[(size_t)d]) v[(size_t)d] = std::make_unique<T>();
+    return *v[(size_t)d];
+}
+
+// Named scratch slots of the calling thread on the current device.
+enum Slot { kMem, kQuery, kOut, kOut2, kIdx, kWork, kAux, kAux2, kAux3, kSlots };
+struct ScratchSet {
+    DeviceBuffer buf[kSlots];
+};
+inline DeviceBuffer& scratch(Slot s) { return per_device<ScratchSet>().buf[s]; }
 
 // Bytes this thread has copied host -> device through the adapters (read by
 // h2d_bytes(), deploy/device_chain.h).
@@ -118,7 +138,7 @@ void download(std::vector<T>& host, const T* dev) {
                    "cudaMemcpy D2H");
 }
 
-// Device copies of recently used row arrays, per thread: up to kMirrors,
+// Device copies of recently used row arrays, per thread and device: up to kMirrors,
 // keyed by the owning object's generation (renewed by every change of its
 // contents), which of its arrays it is (tag) and the packed shape.  A hit skips
 // the packing and the upload of unchanged rows.  A new copy replaces the least
@@ -138,10 +158,7 @@ struct MirrorTable {
     Mirror m[kMirrors];
     uint64_t clock = 0;
 };
-inline MirrorTable& mirror_table() {
-    thread_local MirrorTable t;
-    return t;
-}
+inline MirrorTable& mirror_table() { return per_device<MirrorTable>(); }
 
 inline Mirror* find_mirror(uint64_t gen, int tag, size_t n, size_t d) {
     MirrorTable& t = mirror_table();
@@ -190,7 +207,7 @@ std::vector<T> pack_rows(const std::vector<std::vector<T>>& rows, size_t cols, c
     return out;
 }
 
-// Two pinned host buffers of kStageBytes per thread, with an event each: a
+// Two pinned host buffers of kStageBytes per thread and GPU, with an event each: a
 // full upload packs the next chunk of rows into one while the copy from the
 // other runs, so packing and the host->device transfer overlap, and the copies
 // run from pinned memory at full link speed.
@@ -219,10 +236,7 @@ struct PinnedStage {
         pending[i] = false;
     }
 };
-inline PinnedStage& pinned_stage() {
-    thread_local PinnedStage s;
-    return s;
-}
+inline PinnedStage& pinned_stage() { return per_device<PinnedStage>(); }
 
 // The first d columns of rows[0..n) into dev (n x d floats); every row must
 // have d values (checked before anything is copied).

@@ -3,8 +3,8 @@
 //
 // The reference's data types carry a DataLocation tag (types/base_types.h:26-30,
 // 57-59: SYS_DRAM, GPU_MEM, FPGA_MEM) that nothing acts on.  Here the GPU arms
-// of the steps keep per-thread device copies ("mirrors") of the rows they read,
-// keyed by each object's generation, and act on the tag:
+// of the steps keep device copies ("mirrors") of the rows they read, per
+// thread and GPU, keyed by each object's generation, and act on the tag:
 //   - a copy of an object tagged GPU_MEM is held: it is replaced only after
 //     every copy that is not;
 //   - make_resident() takes the copy now, so the first GPU step on the object
@@ -14,7 +14,7 @@
 //     device (appended rows copied up, erased rows closed up) from the
 //     memory's row log instead of uploading the memory again.
 // Full uploads pack the rows into pinned chunks, overlapped with the copies.
-// All of it is per calling thread, as the adapters' scratch is.
+// All of it is per calling thread and current GPU, as the adapters' scratch is.
 #ifndef HETEROMM_B200_RESIDENCY_H_
 #define HETEROMM_B200_RESIDENCY_H_
 
