@@ -1,5 +1,5 @@
 """The multi-rank exchange of the sharded flat retrieval (heteromm_b200.shard)
-on world-size-2 gloo CPU ranks: each rank takes its row range, computes its
+on gloo CPU ranks (world sizes 2 and 4): each rank takes its row range, computes its
 local top-k with global indices (the oracle stands in for the GPU kernel),
 all-gathers and merges (the oracle's merge); every rank must hold the
 unsharded top-k."""
@@ -41,8 +41,8 @@ def _rank_main(rank, world, port, n, nq, k, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("n,nq,k", [(20011, 8, 50), (300, 3, 100)])
-def test_sharded_topk_equals_unsharded(tmp_path, n, nq, k):
+@pytest.mark.parametrize("world,n,nq,k", [(2, 20011, 8, 50), (2, 300, 3, 100), (4, 9001, 5, 64)])
+def test_sharded_topk_equals_unsharded(tmp_path, world, n, nq, k):
     sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
     import gen
     from oracle import oracle as O
@@ -50,11 +50,11 @@ def test_sharded_topk_equals_unsharded(tmp_path, n, nq, k):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.spawn(_rank_main, args=(2, port, n, nq, k, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(world, port, n, nq, k, str(tmp_path)), nprocs=world, join=True)
     rows = gen.bf16_bits(gen.normal_f32(1201, (n, 128)))
     qry = gen.bf16_bits(gen.normal_f32(1202, (nq, 128)))
     oi, os_ = O.ip_topk_bf16(rows, qry, k)
-    for r in range(2):
+    for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"idx{r}.npy"), oi)
         assert np.array_equal(np.load(tmp_path / f"sc{r}.npy").view(np.uint32), os_.view(np.uint32))
 
