@@ -86,3 +86,25 @@ def test_dsa_fp8_matches_exact_within_tolerance(cuda, T, H, L, pos0, topk):
         assert len(extra) == len(missing)
         assert (exact[t, extra] >= kth - slack).all()
         assert (exact[t, missing] <= kth + slack).all()
+
+
+@pytest.mark.parametrize("T,chunks", [(700, 1), (700, 3), (700, None), (1500, None)])
+def test_dsa_host_pipeline_equals_device_call(cuda, T, chunks):
+    """dsa_indexer_fp8_host (host inputs and outputs, the token slices'
+    transfers overlapped with the indexer) returns what dsa_indexer_fp8 returns
+    on the same inputs, bit for bit: equal slices with a ragged last one, and
+    the wave-sized slices (two at 700 tokens, three at 1,500 on 148 SMs)."""
+    H, L, topk = 64, 4096, 256
+    pos0 = L - T
+    q, k, w = inputs(1700 + T + (chunks or 0), T, H, L)
+    qd = torch.from_numpy(np.ascontiguousarray(q)).to(cuda)
+    kd = torch.from_numpy(np.ascontiguousarray(k)).to(cuda)
+    wd = torch.from_numpy(np.ascontiguousarray(w)).to(cuda)
+    ref_i, ref_s = hmm.dsa_indexer_fp8(qd, kd, wd, pos0, topk)
+    qh = torch.from_numpy(np.ascontiguousarray(q)).pin_memory()
+    wh = torch.from_numpy(np.ascontiguousarray(w)).pin_memory()
+    for _ in range(2):   # twice: the copy streams are reused
+        i, s = hmm.dsa_indexer_fp8_host(qh, kd, wh, pos0, topk, chunks=chunks)
+        assert not i.is_cuda and i.is_pinned()
+        assert torch.equal(i, ref_i.cpu())
+        assert torch.equal(s.view(torch.int32), ref_s.cpu().view(torch.int32))
