@@ -852,7 +852,30 @@ hmm_status_t read_status(const int* status, cudaStream_t st, const char* what) {
     return HMM_OK;
 }
 
-// Page-granular plan: splits over the pages of the selected list.
+// Resident blocks per SM of the page kernel for head size D with `smem`
+// bytes of dynamic shared memory on the current device (0 if unknown).
+int page_kernel_blocks_per_sm(int64_t D, size_t smem) {
+    int n = 0;
+    cudaError_t e = cudaErrorInvalidValue;
+    if (D == 64)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, bsa_page_kernel<64, 16>, BSA_THREADS, smem);
+    else if (D == 128)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, bsa_page_kernel<128, 16>, BSA_THREADS, smem);
+    else if (D == 256)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, bsa_page_kernel<256, 16>, BSA_THREADS, smem);
+    if (e != cudaSuccess) {
+        cudaGetLastError();   // a failed query leaves no sticky error behind
+        return 0;
+    }
+    return n;
+}
+
+// Page-granular plan: splits over the pages of the selected list.  The
+// first guess gives the GPU about 8 blocks per SM.  Then, from that split
+// count up to 1.6 times it, the count whose blocks fill their last wave best is
+// taken when it fills it clearly better (more than 2 points): at 256
+// sequences and 2 resident blocks per SM, 5 splits leave the fifth wave a
+// third full and 8 fill 7 waves (0.105 -> 0.102 ms per decode step).
 BsaPlan bsa_page_plan(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_t page_tokens,
                       int64_t D) {
     BsaPlan p;
@@ -860,10 +883,25 @@ BsaPlan bsa_page_plan(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_
     const int64_t sms = device_sm_count();
     const int64_t want = (8 * sms + n_seq - 1) / std::max<int64_t>(1, n_seq);
     const int64_t by_pages = (max_pages + BSA_MIN_SPLIT_PAGES - 1) / BSA_MIN_SPLIT_PAGES;
-    const int64_t sp = std::max<int64_t>(1, std::min(want, by_pages));
+    int64_t sp = std::max<int64_t>(1, std::min(want, by_pages));
+    p.smem = sizeof(int) * (n_sel + 1) + sizeof(float) * (2 * BSA_WARPS + BSA_WARPS * D);
+    const int64_t slots = sms * page_kernel_blocks_per_sm(D, p.smem);
+    if (slots > 0 && n_seq > 0) {
+        auto fill = [&](int64_t s) {
+            const int64_t blocks = n_seq * s, waves = (blocks + slots - 1) / slots;
+            return (double)blocks / (double)(waves * slots);
+        };
+        int64_t best = sp;
+        double best_fill = fill(sp);
+        for (int64_t s = sp + 1; s <= std::min<int64_t>(sp + (3 * sp + 4) / 5, by_pages); ++s)
+            if (fill(s) > best_fill + 0.02) {
+                best = s;
+                best_fill = fill(s);
+            }
+        sp = best;
+    }
     p.splits = (int)sp;
     p.split_tokens = (int)((max_pages + sp - 1) / sp);   // pages per split
-    p.smem = sizeof(int) * (n_sel + 1) + sizeof(float) * (2 * BSA_WARPS + BSA_WARPS * D);
     p.part_bytes = sizeof(float) * (size_t)n_seq * p.splits * (2 + D);
     return p;
 }
