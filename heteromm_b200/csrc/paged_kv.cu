@@ -38,6 +38,7 @@ constexpr int BSA_MAX_SPLIT_TOKENS = 8192;
 // decode sequence then spreads over ~n_list / 32 blocks instead of a handful.
 constexpr int BSA_MIN_SPLIT_TOKENS = BSA_WARPS * 4;
 constexpr int BSA_MIN_SPLIT_PAGES = BSA_WARPS;
+constexpr int BSA_PAGES_PER_SPLIT = 8 * BSA_WARPS;   // pages a split takes when sequences are many
 constexpr int SEL_MAX_BLOCKS = 8192;    // summaries per sequence for the fused selection
 
 struct PagedCache {
@@ -818,7 +819,7 @@ BsaPlan bsa_page_plan(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_
 
 // Partial-result bytes that cover both the token-granular and the
 // page-granular plans (the page path has 16-token pages, so its plan is
-// computed for page_tokens 16; both plans cap their splits at 8 per SM).
+// computed for page_tokens 16).
 size_t bsa_part_bytes(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_t D) {
     const BsaPlan t = bsa_plan(n_seq, n_sel, block_tokens, D);
     const BsaPlan g = bsa_page_plan(n_seq, n_sel, block_tokens, 16, D);
@@ -870,36 +871,27 @@ int page_kernel_blocks_per_sm(int64_t D, size_t smem) {
     return n;
 }
 
-// Page-granular plan: splits over the pages of the selected list.  The
-// first guess gives the GPU about 8 blocks per SM.  Then, from that split
-// count up to 1.6 times it, the count whose blocks fill their last wave best is
-// taken when it fills it clearly better (more than 2 points): at 256
-// sequences and 2 resident blocks per SM, 5 splits leave the fifth wave a
-// third full and 8 fill 7 waves (0.105 -> 0.102 ms per decode step).
+// Page-granular plan: splits over the pages of the selected list.  A split
+// carries fixed costs (its page-list scan, its partial result, its share of
+// the combine), and measured on a B200 fewer, longer splits win: at 256
+// sequences of 256 pages 4 splits took 101 us, 8 took 102-105, 16 took 117;
+// at 64 sequences 4, 8, 16 took 31, 33, 37 us.  So a split gets 64 pages (8
+// per warp) or more, and more splits only when the sequences are too few to
+// give every resident block slot of the GPU one (a single decode sequence
+// spreads over up to 32 blocks of 8 pages).
 BsaPlan bsa_page_plan(int64_t n_seq, int64_t n_sel, int64_t block_tokens, int64_t page_tokens,
                       int64_t D) {
     BsaPlan p;
     const int64_t max_pages = std::max<int64_t>(1, n_sel * (block_tokens / page_tokens));
     const int64_t sms = device_sm_count();
-    const int64_t want = (8 * sms + n_seq - 1) / std::max<int64_t>(1, n_seq);
     const int64_t by_pages = (max_pages + BSA_MIN_SPLIT_PAGES - 1) / BSA_MIN_SPLIT_PAGES;
-    int64_t sp = std::max<int64_t>(1, std::min(want, by_pages));
     p.smem = sizeof(int) * (n_sel + 1) + sizeof(float) * (2 * BSA_WARPS + BSA_WARPS * D);
-    const int64_t slots = sms * page_kernel_blocks_per_sm(D, p.smem);
-    if (slots > 0 && n_seq > 0) {
-        auto fill = [&](int64_t s) {
-            const int64_t blocks = n_seq * s, waves = (blocks + slots - 1) / slots;
-            return (double)blocks / (double)(waves * slots);
-        };
-        int64_t best = sp;
-        double best_fill = fill(sp);
-        for (int64_t s = sp + 1; s <= std::min<int64_t>(sp + (3 * sp + 4) / 5, by_pages); ++s)
-            if (fill(s) > best_fill + 0.02) {
-                best = s;
-                best_fill = fill(s);
-            }
-        sp = best;
-    }
+    const int64_t per_sm = page_kernel_blocks_per_sm(D, p.smem);
+    const int64_t slots = sms * (per_sm > 0 ? per_sm : 2);
+    const int64_t fill = slots / std::max<int64_t>(1, n_seq);   // splits giving each slot a block
+    const int64_t sp = std::max<int64_t>(
+        1, std::min(by_pages, std::max((max_pages + BSA_PAGES_PER_SPLIT - 1) / BSA_PAGES_PER_SPLIT,
+                                       fill)));
     p.splits = (int)sp;
     p.split_tokens = (int)((max_pages + sp - 1) / sp);   // pages per split
     p.part_bytes = sizeof(float) * (size_t)n_seq * p.splits * (2 + D);
