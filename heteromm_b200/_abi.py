@@ -36,6 +36,7 @@ SIGNATURES = {
     "hmm_ip_topk_f32": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _F, _P, _P, _S, _P]),
     "hmm_ip_topk_bf16_workspace_size": (_S, [_I, _I, _I, _I]),
     "hmm_ip_topk_bf16": (C.c_int, [_P, _I, _I, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
+    "hmm_ip_topk_bf16_async": (C.c_int, [_P, _I, _I, _P, _I, _I, _I, _P, _P, _P, _P, _S, _P]),
     "hmm_ip_topk_f32_noalloc": (C.c_int, [_P, _I, _I, _P, _I, _I, _P, _P, _F, _P, _P]),
     "hmm_shard_merge_topk_workspace_size": (_S, [_I, _I, _I]),
     "hmm_shard_merge_topk": (C.c_int, [_P, _P, _I, _I, _I, _P, _P, _P, _S, _P]),
@@ -76,6 +77,7 @@ SIGNATURES = {
     "hmm_kernel_launches": (_I, []),
     "hmm_profile_enable": (C.c_int, [C.c_int]),
     "hmm_profile_read": (C.c_int, [_P, _P]),
+    "hmm_debug_set_wait_limit_ns": (C.c_int, [_I]),
 }
 
 
@@ -130,6 +132,12 @@ def kernel_launches() -> int:
 def profile_enable(on: bool) -> None:
     """Starts / stops CUDA-event timing of the dominant scoring kernel."""
     call("hmm_profile_enable", 1 if on else 0)
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Test hook: limit of the tensor-core kernels' bounded waits for the
+    calls that follow (ns; negative restores the 2 s default)."""
+    call("hmm_debug_set_wait_limit_ns", int(ns))
 
 
 def profile_read() -> tuple:

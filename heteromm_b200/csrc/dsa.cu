@@ -46,7 +46,6 @@ constexpr int K_TILE_BYTES = KT * DK;   // 16 KB
 constexpr int Q_TILE_BYTES = NQ * DK;   // 32 KB
 constexpr int D_EPI_WG = 4;              // epilogue warpgroups: (tile parity, token half)
 constexpr int D_THREADS = 128 + 128 * D_EPI_WG;
-constexpr uint64_t D_WAIT_NS = 2000000000ull;
 
 struct DsaCtrl {
     float wsm[4 * D_EPI_WG][NQ / 2];        // each epilogue warp's token weights for its group
@@ -65,6 +64,7 @@ struct DsaArgs {
     int64_t T, L, pos0;
     int H, tg;            // heads, tokens per group (NQ / H)
     int n_groups, key_tiles;
+    uint64_t wait_ns;     // limit of every bounded wait (wait_limit_ns())
 };
 
 // Packed fp32 pairs for fma.rn.f32x2 (sm_100a).
@@ -89,8 +89,9 @@ __device__ __forceinline__ int group_tiles(const DsaArgs& a, int g) {
     return (int)min((int64_t)a.key_tiles, (vis + KT - 1) / KT);
 }
 
-__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    const bool ok = mbar_wait_bounded(bar, parity, abort, D_WAIT_NS);
+__device__ __forceinline__ bool wait_all(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                         uint64_t limit_ns) {
+    const bool ok = mbar_wait_bounded(bar, parity, abort, limit_ns);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -148,7 +149,7 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const int nt = group_tiles(a, g);
             if (nt == 0) continue;
             const int qb = k & 1;
-            if (!wait_all(&ctl->q_empty[qb], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+            if (!wait_all(&ctl->q_empty[qb], ((k >> 1) & 1) ^ 1, abort, a.wait_ns)) { ok = false; break; }
             if (lane == 0) {
                 mbar_expect_tx(&ctl->q_full[qb], Q_TILE_BYTES);
                 tma_load_2d(Qs + qb * Q_TILE_BYTES, &tmQ, &ctl->q_full[qb], 0, g * NQ);
@@ -156,7 +157,7 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             qk = ++k;
             for (int t = 0; t < nt; ++t, ++i) {
                 const int s = i % D_STAGES;
-                if (!wait_all(&ctl->a_empty[s], ((i / D_STAGES) & 1) ^ 1, abort)) { ok = false; break; }
+                if (!wait_all(&ctl->a_empty[s], ((i / D_STAGES) & 1) ^ 1, abort, a.wait_ns)) { ok = false; break; }
                 if (lane == 0) {
                     mbar_expect_tx(&ctl->a_full[s], K_TILE_BYTES);
                     tma_load_2d(Ks + s * K_TILE_BYTES, &tmK, &ctl->a_full[s], 0, t * KT);
@@ -169,9 +170,9 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             if (lane == 0) dsa_abort(ctl, a.status);
             // drain: the copies in flight must land before the CTA exits
             for (int j = max(0, issued - D_STAGES); j < issued; ++j)
-                mbar_wait_bounded(&ctl->a_full[j % D_STAGES], (j / D_STAGES) & 1, abort, 100000000ull);
+                mbar_wait_drain(&ctl->a_full[j % D_STAGES], (j / D_STAGES) & 1);
             for (int j = max(0, qk - 2); j < qk; ++j)
-                mbar_wait_bounded(&ctl->q_full[j & 1], (j >> 1) & 1, abort, 100000000ull);
+                mbar_wait_drain(&ctl->q_full[j & 1], (j >> 1) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA
@@ -182,12 +183,12 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const int nt = group_tiles(a, g);
             if (nt == 0) continue;
             const int qb = k & 1;
-            if (!wait_all(&ctl->q_full[qb], (k >> 1) & 1, abort)) { ok = false; break; }
+            if (!wait_all(&ctl->q_full[qb], (k >> 1) & 1, abort, a.wait_ns)) { ok = false; break; }
             ++k;
             for (int t = 0; t < nt; ++t, ++i) {
                 const int s = i % D_STAGES, b = i & 1;
-                if (!wait_all(&ctl->a_full[s], (i / D_STAGES) & 1, abort) ||
-                    !wait_all(&ctl->acc_empty[b], ((i >> 1) & 1) ^ 1, abort)) {
+                if (!wait_all(&ctl->a_full[s], (i / D_STAGES) & 1, abort, a.wait_ns) ||
+                    !wait_all(&ctl->acc_empty[b], ((i >> 1) & 1) ^ 1, abort, a.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -210,8 +211,8 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
         if (!ok) {
             if (lane == 0) dsa_abort(ctl, a.status);
-            if (last >= 0)
-                mbar_wait_bounded(&ctl->acc_full[last & 1], (last >> 1) & 1, abort, 100000000ull);
+            if (last >= 0)   // the MMAs issued must finish before TMEM is freed
+                mbar_wait_drain(&ctl->acc_full[last & 1], (last >> 1) & 1);
         }
     } else if (warp >= 4) {
         // -------------------------------------------------------- epilogue
@@ -239,7 +240,7 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     g_loaded = g;
                 }
                 const int b = i & 1;
-                if (!wait_all(&ctl->acc_full[b], (i >> 1) & 1, abort)) { ok = false; break; }
+                if (!wait_all(&ctl->acc_full[b], (i >> 1) & 1, abort, a.wait_ns)) { ok = false; break; }
                 tc_fence_after();
                 const int64_t j = (int64_t)t * KT + r;
                 const uint32_t tb = tmem + (uint32_t)(b * NQ) + ((uint32_t)(sub * 32) << 16);
@@ -565,6 +566,7 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
         a.tg = NQ / (int)H;
         a.n_groups = (int)((T + a.tg - 1) / a.tg);
         a.key_tiles = (int)((L + KT - 1) / KT);
+        a.wait_ns = wait_limit_ns();
         auto kern = H == 64 ? dsa_scores_kernel<64> : H == 32 ? dsa_scores_kernel<32>
                                                               : dsa_scores_kernel<16>;
         HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,

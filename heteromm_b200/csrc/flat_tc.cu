@@ -69,7 +69,6 @@ constexpr int RING = 128;                       // pairs per epilogue warp await
 constexpr int N_RESCORERS = 4;                  // warps 2, 3, 16 and 17
 constexpr int RPR = N_EPI_WARPS / N_RESCORERS;  // rings per rescorer
 constexpr int TMEM_COLS = 512;
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;   // 2 s: far above any legitimate wait
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
 #ifndef HMM_SEED_ROWS
 #define HMM_SEED_ROWS 8192
@@ -126,6 +125,7 @@ struct TcArgs {
     int* pool_cnt;           // [nq]
     int* status;             // [0] timeout flag, [1] pool overflow flag,
                              // [2] pairs rescored, [3] threshold raises
+    uint64_t wait_ns;        // limit of every bounded wait (wait_limit_ns())
 };
 
 __device__ __forceinline__ float tau_score(uint64_t t) {
@@ -220,7 +220,7 @@ __device__ __forceinline__ float row_absmax(const unsigned char* As, int r) {
 // Every lane polls (so each observes the phase itself); the warp proceeds
 // only if all lanes saw it, keeping the warp converged either way.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint64_t limit = WAIT_LIMIT_NS) {
+                                          uint64_t limit) {
     const bool ok = mbar_wait_bounded(bar, parity, abort, limit);
     return __all_sync(0xffffffffu, ok);
 }
@@ -385,7 +385,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         int issued = 0;
         for (int i = 0; i < my_tiles; ++i) {
             const int s = i % STAGES;
-            if (!warp_wait(&ctl->a_empty[s], ((i / STAGES) & 1) ^ 1, abort)) {
+            if (!warp_wait(&ctl->a_empty[s], ((i / STAGES) & 1) ^ 1, abort, a.wait_ns)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
@@ -401,19 +401,19 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         if (*abort) {
             // drain: the latest arming of each stage must land before exit
             for (int i = max(0, issued - STAGES); i < issued; ++i)
-                mbar_wait_bounded(&ctl->a_full[i % STAGES], (i / STAGES) & 1, abort, 100000000ull);
-            mbar_wait_bounded(&ctl->b_full, 0, abort, 100000000ull);
+                mbar_wait_drain(&ctl->a_full[i % STAGES], (i / STAGES) & 1);
+            mbar_wait_drain(&ctl->b_full, 0);
         }
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
         const uint32_t idesc = idesc_f16(TC_M, TC_NMAX, 1);
         int last = -1;
-        bool ok = warp_wait(&ctl->b_full, 0, abort);
+        bool ok = warp_wait(&ctl->b_full, 0, abort, a.wait_ns);
         if (!ok && lane == 0) set_abort(ctl, a.status);
         for (int i = 0; ok && i < my_tiles; ++i) {
             const int s = i % STAGES, b = i & 1;
-            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort) ||
-                !warp_wait(&ctl->acc_empty[b], ((i >> 1) & 1) ^ 1, abort)) {
+            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort, a.wait_ns) ||
+                !warp_wait(&ctl->acc_empty[b], ((i >> 1) & 1) ^ 1, abort, a.wait_ns)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
@@ -435,14 +435,14 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             __syncwarp();
             last = i;
         }
-        if (*abort && last >= 0)
-            mbar_wait_bounded(&ctl->acc_full[last & 1], (last >> 1) & 1, abort, 100000000ull);
+        if (*abort && last >= 0)   // the MMAs issued must finish before TMEM is freed
+            mbar_wait_drain(&ctl->acc_full[last & 1], (last >> 1) & 1);
     } else if (warp >= 4 && warp < 8) {
         // ---------------------------------------------------- row-bound warps
         const int r = (warp - 4) * 32 + lane;
         for (int i = 0; i < my_tiles; ++i) {
             const int s = i % STAGES;
-            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort)) {
+            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort, a.wait_ns)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
@@ -466,7 +466,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
         for (int i = 0; i < my_tiles; ++i) {
             const int b = i & 1;
             // ---- off the critical path: the tile's row bounds are published
-            if (!warp_wait(&ctl->mr_full[i % MR_RING], (i / MR_RING) & 1, abort)) {
+            if (!warp_wait(&ctl->mr_full[i % MR_RING], (i / MR_RING) & 1, abort, a.wait_ns)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
@@ -475,7 +475,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             const float er = ctl->mrow[i % MR_RING][r];
 
             // ---- critical path: accumulator ready -> filter -> release
-            if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort)) {
+            if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort, a.wait_ns)) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
@@ -535,7 +535,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                         published = tail;
                         const uint64_t t0 = globaltimer_ns();
                         while (tail + n - ld_volatile(&ctl->ring_head[ew]) > RING) {
-                            if (*abort || globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+                            if (*abort || globaltimer_ns() - t0 >= a.wait_ns) {
                                 ring_ok = false;
                                 break;
                             }
@@ -655,7 +655,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             }
             if (__all_sync(0xffffffffu, done)) break;
             if (*abort) break;
-            if (globaltimer_ns() - last > WAIT_LIMIT_NS) {
+            if (globaltimer_ns() - last >= a.wait_ns) {
                 if (lane == 0) set_abort(ctl, a.status);
                 break;
             }
@@ -691,6 +691,18 @@ __global__ void seed_pool_kernel(const int64_t* __restrict__ seed_idx,
     if (threadIdx.x == 0) {
         cnt[q] = m;
         tau[q] = m == k ? pool[(int64_t)q * pool_cap + k - 1] : 0ull;
+    }
+}
+
+// Folds one pass's status words into a caller-owned device status word
+// (asynchronous form): bit 2 = a bounded wait gave up, bit 3 = a candidate
+// pool filled up (the pass's results are incomplete).
+__global__ void status_fold_kernel(const int* __restrict__ status, int32_t* __restrict__ dev_status) {
+    if (threadIdx.x == 0) {
+        int bits = 0;
+        if (status[0]) bits |= HMM_STATUS_TIMEOUT;
+        if (status[1]) bits |= HMM_STATUS_POOL_OVERFLOW;
+        if (bits) atomicOr(dev_status, bits);
     }
 }
 
@@ -760,10 +772,14 @@ size_t tc_ws_bytes(int64_t n, int64_t nq, int64_t k) {
 }
 
 // Scores one shard on tensor cores and returns its exact top-k (int64 rows
-// + row_offset, fp32 scores), query passes of at most 256.
+// + row_offset, fp32 scores), query passes of at most 256.  With dev_status
+// null the call reads each pass's status back (waiting for the stream) and
+// recomputes a pass whose pool filled up on the exact CUDA-core path; with
+// dev_status set it never waits, and ORs HMM_STATUS_TIMEOUT /
+// HMM_STATUS_POOL_OVERFLOW into *dev_status instead.
 hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, int64_t nq,
                           int64_t k, int64_t row_offset, int64_t* out_idx, float* out_scores,
-                          void* ws, size_t ws_bytes, cudaStream_t st) {
+                          void* ws, size_t ws_bytes, cudaStream_t st, int32_t* dev_status) {
     HMM_REQUIRE(n < (int64_t(1) << 31), "n_rows must be < 2^31");
     HMM_CUDA_TRY(cudaFuncSetAttribute(tc_score_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
@@ -819,6 +835,7 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
             a.pool = pool;
             a.pool_cnt = cnt;
             a.status = status;
+            a.wait_ns = wait_limit_ns();
             const int grid = std::max(1, std::min(sms, a.n_tiles));
             const ProfileMark pm = profile_begin(st);
             tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
@@ -831,6 +848,12 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
                               out_idx + q0 * k, out_scores + q0 * k, st);
         if (s != HMM_OK) return s;
 
+        if (dev_status) {
+            status_fold_kernel<<<1, 32, 0, st>>>(status, dev_status);
+            s = check_launch("status_fold_kernel");
+            if (s != HMM_OK) return s;
+            continue;
+        }
         // The kernel reports a bounded wait that gave up (status[0]) and a
         // query whose candidate pool filled up (status[1]; only inputs whose
         // row order makes the running k-th best climb for thousands of rows,

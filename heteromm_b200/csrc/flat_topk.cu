@@ -622,7 +622,7 @@ bool tc_path_applies(int64_t n, int64_t dim, int64_t nq, int64_t k, const void* 
 size_t tc_ws_bytes(int64_t n, int64_t nq, int64_t k);
 hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, int64_t nq,
                           int64_t k, int64_t row_offset, int64_t* out_idx, float* out_scores,
-                          void* ws, size_t ws_bytes, cudaStream_t st);
+                          void* ws, size_t ws_bytes, cudaStream_t st, int32_t* dev_status);
 
 // Scratch of hmm_ip_topk_f32_noalloc: a fixed device array, so that the
 // entry point never allocates.  Host code may not use `g_noalloc_scratch` as
@@ -632,22 +632,48 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[HMM_NOALLOC_SCR
 
 namespace {
 
+// The calling thread's current CUDA context (driver API, reached through the
+// runtime's entry-point query so that the library needs no -lcuda).
+void* current_context() {
+    using GetCurrent = int (*)(void**);
+    static GetCurrent fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetCurrent>(p);
+    });
+    void* ctx = nullptr;
+    if (fn && fn(&ctx) != 0) ctx = nullptr;
+    return ctx;
+}
+
 // Device address of g_noalloc_scratch on the current device, looked up on
-// the first call per device (with that device current) and cached.
+// the first call per device (with that device current) and cached together
+// with the context it was looked up in.  A device reset or a re-created
+// primary context reloads the module, possibly at another address, so a
+// call made in a context other than the cached one looks the address up
+// again.
 hmm_status_t noalloc_scratch_ptr(void** out) {
     static std::mutex mu;
     static void* cache[128] = {nullptr};
+    static void* cache_ctx[128] = {nullptr};
     int dev = 0;
     HMM_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 128) return set_error(HMM_ERR_UNSUPPORTED, "device id %d", dev);
+    void* ctx = current_context();
     std::lock_guard<std::mutex> lock(mu);
-    if (!cache[dev]) {
+    if (!cache[dev] || ctx == nullptr || ctx != cache_ctx[dev]) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p)
             return set_error(HMM_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s",
                              cudaGetErrorString(e));
         cache[dev] = p;
+        cache_ctx[dev] = current_context();   // the lookup made the primary context current
     }
     *out = cache[dev];
     return HMM_OK;
@@ -775,7 +801,31 @@ hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
     if (n_queries > 0 && tc_path_applies(n_rows, dim, n_queries, k, mem, queries)) {
         if (!workspace) return set_error(HMM_ERR_OOM, "workspace is null");
         return flat_bf16_tc(mem, n_rows, queries, n_queries, k, row_offset, out_idx, out_scores,
-                            workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                            workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                            nullptr);
+    }
+    return run_fused<BF16In, int64_t>(mem, n_rows, dim, queries, n_queries, k, row_offset,
+                                      out_idx, out_scores, 0.0f, nullptr, nullptr, workspace,
+                                      workspace_bytes, static_cast<cudaStream_t>(stream),
+                                      fused_ws_bytes(n_rows, n_queries, k));
+}
+
+hmm_status_t hmm_ip_topk_bf16_async(const uint16_t* mem, int64_t n_rows, int64_t dim,
+                                    const uint16_t* queries, int64_t n_queries, int64_t k,
+                                    int64_t row_offset, int64_t* out_idx, float* out_scores,
+                                    int32_t* device_status, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    HMM_REQUIRE(device_status, "device_status is null");
+    hmm_status_t s = check_common(mem, n_rows, dim, queries, n_queries, k);
+    if (s != HMM_OK) return s;
+    HMM_REQUIRE(row_offset >= 0, "row_offset must be >= 0");
+    HMM_REQUIRE(n_queries == 0 || out_scores, "out_scores is null");
+    HMM_REQUIRE(n_queries == 0 || out_idx, "out_idx is null");
+    if (n_queries > 0 && tc_path_applies(n_rows, dim, n_queries, k, mem, queries)) {
+        if (!workspace) return set_error(HMM_ERR_OOM, "workspace is null");
+        return flat_bf16_tc(mem, n_rows, queries, n_queries, k, row_offset, out_idx, out_scores,
+                            workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                            device_status);
     }
     return run_fused<BF16In, int64_t>(mem, n_rows, dim, queries, n_queries, k, row_offset,
                                       out_idx, out_scores, 0.0f, nullptr, nullptr, workspace,

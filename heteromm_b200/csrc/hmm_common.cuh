@@ -25,6 +25,9 @@ ProfileMark profile_begin(cudaStream_t st);
 void profile_end(const ProfileMark& m, cudaStream_t st);
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
+// Limit of every bounded pipeline wait of the tensor-core kernels, in ns:
+// 2 s unless hmm_debug_set_wait_limit_ns changed it.
+uint64_t wait_limit_ns();
 
 #define HMM_REQUIRE(cond, ...)                                   \
     do {                                                         \

@@ -82,7 +82,17 @@ int device_sm_count() {
     return cache[dev];
 }
 
+constexpr int64_t DEFAULT_WAIT_NS = 2000000000ll;   // far above any legitimate wait
+std::atomic<int64_t> g_wait_ns{DEFAULT_WAIT_NS};
+
+uint64_t wait_limit_ns() { return (uint64_t)g_wait_ns.load(std::memory_order_relaxed); }
+
 }  // namespace hmm
+
+extern "C" hmm_status_t hmm_debug_set_wait_limit_ns(int64_t ns) {
+    hmm::g_wait_ns.store(ns < 0 ? hmm::DEFAULT_WAIT_NS : ns, std::memory_order_relaxed);
+    return HMM_OK;
+}
 
 extern "C" const char* hmm_last_error(void) { return hmm::g_last_error; }
 

@@ -848,8 +848,18 @@ hmm_status_t read_status(const int* status, cudaStream_t st, const char* what) {
     int h = 0;
     HMM_CUDA_TRY(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, st));
     HMM_CUDA_TRY(cudaStreamSynchronize(st));
-    if (h & 1) return set_error(HMM_ERR_BOUNDS, "%s: a page-table entry is outside [0, n_pages)", what);
-    if (h & 2) return set_error(HMM_ERR_BOUNDS, "%s: a selected block id is negative", what);
+    if (h & HMM_STATUS_PAGE_BOUNDS)
+        return set_error(HMM_ERR_BOUNDS, "%s: a page-table entry is outside [0, n_pages)", what);
+    if (h & HMM_STATUS_BLOCK_BOUNDS)
+        return set_error(HMM_ERR_BOUNDS, "%s: a selected block id is negative", what);
+    if (h & HMM_STATUS_TIMEOUT)
+        return set_error(HMM_ERR_TIMEOUT, "%s: a bounded pipeline wait gave up; outputs invalid",
+                         what);
+    if (h & HMM_STATUS_POOL_OVERFLOW)
+        return set_error(HMM_ERR_UNSUPPORTED,
+                         "%s: a candidate pool filled up (rows ordered so that the k-th best "
+                         "keeps rising); outputs incomplete: recompute with hmm_ip_topk_bf16",
+                         what);
     return HMM_OK;
 }
 

@@ -73,16 +73,32 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Waits for the phase with `parity`; gives up after `limit_ns` nanoseconds of
 // wall time or when *abort becomes nonzero.  Returns false when it gave up.
+// The limit and the abort flag are checked before the first suspended
+// try_wait and then every eighth, so a limit of 0 gives up the first time the
+// phase is found incomplete.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 0;; ++i) {
-        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-        if ((i & 7u) == 7u) {
+        if ((i & 7u) == 0u) {
             if (*abort) return false;
-            if (globaltimer_ns() - t0 > limit_ns) return false;
+            if (globaltimer_ns() - t0 >= limit_ns) return false;
         }
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    }
+}
+
+// Waits for the phase with `parity` whatever any abort flag says, for at
+// most `limit_ns`: a CTA that gave up uses it to let the copies and MMAs it
+// already issued complete before it exits.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity,
+                                                uint64_t limit_ns = 100000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (globaltimer_ns() - t0 >= limit_ns) return false;
     }
 }
 

@@ -93,8 +93,12 @@ def ip_topk_f32(mem: torch.Tensor, queries: torch.Tensor, k: int, threshold: flo
     return idx, sc, bm
 
 
-def ip_topk_bf16(mem: torch.Tensor, queries: torch.Tensor, k: int, row_offset: int = 0):
-    """One shard of a bf16 memory: returns (global idx int64 [nq,k], scores fp32 [nq,k])."""
+def ip_topk_bf16(mem: torch.Tensor, queries: torch.Tensor, k: int, row_offset: int = 0,
+                 status: torch.Tensor | None = None):
+    """One shard of a bf16 memory: returns (global idx int64 [nq,k], scores fp32 [nq,k]).
+    With `status` (int32 device word, zeroed by the caller) the call never
+    waits for the stream (hmm_ip_topk_bf16_async); check_status(status) later
+    raises HmmError for a timeout or a pool overflow."""
     if mem.dtype == torch.bfloat16:
         mem = mem.view(torch.int16)
     if queries.dtype == torch.bfloat16:
@@ -107,9 +111,22 @@ def ip_topk_bf16(mem: torch.Tensor, queries: torch.Tensor, k: int, row_offset: i
     sc = torch.empty((nq, k), dtype=torch.float32, device=mem.device)
     need = load().hmm_ip_topk_bf16_workspace_size(n, d, nq, k)
     ws = workspace(need, mem.device)
-    call("hmm_ip_topk_bf16", mem.data_ptr(), n, d, q2.data_ptr(), nq, k, int(row_offset),
-         idx.data_ptr(), sc.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    if status is None:
+        call("hmm_ip_topk_bf16", mem.data_ptr(), n, d, q2.data_ptr(), nq, k, int(row_offset),
+             idx.data_ptr(), sc.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    else:
+        _check(status, torch.int32, "status")
+        call("hmm_ip_topk_bf16_async", mem.data_ptr(), n, d, q2.data_ptr(), nq, k,
+             int(row_offset), idx.data_ptr(), sc.data_ptr(), status.data_ptr(), ws.data_ptr(),
+             ws.numel(), _stream())
     return idx, sc
+
+
+def check_status(status: torch.Tensor) -> None:
+    """Waits for the stream and raises HmmError if the device status word has
+    bits set (HMM_ERR_TIMEOUT, HMM_ERR_UNSUPPORTED for a pool overflow,
+    HMM_ERR_BOUNDS for the paged kernels' bounds flags)."""
+    call("hmm_status_read", status.data_ptr(), _stream())
 
 
 def shard_merge_topk(cand_scores: torch.Tensor, cand_idx: torch.Tensor, k: int):

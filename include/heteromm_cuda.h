@@ -110,6 +110,21 @@ hmm_status_t hmm_ip_topk_bf16(const uint16_t* mem, int64_t n_rows, int64_t dim,
                               int64_t row_offset, int64_t* out_idx, float* out_scores,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same shard step without waiting for `stream` (no host synchronisation,
+ * so a caller can queue the all-gather and merge behind it).  On the
+ * tensor-core path a bounded wait that gave up sets HMM_STATUS_TIMEOUT, and
+ * a candidate pool that filled up (possible only for rows ordered so that
+ * the running k-th best keeps rising) sets HMM_STATUS_POOL_OVERFLOW, in
+ * *device_status (an int32 in device memory that the caller zeroes); the
+ * outputs are then invalid and hmm_status_read reports HMM_ERR_TIMEOUT or
+ * HMM_ERR_UNSUPPORTED.  Recompute an overflowed call with hmm_ip_topk_bf16,
+ * which falls back to the exact CUDA-core kernel by itself. */
+hmm_status_t hmm_ip_topk_bf16_async(const uint16_t* mem, int64_t n_rows, int64_t dim,
+                                    const uint16_t* queries, int64_t n_queries, int64_t k,
+                                    int64_t row_offset, int64_t* out_idx, float* out_scores,
+                                    int32_t* device_status, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
 /* Final merge of per-shard candidates after the all-gather: cand_* are
  * [n_shards][n_queries][k] (index -1 = empty slot); outputs [n_queries][k]
  * by (score desc, global index asc).  No reference counterpart: the
@@ -138,7 +153,10 @@ hmm_status_t hmm_shard_merge_topk(const float* cand_scores, const int64_t* cand_
  *     queries, k = 64) need about 2 MiB.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The address is cached per device together
+ *     with the CUDA context it belongs to; after a device reset (or any other
+ *     re-creation of the context) the next call looks it up again, and that
+ *     call, too, belongs before any stream capture.
  *   - Every call on a device shares the one array, which keeps the previous
  *     call's contents (nothing in it needs to start at zero: each call writes
  *     every slot it later reads).  Calls that overlap on the same GPU - on
@@ -265,10 +283,17 @@ hmm_status_t hmm_block_sparse_decode_bf16(const uint16_t* q, const float* summar
 
 /* The same step without waiting for `stream`: page-table entries outside
  * [0, n_pages) and negative block ids set bits in *device_status (an int32
- * in device memory the caller zeroes; bit 0 page, bit 1 block) instead of
- * making the call return HMM_ERR_BOUNDS; the kernels never follow them.
- * hmm_status_read waits for `stream` and turns such bits into
- * HMM_ERR_BOUNDS.  For decode loops that check once per many steps. */
+ * in device memory the caller zeroes; HMM_STATUS_PAGE_BOUNDS,
+ * HMM_STATUS_BLOCK_BOUNDS) instead of making the call return
+ * HMM_ERR_BOUNDS; the kernels never follow them.  hmm_status_read waits for
+ * `stream` and turns the bits of a device status word into a status:
+ * HMM_ERR_BOUNDS for the two above, HMM_ERR_TIMEOUT for HMM_STATUS_TIMEOUT,
+ * HMM_ERR_UNSUPPORTED for HMM_STATUS_POOL_OVERFLOW.  For loops that check
+ * once per many steps. */
+#define HMM_STATUS_PAGE_BOUNDS 1
+#define HMM_STATUS_BLOCK_BOUNDS 2
+#define HMM_STATUS_TIMEOUT 4
+#define HMM_STATUS_POOL_OVERFLOW 8
 hmm_status_t hmm_block_sparse_decode_bf16_async(
     const uint16_t* q, const float* summaries, const uint16_t* k_pages, const uint16_t* v_pages,
     int64_t n_pages, const int32_t* page_table, int64_t n_seq, int64_t pages_per_seq,
@@ -417,6 +442,16 @@ hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* keys, const fl
 int64_t hmm_kernel_launches(void);
 hmm_status_t hmm_profile_enable(int enable);
 hmm_status_t hmm_profile_read(double* total_ms, int64_t* launches);
+
+/* Test hook, no reference counterpart.  Sets the limit of every bounded
+ * pipeline wait inside the tensor-core kernels (tc_score_select_kernel,
+ * dsa_scores_kernel) for the calls that follow, in nanoseconds; a negative
+ * value restores the default of 2 s.  A wait that runs out makes its CTA let
+ * the copies and MMAs already in flight complete, then exit, and the entry
+ * point returns HMM_ERR_TIMEOUT with its outputs invalid.  With 0, the first
+ * wait that finds its pipeline stage not yet ready gives up: tests use it to
+ * exercise that path without a fault or a hang. */
+hmm_status_t hmm_debug_set_wait_limit_ns(int64_t ns);
 
 #ifdef __cplusplus
 }

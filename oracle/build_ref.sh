@@ -23,11 +23,13 @@
 # compiled the same way as a free function, with its ambiguous
 # `TopKIndex({})` spelled `TopKIndex(std::vector<int>{})`.
 #
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+#   (default: $HMM_REFERENCE_ROOT, else a directory named "reference" beside the
+#   repository)
 set -euo pipefail
 
-REF=${1:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
+REF=${1:-${HMM_REFERENCE_ROOT:-$(cd "$HERE/../.." && pwd)/reference}}
 OUT="$HERE/_ref"
 DEV="$REF/toolchain/frontend/dev"
 KER="$REF/kernels"

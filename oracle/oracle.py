@@ -21,12 +21,20 @@ _P = C.c_void_p
 _I = C.c_int64
 
 
+def reference_root() -> str:
+    """The reference checkout: $HMM_REFERENCE_ROOT, else a directory named
+    "reference" beside this repository."""
+    return os.environ.get("HMM_REFERENCE_ROOT") or os.path.join(
+        os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
 def build(force: bool = False) -> None:
     """Compile the oracle (gcc); compile the reference when its checkout exists."""
     if force or not os.path.exists(ORACLE_SO):
         subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if os.path.isdir("/root/reference/toolchain") and (force or not os.path.exists(REF_SO)):
-        subprocess.run([os.path.join(HERE, "build_ref.sh")], check=True,
+    ref = reference_root()
+    if os.path.isdir(os.path.join(ref, "toolchain")) and (force or not os.path.exists(REF_SO)):
+        subprocess.run([os.path.join(HERE, "build_ref.sh"), ref], check=True,
                        stdout=subprocess.DEVNULL)
 
 

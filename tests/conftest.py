@@ -7,7 +7,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
 
-REFERENCE = "/root/reference"
+# The reference checkout: $HMM_REFERENCE_ROOT, else a directory named
+# "reference" beside this repository.  Tests that read it skip when it is absent.
+REFERENCE = os.environ.get("HMM_REFERENCE_ROOT") or os.path.join(os.path.dirname(ROOT),
+                                                                 "reference")
 
 
 def pytest_configure(config):

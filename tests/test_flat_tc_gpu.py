@@ -115,8 +115,8 @@ def test_tc_normal_call_launch_count(cuda):
 
 
 def test_tc_two_pass_shard(cuda):
-    """A shard large enough for the two-pass flow (the exact top-k of the first
-    1Mi rows reseeds the pools for the rest)."""
+    """A 4Mi-row shard with a ragged last tile: the exact seed of the first
+    8,192 rows, then one tensor-core pass over the rest."""
     n, nq, k = (1 << 22) + 12345, 8, 100
     mem = gen.bf16_bits(gen.normal_f32(95, (n, 128)))
     qry = gen.bf16_bits(gen.normal_f32(96, (nq, 128)))

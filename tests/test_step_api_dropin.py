@@ -14,7 +14,9 @@ import tempfile
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_UNITTEST = "/root/reference/toolchain/frontend/dev/unittest"
+from conftest import REFERENCE  # noqa: E402
+
+REF_UNITTEST = os.path.join(REFERENCE, "toolchain", "frontend", "dev", "unittest")
 TESTS = ["test_innerproduct", "test_topk_retrieval", "test_threshold_retrieval",
          "test_paged_kv_index_builder", "test_block_sparse_attention"]
 
