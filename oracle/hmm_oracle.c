@@ -202,19 +202,66 @@ void orc_ip_topk_f32(const float* mem, int64_t n, int64_t d, const float* qry, i
 
 /* -------------------------------------------------------- bf16 (cfg 5) */
 
+/* dot_bf16 of four rows at once: four independent chains, each in the
+ * reference's order (multiply, then add, j ascending), so each result equals
+ * dot_bf16's bit for bit; only the CPU's latency is hidden. */
+static void dot_bf16_x4(const uint16_t* a, int64_t d, const float* bq, float out[4]) {
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    for (int64_t j = 0; j < d; ++j) {
+        float p0 = bf16_to_f32(a[j]) * bq[j];
+        float p1 = bf16_to_f32(a[d + j]) * bq[j];
+        float p2 = bf16_to_f32(a[2 * d + j]) * bq[j];
+        float p3 = bf16_to_f32(a[3 * d + j]) * bq[j];
+        s0 = s0 + p0;
+        s1 = s1 + p1;
+        s2 = s2 + p2;
+        s3 = s3 + p3;
+    }
+    out[0] = s0; out[1] = s1; out[2] = s2; out[3] = s3;
+}
+
+/* Exact top-k (score desc, row asc) of every query over bf16 rows.  The work
+ * is split into (query, row chunk) pieces, each an exact top-k of its chunk,
+ * merged per query: the top-k of a union is the top-k of the parts' top-ks,
+ * so the result does not depend on the split. */
 void orc_ip_topk_bf16(const uint16_t* mem, int64_t n, int64_t d, const uint16_t* qry,
                       int64_t nq, int64_t k, int64_t row_offset, int64_t* out_idx,
                       float* out_scores) {
-    int64_t q;
+    const int64_t CH = (int64_t)1 << 20;
+    const int64_t nch = n > 0 ? (n + CH - 1) / CH : 1;
+    const int64_t kk = k < n ? k : n;
+    kent_t* part = (kent_t*)malloc(sizeof(kent_t) * (size_t)(nq * nch * (kk > 0 ? kk : 1)));
+    int64_t* part_n = (int64_t*)calloc((size_t)(nq * nch), sizeof(int64_t));
+    float* qf_all = (float*)malloc(sizeof(float) * (size_t)(nq * d + 1));
+    int64_t w, q;
+    for (int64_t i = 0; i < nq * d; ++i) qf_all[i] = bf16_to_f32(qry[i]);
+#pragma omp parallel for schedule(dynamic)
+    for (w = 0; w < nq * nch; ++w) {
+        const int64_t qq = w / nch, c = w % nch;
+        const int64_t r0 = c * CH, r1 = r0 + CH < n ? r0 + CH : n;
+        const float* qf = qf_all + qq * d;
+        topk_t t;
+        int64_t i = r0;
+        topk_init(&t, kk);
+        for (; i + 4 <= r1; i += 4) {
+            float s4[4];
+            dot_bf16_x4(mem + i * d, d, qf, s4);
+            for (int u = 0; u < 4; ++u) topk_push(&t, orc_f32_key(s4[u]), i + u);
+        }
+        for (; i < r1; ++i) topk_push(&t, orc_f32_key(dot_bf16(mem + i * d, qf, d)), i);
+        part_n[w] = topk_finish(&t);
+        memcpy(part + w * kk, t.h, sizeof(kent_t) * (size_t)part_n[w]);
+        topk_free(&t);
+    }
 #pragma omp parallel for schedule(dynamic)
     for (q = 0; q < nq; ++q) {
-        float* qf = (float*)malloc(sizeof(float) * (size_t)d);
+        const float* qf = qf_all + q * d;
         topk_t t;
-        int64_t m, kk = k < n ? k : n;
-        for (int64_t j = 0; j < d; ++j) qf[j] = bf16_to_f32(qry[q * d + j]);
+        int64_t m;
         topk_init(&t, kk);
-        for (int64_t i = 0; i < n; ++i)
-            topk_push(&t, orc_f32_key(dot_bf16(mem + i * d, qf, d)), i);
+        for (int64_t c = 0; c < nch; ++c)
+            for (int64_t i = 0; i < part_n[q * nch + c]; ++i)
+                topk_push(&t, part[(q * nch + c) * kk + i].key, part[(q * nch + c) * kk + i].idx);
         m = topk_finish(&t);
         for (int64_t i = 0; i < k; ++i) {
             int64_t r = i < m ? t.h[i].idx : -1;
@@ -222,8 +269,10 @@ void orc_ip_topk_bf16(const uint16_t* mem, int64_t n, int64_t d, const uint16_t*
             out_scores[q * k + i] = r >= 0 ? dot_bf16(mem + r * d, qf, d) : -INFINITY;
         }
         topk_free(&t);
-        free(qf);
     }
+    free(part);
+    free(part_n);
+    free(qf_all);
 }
 
 void orc_shard_merge_topk(const float* cand_scores, const int64_t* cand_idx,
