@@ -19,9 +19,11 @@
 //               thread = key; per token, sum_h w * max(x, 0) over the
 //               token's head columns (weights staged in shared memory per
 //               warp and group), causal mask, coalesced fp32 score rows
-// The top-k over each token's score row is the flat top-k kernel
-// (hmm_topk_f32).  Scores are fp32 tensor-core sums of exact e4m3 products;
-// they differ from the exact dot products by the accumulation's rounding.
+// Scores are fp32 tensor-core sums of exact e4m3 products; they differ from
+// the exact dot products by the accumulation's rounding.  The selection is
+// exact: dsa_exact.cu takes each token's band of keys whose score could reach
+// the k-th, rescores them exactly (integer limbs on the tensor cores) and
+// selects the top-k from the exact scores.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -337,168 +339,16 @@ hmm_status_t make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int bo
     return HMM_OK;
 }
 
-// Exact top-k of each score row for long rows and large k (one block of 512
-// threads per row: twice the loads in flight of 256, at the same shared memory).  A strided sample of RT_SAMPLE scores gives a lower
-// threshold expected to pass ~2k scores; one read of the row gathers every
-// (score key, ~index) composite at or above it into shared memory; a radix
-// select finds the k-th composite among them and the k best are sorted.  If
-// fewer than k scores pass or more than RT_CAP do, the row is flagged
-// (status bit 1) and the caller reruns the general top-k.  The result equals
-// hmm_topk_f32's: best first, ties to the lowest index.
-constexpr int RT_THREADS = 512;
-constexpr int RT_SAMPLE = 4096;
-constexpr int RT_CAP = 8192;
-constexpr int RT_KMAX = 4096;
-constexpr size_t RT_SMEM = sizeof(uint64_t) * (RT_CAP + RT_KMAX);
-
-// Block-wide inclusive scan of one value per thread for NT threads (a
-// multiple of 32, at most 1024); warp_tot holds NT / 32 words.
-template <int NT>
-__device__ __forceinline__ unsigned rt_scan_incl(unsigned v, unsigned* warp_tot) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const unsigned t = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += t;
-    }
-    if (lane == 31) warp_tot[w] = v;
-    __syncthreads();
-    if (w == 0) {
-        unsigned t = lane < NT / 32 ? warp_tot[lane] : 0u;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned u = __shfl_up_sync(0xffffffffu, t, o);
-            if (lane >= o) t += u;
-        }
-        if (lane < NT / 32) warp_tot[lane] = t;
-    }
-    __syncthreads();
-    const unsigned r = v + (w > 0 ? warp_tot[w - 1] : 0u);
-    __syncthreads();
-    return r;
-}
-
-// block_select_threshold for NT threads (a multiple of 256): the threshold T
-// such that exactly min(k, M) keys are >= T among keys[0, M) (0 if k >= M).
-// sm holds >= 256 + 32 + 3 words.
-template <int NT>
-__device__ __forceinline__ uint64_t rt_select_threshold(const uint64_t* keys, int64_t M, int64_t k,
-                                                        unsigned* sm) {
-    unsigned* hist = sm;          // 256
-    unsigned* wt = sm + 256;      // NT / 32
-    unsigned* res = sm + 288;     // 3
-    if (k >= M) return 0ull;
-    uint64_t prefix = 0, mask = 0;
-    unsigned need = (unsigned)k;
-    for (int shift = 56; shift >= 0; shift -= 8) {
-        if (threadIdx.x < 256) hist[threadIdx.x] = 0;
-        __syncthreads();
-        for (int64_t i = threadIdx.x; i < M; i += NT) {
-            const uint64_t key = keys[i];
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1u);
-        }
-        __syncthreads();
-        const unsigned c = threadIdx.x < 256 ? hist[255 - threadIdx.x] : 0u;
-        const unsigned incl = rt_scan_incl<NT>(c, wt);
-        const unsigned excl = incl - c;
-        if (threadIdx.x < 256 && excl < need && need <= incl) {
-            res[0] = 255 - threadIdx.x; res[1] = excl; res[2] = c;
-        }
-        __syncthreads();
-        const unsigned bucket = res[0], before = res[1], cnt = res[2];
-        need -= before;
-        prefix |= (uint64_t)bucket << shift;
-        mask |= (uint64_t)0xff << shift;
-        __syncthreads();
-        if (cnt == need) break;
-    }
-    return prefix;
-}
-
-__global__ void __launch_bounds__(RT_THREADS) dsa_row_topk_kernel(const float* __restrict__ scores,
-                                                                  int64_t L, int k,
-                                                                  int32_t* __restrict__ out_idx,
-                                                                  float* __restrict__ out_sc,
-                                                                  int* status) {
-    extern __shared__ uint64_t rsm[];
-    uint64_t* cand = rsm;              // RT_CAP
-    uint64_t* best = rsm + RT_CAP;     // RT_KMAX: the sample, then the k best
-    __shared__ unsigned sm[320];
-    __shared__ int cnt;
-    const int64_t t = blockIdx.x;
-    const float* row = scores + t * L;
-
-    for (int i = threadIdx.x; i < RT_SAMPLE; i += RT_THREADS) {
-        const int64_t j = (int64_t)i * L / RT_SAMPLE;
-        best[i] = make_cand(f32_key(row[j]), (uint32_t)j);
-    }
-    if (threadIdx.x == 0) cnt = 0;
-    __syncthreads();
-    const int64_t r = min((int64_t)RT_SAMPLE - 1, 2 * (int64_t)k * RT_SAMPLE / L + 32);
-    const uint64_t ts = rt_select_threshold<RT_THREADS>(best, RT_SAMPLE, r + 1, sm);
-    const uint32_t tlo = (uint32_t)(ts >> 32);
-    __syncthreads();
-
-    auto take = [&](float v, int64_t j) {
-        const uint32_t key = f32_key(v);
-        if (key >= tlo) {
-            const int pos = atomicAdd(&cnt, 1);
-            if (pos < RT_CAP) cand[pos] = make_cand(key, (uint32_t)j);
-        }
-    };
-    if ((L & 3) == 0) {
-        const float4* row4 = reinterpret_cast<const float4*>(row);
-        const int64_t L4 = L >> 2;
-        for (int64_t b = threadIdx.x; b < L4; b += RT_THREADS * 4) {
-            float4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int64_t j4 = b + (int64_t)u * RT_THREADS;
-                v[u] = j4 < L4 ? __ldg(row4 + j4)
-                               : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int64_t j4 = b + (int64_t)u * RT_THREADS;
-                if (j4 < L4) {
-                    take(v[u].x, 4 * j4 + 0);
-                    take(v[u].y, 4 * j4 + 1);
-                    take(v[u].z, 4 * j4 + 2);
-                    take(v[u].w, 4 * j4 + 3);
-                }
-            }
-        }
-    } else {
-        for (int64_t j = threadIdx.x; j < L; j += RT_THREADS) take(__ldg(row + j), j);
-    }
-    __syncthreads();
-    const int C = cnt;
-    if (C < k || C > RT_CAP) {
-        if (threadIdx.x == 0) atomicOr(&status[1], 1);
-        return;
-    }
-    const uint64_t T = rt_select_threshold<RT_THREADS>(cand, C, k, sm);   // exactly k composites >= T
-    __syncthreads();
-    const int kp = next_pow2(k);
-    for (int i = threadIdx.x; i < kp; i += RT_THREADS) best[i] = 0ull;
-    if (threadIdx.x == 0) cnt = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < C; i += RT_THREADS)
-        if (cand[i] >= T) best[atomicAdd(&cnt, 1)] = cand[i];
-    __syncthreads();
-    block_bitonic_sort_desc(best, kp);
-    for (int i = threadIdx.x; i < k; i += RT_THREADS) {
-        const uint64_t c = best[i];
-        out_idx[t * k + i] = c ? (int32_t)cand_row(c) : -1;
-        out_sc[t * k + i] = c ? cand_score(c) : -INFINITY;
-    }
-}
-
 // Selections of keys nobody can see (score -inf: fewer visible keys than k)
 // become -1, as the reference returns only min(k, visible) indices.
 __global__ void dsa_pad_kernel(int32_t* __restrict__ idx, float* __restrict__ sc, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n && sc[i] == -INFINITY) idx[i] = -1;
+}
+
+__global__ void dsa_fill_kernel(float* __restrict__ sc, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) sc[i] = -INFINITY;
 }
 
 size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -508,12 +358,22 @@ size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 
 using namespace hmm;
 
+namespace hmm {
+size_t dsa_exact_ws_bytes(int64_t T, int64_t L);
+hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* ws,
+                               cudaStream_t st, int** status_out);
+hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float* w, int64_t T,
+                              int64_t H, int64_t L, int64_t pos0, int64_t topk, float* scores,
+                              int32_t* out_idx, float* out_sc, void* ws, void* topk_ws,
+                              size_t topk_ws_bytes, cudaStream_t st);
+}  // namespace hmm
+
 extern "C" size_t hmm_dsa_indexer_fp8_workspace_size(int64_t T, int64_t H, int64_t L,
                                                      int64_t topk) {
     if (T < 0 || H < 1 || L < 0 || topk < 1) return 0;
-    return up256(sizeof(float) * (size_t)T * (size_t)L) + 256 +
+    return up256(sizeof(float) * (size_t)T * (size_t)L) + up256(dsa_exact_ws_bytes(T, L)) +
            up256(sizeof(float) * (size_t)T * (size_t)topk) +
-           hmm_topk_f32_workspace_size(L, T, topk);
+           hmm_topk_f32_workspace_size(L, 1, topk);
 }
 
 extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* keys,
@@ -538,75 +398,62 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     const size_t sc_bytes = all_scores ? 0 : up256(sizeof(float) * (size_t)T * (size_t)L);
+    const size_t ex_bytes = up256(dsa_exact_ws_bytes(T, L));
     const size_t sel_bytes = up256(sizeof(float) * (size_t)T * (size_t)topk);
-    const size_t tk_bytes = hmm_topk_f32_workspace_size(L, T, topk);
-    const size_t need = sc_bytes + 256 + sel_bytes + tk_bytes;
+    const size_t tk_bytes = hmm_topk_f32_workspace_size(L, 1, topk);
+    const size_t need = sc_bytes + ex_bytes + sel_bytes + tk_bytes;
     if (!ws || workspace_bytes < need)
         return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", workspace_bytes, need);
     float* scores = all_scores ? all_scores : reinterpret_cast<float*>(ws);
-    int* status = reinterpret_cast<int*>(ws + sc_bytes);
-    float* sel_sc = out_scores ? out_scores : reinterpret_cast<float*>(ws + sc_bytes + 256);
-    void* tk_ws = ws + sc_bytes + 256 + sel_bytes;
-
-    if (L > 0) {
-        HMM_CUDA_TRY(cudaMemsetAsync(status, 0, 2 * sizeof(int), st));
-        CUtensorMap tmK, tmQ;
-        hmm_status_t s = make_tmap_u8(&tmK, keys, L, KT);
-        if (s != HMM_OK) return s;
-        s = make_tmap_u8(&tmQ, q, T * H, NQ);
-        if (s != HMM_OK) return s;
-        DsaArgs a;
-        a.w = w;
-        a.scores = scores;
-        a.status = status;
-        a.T = T;
-        a.L = L;
-        a.pos0 = pos0;
-        a.H = (int)H;
-        a.tg = NQ / (int)H;
-        a.n_groups = (int)((T + a.tg - 1) / a.tg);
-        a.key_tiles = (int)((L + KT - 1) / KT);
-        a.wait_ns = wait_limit_ns();
-        auto kern = H == 64 ? dsa_scores_kernel<64> : H == 32 ? dsa_scores_kernel<32>
-                                                              : dsa_scores_kernel<16>;
-        HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)D_SMEM));
-        const int grid = std::max(1, std::min(device_sm_count(), a.n_groups));
-        const ProfileMark pm = profile_begin(st);
-        kern<<<grid, D_THREADS, D_SMEM, st>>>(tmK, tmQ, a);
-        s = check_launch("dsa_scores_kernel");
-        profile_end(pm, st);
-        if (s != HMM_OK) return s;
-        dsa_tail_kernel<<<dim3(16, (unsigned)T), 256, 0, st>>>(scores, T, L, pos0, a.tg,
-                                                               a.key_tiles);
-        s = check_launch("dsa_tail_kernel");
-        if (s != HMM_OK) return s;
-    }
+    void* ex_ws = ws + sc_bytes;
+    float* sel_sc = out_scores ? out_scores : reinterpret_cast<float*>(ws + sc_bytes + ex_bytes);
+    void* tk_ws = ws + sc_bytes + ex_bytes + sel_bytes;
     const int64_t n_sel = T * topk;
-    // long rows: the sampled per-row selection; otherwise (or for a row it
-    // flags) the general top-k
-    const bool row_path = L >= 16 * topk && L >= RT_SAMPLE;
-    if (row_path) {
-        HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_row_topk_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)RT_SMEM));
-        dsa_row_topk_kernel<<<(unsigned)T, RT_THREADS, RT_SMEM, st>>>(scores, L, (int)topk,
-                                                                      out_idx, sel_sc, status);
-        hmm_status_t s = check_launch("dsa_row_topk_kernel");
-        if (s != HMM_OK) return s;
+
+    if (L == 0) {   // no key is visible to any token
+        HMM_CUDA_TRY(cudaMemsetAsync(out_idx, 0xff, sizeof(int32_t) * (size_t)n_sel, st));
+        dsa_fill_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(sel_sc, n_sel);
+        return check_launch("dsa_fill_kernel");
     }
-    int h[2] = {0, 0};
-    if (L > 0) {
-        HMM_CUDA_TRY(cudaMemcpyAsync(h, status, sizeof(h), cudaMemcpyDeviceToHost, st));
-        HMM_CUDA_TRY(cudaStreamSynchronize(st));
-        if (h[0])
-            return set_error(HMM_ERR_TIMEOUT,
-                             "dsa_scores_kernel: a bounded pipeline wait gave up; outputs invalid");
-    }
-    if (!row_path || h[1]) {
-        hmm_status_t s = hmm_topk_f32(scores, L, T, topk, out_idx, sel_sc, tk_ws, tk_bytes, st);
-        if (s != HMM_OK) return s;
-    }
+    int* status = nullptr;
+    hmm_status_t s = dsa_exact_prepare(keys, T, L, ex_ws, st, &status);
+    if (s != HMM_OK) return s;
+    CUtensorMap tmK, tmQ;
+    s = make_tmap_u8(&tmK, keys, L, KT);
+    if (s != HMM_OK) return s;
+    s = make_tmap_u8(&tmQ, q, T * H, NQ);
+    if (s != HMM_OK) return s;
+    DsaArgs a;
+    a.w = w;
+    a.scores = scores;
+    a.status = status;   // [0]: a bounded wait gave up
+    a.T = T;
+    a.L = L;
+    a.pos0 = pos0;
+    a.H = (int)H;
+    a.tg = NQ / (int)H;
+    a.n_groups = (int)((T + a.tg - 1) / a.tg);
+    a.key_tiles = (int)((L + KT - 1) / KT);
+    a.wait_ns = wait_limit_ns();
+    auto kern = H == 64 ? dsa_scores_kernel<64> : H == 32 ? dsa_scores_kernel<32>
+                                                          : dsa_scores_kernel<16>;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)D_SMEM));
+    const int grid = std::max(1, std::min(device_sm_count(), a.n_groups));
+    const ProfileMark pm = profile_begin(st);
+    kern<<<grid, D_THREADS, D_SMEM, st>>>(tmK, tmQ, a);
+    s = check_launch("dsa_scores_kernel");
+    profile_end(pm, st);
+    if (s != HMM_OK) return s;
+    dsa_tail_kernel<<<dim3(16, (unsigned)T), 256, 0, st>>>(scores, T, L, pos0, a.tg,
+                                                           a.key_tiles);
+    s = check_launch("dsa_tail_kernel");
+    if (s != HMM_OK) return s;
+    // exact selection over the approximate scores (reads the status words, so
+    // this waits for the stream), then -1 for the slots of keys nobody sees
+    s = dsa_exact_select(q, keys, w, T, H, L, pos0, topk, scores, out_idx, sel_sc, ex_ws, tk_ws,
+                         tk_bytes, st);
+    if (s != HMM_OK) return s;
     dsa_pad_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(out_idx, sel_sc, n_sel);
     return check_launch("dsa_pad_kernel");
 }

@@ -1,0 +1,828 @@
+// dsa_exact.cu — exact selection for the FP8 DSA lightning indexer.
+//
+// Reference: indexer_top_ref (kernels/dsa_indexer/indexer_tb.cpp:27-56): per
+// key j, total = sum over heads h (in order) of w[h] * (float)ReLU(q_h . k_j)
+// with the dot exact, then the TOP_K best keys, best first.  With e4m3 inputs
+// the exact dot is an integer multiple of 2^-18, so that arithmetic is:
+//   x_h = fl32(ReLU(D_h) * 2^-18),  total = fl32(total + fl32(w_h * x_h)).
+//
+// The tensor-core pass (dsa.cu) gives approximate scores s~ with
+//   |s~ - s| <= C_TOL * sum_h |w_h| sum_d |q_hd| |k_jd|
+//            <= C_TOL * ||u_t||_2 * ||k_j||_2,  u_t[d] = sum_h |w_h| |q_hd|
+// where C_TOL covers the tensor core's fp32 accumulation (assumed to lose at
+// most 2^-10 of sum_d |q_hd||k_jd|, 128x the worst case of sequential fp32;
+// measured below 2e-5 of that) and the fp32 roundings of both head sums.
+// Then, per query token:
+//   1. dsa_band_kernel: lo_j = s~_j - tol_j, hi_j = s~_j + tol_j; L_k = the
+//      k-th largest lo.  Every key of the exact top-k has hi >= L_k (k keys
+//      have s >= lo >= L_k, so the exact k-th score is >= L_k), so the keys
+//      with hi_j >= L_k are the candidates.
+//   2. dsa_rescore_kernel: the candidates' exact scores on the tensor cores
+//      (tcgen05.mma kind::i8, exact int32 accumulation): every e4m3 value
+//      times 2^9 is an integer v, |v| <= 229,376, split into three signed
+//      6-bit limbs v = l0 + 64 l1 + 4096 l2; the nine limb products are summed
+//      in five TMEM accumulators by the scale 64^(i+i') they carry and joined
+//      exactly in 64-bit integers; the head sum is then the reference's.
+//   3. dsa_select_kernel: the exact top-k of the candidates, best first,
+//      ties to the lowest key.
+// A token whose band does not fit (possible only for near-identical keys,
+// whose scores crowd the k-th) is flagged; the host recomputes its whole row
+// exactly on CUDA cores (dsa_exact_row_kernel) and selects from that.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "heteromm_cuda.h"
+#include "hmm_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace hmm {
+using namespace sm100;
+
+namespace {
+
+constexpr int DK = 128;                    // head dim: bytes per fp8 row and per limb row
+constexpr int NLIMB = 3;
+constexpr int KEY_LIMB_BYTES = NLIMB * DK; // 384 bytes of limbs per key
+constexpr int CAP_C = 8192;                // candidates per token
+constexpr int BAND_THREADS = 512;
+constexpr int BAND_SAMPLE = 4096;
+constexpr int BAND_COLLECT = 8192;         // keys with hi >= the sampled threshold
+constexpr int SEL_THREADS = 512;
+constexpr int KMAX = 4096;
+// C_TOL: 2^-10 for the tensor-core accumulation plus 2^-16, which covers the
+// fp32 roundings of x_h and of both head sums (about 100 * 2^-24).
+constexpr double C_TOL = 1.0 / 1024.0 + 1.0 / 65536.0;
+
+// Status words (int) at the start of the selection workspace.
+enum { ST_TIMEOUT = 0, ST_NAN = 1, ST_NFLAG = 2, ST_FLAGS = 4 };   // ST_FLAGS: T token ids
+
+// e4m3 (OCP FP8: bias 7, no infinities, S.1111.111 = NaN) times 2^9 as an
+// integer; the NaN encodings give 0 and are reported by the callers.
+__device__ __forceinline__ int e4m3_scaled(uint32_t b) {
+    const int e = (int)((b >> 3) & 15u), m = (int)(b & 7u);
+    if (e == 15 && m == 7) return 0;
+    const int mag = e == 0 ? m : (8 + m) << (e - 1);
+    return (b & 0x80u) ? -mag : mag;
+}
+__device__ __forceinline__ bool e4m3_is_nan(uint32_t b) { return (b & 0x7fu) == 0x7fu; }
+
+// Limb i of v (signed 6-bit pieces of |v|, carrying v's sign), as a byte.
+__device__ __forceinline__ uint32_t limb_byte(int v, int i) {
+    const int a = v < 0 ? -v : v;
+    int l = (a >> (6 * i)) & (i == 2 ? 0xff : 63);
+    if (v < 0) l = -l;
+    return (uint32_t)(l & 0xff);
+}
+
+// Limbs of 4 e4m3 bytes packed in w: three 32-bit words (limb 0, 1, 2), byte
+// order kept.  *nan is set if a byte is a NaN encoding.
+__device__ __forceinline__ void limbs4(uint32_t w, uint32_t out[3], bool* nan) {
+    out[0] = out[1] = out[2] = 0u;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t byte = (w >> (8 * b)) & 0xffu;
+        *nan |= e4m3_is_nan(byte);
+        const int v = e4m3_scaled(byte);
+#pragma unroll
+        for (int i = 0; i < NLIMB; ++i) out[i] |= limb_byte(v, i) << (8 * b);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// K0: per key, its limb rows [3][128] (int8) and ||k_j||_2 rounded up; flags
+// NaN encodings.  One warp per key, 4 bytes per lane.
+__global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
+                                    uint8_t* __restrict__ limbs, float* __restrict__ knorm,
+                                    int* __restrict__ status) {
+    const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (j >= L) return;
+    const uint32_t w = reinterpret_cast<const uint32_t*>(keys + j * DK)[lane];
+    uint32_t l[3];
+    bool nan = false;
+    limbs4(w, l, &nan);
+#pragma unroll
+    for (int i = 0; i < NLIMB; ++i)
+        reinterpret_cast<uint32_t*>(limbs + j * KEY_LIMB_BYTES + i * DK)[lane] = l[i];
+    long long sq = 0;   // sum of v^2 (v = value * 2^9): exact in 64 bits
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const long long v = e4m3_scaled((w >> (8 * b)) & 0xffu);
+        sq += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(&status[ST_NAN], 1);
+    if (lane == 0) knorm[j] = __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0));
+}
+
+// ---------------------------------------------------------------------------
+// K2: the candidate band of each token (one block per token).
+
+template <int NT>
+__device__ __forceinline__ unsigned band_scan_incl(unsigned v, unsigned* warp_tot) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    if (lane == 31) warp_tot[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        unsigned t = lane < NT / 32 ? warp_tot[lane] : 0u;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned u = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += u;
+        }
+        if (lane < NT / 32) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const unsigned r = v + (w > 0 ? warp_tot[w - 1] : 0u);
+    __syncthreads();
+    return r;
+}
+
+// Threshold T such that exactly min(k, M) of the distinct nonzero composites
+// keys[0, M) are >= T (0 if k >= M); NT threads; sm >= 256 + NT/32 + 3 words.
+template <int NT>
+__device__ __forceinline__ uint64_t band_select(const uint64_t* keys, int64_t M, int64_t k,
+                                                unsigned* sm) {
+    unsigned* hist = sm;
+    unsigned* wt = sm + 256;
+    unsigned* res = sm + 256 + NT / 32;
+    if (k >= M) return 0ull;
+    uint64_t prefix = 0, mask = 0;
+    unsigned need = (unsigned)k;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        if (threadIdx.x < 256) hist[threadIdx.x] = 0;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < M; i += NT) {
+            const uint64_t key = keys[i];
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1u);
+        }
+        __syncthreads();
+        const unsigned c = threadIdx.x < 256 ? hist[255 - threadIdx.x] : 0u;
+        const unsigned incl = band_scan_incl<NT>(c, wt);
+        const unsigned excl = incl - c;
+        if (threadIdx.x < 256 && excl < need && need <= incl) {
+            res[0] = 255 - threadIdx.x; res[1] = excl; res[2] = c;
+        }
+        __syncthreads();
+        const unsigned bucket = res[0], before = res[1], cnt = res[2];
+        need -= before;
+        prefix |= (uint64_t)bucket << shift;
+        mask |= (uint64_t)0xff << shift;
+        __syncthreads();
+        if (cnt == need) break;
+    }
+    return prefix;
+}
+
+struct BandArgs {
+    const float* scores;     // [T][L] approximate scores (tensor-core pass)
+    const uint8_t* q;        // [T][H][128] e4m3
+    const float* w;          // [T][H]
+    const float* knorm;      // [L]
+    int32_t* cand;           // [T][CAP_C] candidate keys
+    int* cand_cnt;           // [T]
+    int* status;
+    int64_t T, L, pos0;
+    int H, k;
+};
+
+__device__ __forceinline__ void band_flag(const BandArgs& a, int64_t t) {
+    const int pos = atomicAdd(&a.status[ST_NFLAG], 1);
+    if (pos < a.T) a.status[ST_FLAGS + pos] = (int)t;
+}
+
+__global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a) {
+    extern __shared__ uint64_t bsm[];
+    uint64_t* col = bsm;                    // BAND_COLLECT: (f32_key(s~) << 32) | j
+    uint64_t* lok = bsm + BAND_COLLECT;     // BAND_COLLECT: lo composites; first the sample
+    __shared__ unsigned sm[256 + BAND_THREADS / 32 + 4];
+    __shared__ double ured[BAND_THREADS / 32];
+    __shared__ int cnt, cnt_lo, out_n, nan_seen;
+    __shared__ float e_t;
+    const int64_t t = blockIdx.x;
+    const int64_t vis = max((int64_t)0, min(a.L, a.pos0 + t + 1));
+    const int m = (int)min((int64_t)a.k, vis);
+    int32_t* cand = a.cand + t * CAP_C;
+    if (threadIdx.x == 0) { cnt = 0; cnt_lo = 0; out_n = 0; nan_seen = 0; }
+    __syncthreads();
+
+    // E_t = C_TOL * ||u_t||_2 (rounded up), u_t[d] = sum_h |w_h| |q_hd|
+    {
+        double part = 0.0;
+        const uint8_t* qt = a.q + t * (int64_t)a.H * DK;
+        const float* wt = a.w + t * a.H;
+        bool nan = false;
+        for (int d = threadIdx.x; d < DK; d += BAND_THREADS) {
+            double u = 0.0;
+            for (int h = 0; h < a.H; ++h) {
+                const uint32_t b = qt[h * DK + d];
+                nan |= e4m3_is_nan(b);
+                const int v = e4m3_scaled(b);
+                u = __dadd_ru(u, __dmul_ru(fabs((double)wt[h]), (double)(v < 0 ? -v : v)));
+            }
+            part = __dadd_ru(part, __dmul_ru(u, u));
+        }
+        if (nan) atomicOr(&nan_seen, 1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part = __dadd_ru(part, __shfl_xor_sync(0xffffffffu, part, o));
+        if ((threadIdx.x & 31) == 0) ured[threadIdx.x >> 5] = part;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double s = 0.0;
+            for (int i = 0; i < BAND_THREADS / 32; ++i) s = __dadd_ru(s, ured[i]);
+            // ||u|| in real units: v = value * 2^9
+            e_t = __double2float_ru(__dmul_ru(__dmul_ru(__dsqrt_ru(s), 1.0 / 512.0), C_TOL));
+            if (nan_seen) atomicOr(&a.status[ST_NAN], 1);
+        }
+        __syncthreads();
+    }
+    const float E = e_t;
+
+    if (vis <= CAP_C) {   // short rows: every visible key is a candidate
+        for (int64_t j = threadIdx.x; j < vis; j += BAND_THREADS) cand[j] = (int32_t)j;
+        if (threadIdx.x == 0) a.cand_cnt[t] = (int)vis;
+        return;
+    }
+    const float* row = a.scores + t * a.L;
+    auto lo_of = [&](float s, int64_t j) { return __fsub_rd(s, __fmul_ru(E, a.knorm[j])); };
+    auto hi_of = [&](float s, int64_t j) { return __fadd_ru(s, __fmul_ru(E, a.knorm[j])); };
+
+    // 1. a threshold tau on lo, from a strided sample, expected to leave about
+    //    2k keys above it
+    for (int i = threadIdx.x; i < BAND_SAMPLE; i += BAND_THREADS) {
+        const int64_t j = (int64_t)i * vis / BAND_SAMPLE;
+        lok[i] = make_cand(f32_key(lo_of(row[j], j)), (uint32_t)j);
+    }
+    __syncthreads();
+    const int64_t r = min((int64_t)BAND_SAMPLE - 1, 2 * (int64_t)m * BAND_SAMPLE / vis + 32);
+    const uint64_t tau = band_select<BAND_THREADS>(lok, BAND_SAMPLE, r + 1, sm);
+    const uint32_t tau_key = (uint32_t)(tau >> 32);
+    __syncthreads();
+
+    // 2. one read of the row: collect every key whose hi reaches tau; count the
+    //    keys whose lo does (all of those are collected, as hi >= lo)
+    for (int64_t j = threadIdx.x; j < vis; j += BAND_THREADS) {
+        const float s = row[j];
+        if (f32_key(hi_of(s, j)) >= tau_key) {
+            const int pos = atomicAdd(&cnt, 1);
+            if (pos < BAND_COLLECT) col[pos] = ((uint64_t)f32_key(s) << 32) | (uint64_t)j;
+            if (make_cand(f32_key(lo_of(s, j)), (uint32_t)j) >= tau) atomicAdd(&cnt_lo, 1);
+        }
+    }
+    __syncthreads();
+    const int C = cnt;
+    if (C > BAND_COLLECT || cnt_lo < m) {   // the sample's threshold was off: exact row instead
+        if (threadIdx.x == 0) { band_flag(a, t); a.cand_cnt[t] = 0; }
+        return;
+    }
+    // 3. L_k: the m-th largest lo composite among the collected keys (every key
+    //    with lo >= tau is among them, and at least m are)
+    for (int i = threadIdx.x; i < C; i += BAND_THREADS) {
+        const uint64_t e = col[i];
+        const int64_t j = (int64_t)(uint32_t)e;
+        lok[i] = make_cand(f32_key(lo_of(key_to_f32((uint32_t)(e >> 32)), j)), (uint32_t)j);
+    }
+    __syncthreads();
+    const uint64_t Lk = band_select<BAND_THREADS>(lok, C, m, sm);
+    const uint32_t lk_key = (uint32_t)(Lk >> 32);
+    __syncthreads();
+    // 4. the candidates: hi_j >= L_k's lo score
+    for (int i = threadIdx.x; i < C; i += BAND_THREADS) {
+        const uint64_t e = col[i];
+        const int64_t j = (int64_t)(uint32_t)e;
+        if (f32_key(hi_of(key_to_f32((uint32_t)(e >> 32)), j)) >= lk_key) {
+            const int pos = atomicAdd(&out_n, 1);
+            if (pos < CAP_C) cand[pos] = (int32_t)j;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (out_n > CAP_C) {
+            band_flag(a, t);
+            a.cand_cnt[t] = 0;
+        } else {
+            a.cand_cnt[t] = out_n;
+        }
+    }
+}
+
+constexpr size_t BAND_SMEM = sizeof(uint64_t) * 2 * BAND_COLLECT;
+
+// ---------------------------------------------------------------------------
+// K3: exact scores of the candidates on the tensor cores.
+
+constexpr int R_M = 128;                         // candidates per tile (MMA M)
+constexpr int R_STAGES = 3;
+constexpr int R_A_LIMB = R_M * DK;               // 16 KB: one limb of a tile
+constexpr int R_A_STAGE = NLIMB * R_A_LIMB;      // 48 KB
+constexpr int R_PROD_WARPS = 4;
+constexpr int R_THREADS = 32 * 12;               // producers 0-3, MMA 4, TMEM 5, epilogue 8-11
+constexpr int R_SLOTS = 8;                       // accumulator slots of H columns (a ring)
+constexpr int R_GROUPS = 5;                      // limb scales 64^0 .. 64^4
+
+template <int H>
+struct RescoreSmem {
+    static constexpr int Q_LIMB = H * DK;            // one query limb (H rows of 128 B)
+    static constexpr int Q_BUF = NLIMB * Q_LIMB;
+    static constexpr size_t A_OFF = 0;
+    static constexpr size_t Q_OFF = A_OFF + (size_t)R_STAGES * R_A_STAGE;
+    static constexpr size_t W_OFF = Q_OFF + 2 * (size_t)Q_BUF;
+    static constexpr size_t CTRL_OFF = W_OFF + 2 * H * sizeof(float);
+    static constexpr size_t BYTES = CTRL_OFF + 256 + 1024;   // + barriers, + alignment slack
+};
+
+struct RescoreCtrl {
+    uint64_t a_full[R_STAGES], a_empty[R_STAGES];
+    uint64_t q_full[2], q_empty[2];
+    uint64_t acc_full;
+    uint64_t slot_empty[R_SLOTS];
+    uint64_t drain;                  // MMA warp: every MMA issued has completed (abort path)
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct RescoreArgs {
+    const uint8_t* q;          // [T][H][128] e4m3
+    const float* w;            // [T][H]
+    const uint8_t* klimbs;     // [L][3][128]
+    const int32_t* cand;       // [T][CAP_C]
+    const int* cand_cnt;       // [T]
+    float* exact;              // [T][CAP_C] exact scores of the candidates
+    int* status;
+    int64_t T;
+    uint64_t wait_ns;
+};
+
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    // s32 accumulator (2 << 4), signed 8-bit A and B (1 << 7, 1 << 10), K-major
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ bool r_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                       uint64_t limit) {
+    const bool ok = mbar_wait_bounded(bar, parity, abort, limit);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void r_abort(RescoreCtrl* c, int* status) {
+    atomicExch(&c->abort, 1);
+    atomicExch(&status[ST_TIMEOUT], 1);
+}
+
+// Byte offset of 16-byte chunk c of row r in a K-major tile of 128-byte rows
+// with the 128-byte swizzle (the layout the UMMA descriptor expects).
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+    return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <int H>
+__global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const RescoreArgs a) {
+    using S = RescoreSmem<H>;
+    extern __shared__ __align__(1024) unsigned char rsm_raw[];
+    unsigned char* smem = rsm_raw + ((1024u - (smem_u32(rsm_raw) & 1023u)) & 1023u);
+    unsigned char* As = smem + S::A_OFF;
+    unsigned char* Qs = smem + S::Q_OFF;
+    float* Ws = reinterpret_cast<float*>(smem + S::W_OFF);
+    RescoreCtrl* ctl = reinterpret_cast<RescoreCtrl*>(smem + S::CTRL_OFF);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    volatile int* abort = &ctl->abort;
+    constexpr uint32_t TMEM_COLS = R_SLOTS * H < 32 ? 32 : R_SLOTS * H;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < R_STAGES; ++s) {
+            mbar_init(&ctl->a_full[s], 32 * R_PROD_WARPS);
+            mbar_init(&ctl->a_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->q_full[b], 32 * R_PROD_WARPS);
+            mbar_init(&ctl->q_empty[b], 1 + 4);   // the MMAs' commit + the epilogue warps
+        }
+        mbar_init(&ctl->acc_full, 1);
+        for (int s = 0; s < R_SLOTS; ++s) mbar_init(&ctl->slot_empty[s], 4);
+        mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+    const int G = gridDim.x;
+
+    if (warp < R_PROD_WARPS) {
+        // ---------------------------------------------------------- producers
+        const int p = threadIdx.x;   // 0..127
+        int tile_seq = 0, tok_seq = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
+            const int n = a.cand_cnt[t];
+            if (n <= 0) continue;
+            const int qb = tok_seq & 1;
+            if (!r_wait(&ctl->q_empty[qb], ((tok_seq >> 1) & 1) ^ 1, abort, a.wait_ns)) {
+                ok = false;
+                break;
+            }
+            // the token's query limbs (B operand, H rows of 128 B per limb) and weights
+            unsigned char* Qb = Qs + qb * S::Q_BUF;
+            const uint8_t* qt = a.q + t * (int64_t)H * DK;
+            for (int e = p; e < H * 8; e += 32 * R_PROD_WARPS) {   // (row, 16-byte chunk)
+                const int r = e >> 3, c = e & 7;
+                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qt + r * DK + c * 16));
+                uint32_t l[4][3];
+                bool nan = false;
+                limbs4(raw.x, l[0], &nan); limbs4(raw.y, l[1], &nan);
+                limbs4(raw.z, l[2], &nan); limbs4(raw.w, l[3], &nan);
+#pragma unroll
+                for (int i = 0; i < NLIMB; ++i)
+                    *reinterpret_cast<uint4*>(Qb + i * S::Q_LIMB + sw128(r, c)) =
+                        make_uint4(l[0][i], l[1][i], l[2][i], l[3][i]);
+            }
+            for (int h = p; h < H; h += 32 * R_PROD_WARPS) Ws[qb * H + h] = a.w[t * H + h];
+            fence_proxy_async_smem();
+            mbar_arrive(&ctl->q_full[qb]);
+            ++tok_seq;
+            // the candidates' key limbs, 128 per tile (A operand)
+            const int32_t* cl = a.cand + t * CAP_C;
+            const int tiles = (n + R_M - 1) / R_M;
+            for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
+                const int s = tile_seq % R_STAGES;
+                if (!r_wait(&ctl->a_empty[s], ((tile_seq / R_STAGES) & 1) ^ 1, abort, a.wait_ns)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char* Ab = As + s * R_A_STAGE;
+                const int row = ti * R_M + p;
+                if (row < n) {
+                    const int64_t j = cl[row];
+                    const uint4* src = reinterpret_cast<const uint4*>(a.klimbs + j * KEY_LIMB_BYTES);
+                    uint4 v[NLIMB * 8];
+#pragma unroll
+                    for (int e = 0; e < NLIMB * 8; ++e) v[e] = __ldg(src + e);
+#pragma unroll
+                    for (int i = 0; i < NLIMB; ++i)
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<uint4*>(Ab + i * R_A_LIMB + sw128(p, c)) = v[i * 8 + c];
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&ctl->a_full[s]);
+            }
+        }
+        if (!ok && lane == 0) r_abort(ctl, a.status);
+    } else if (warp == 4) {
+        // --------------------------------------------------------- MMA issuer
+        constexpr uint32_t idesc = idesc_i8(R_M, H);
+        int tile_seq = 0, tok_seq = 0;
+        bool ok = true, issued = false;
+        for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
+            const int n = a.cand_cnt[t];
+            if (n <= 0) continue;
+            const int qb = tok_seq & 1;
+            if (!r_wait(&ctl->q_full[qb], (tok_seq >> 1) & 1, abort, a.wait_ns)) {
+                ok = false;
+                break;
+            }
+            ++tok_seq;
+            const uint32_t qbase = smem_u32(Qs + qb * S::Q_BUF);
+            const int tiles = (n + R_M - 1) / R_M;
+            for (int ti = 0; ti < tiles && ok; ++ti, ++tile_seq) {
+                const int s = tile_seq % R_STAGES;
+                if (!r_wait(&ctl->a_full[s], (tile_seq / R_STAGES) & 1, abort, a.wait_ns)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t abase = smem_u32(As + s * R_A_STAGE);
+                for (int g = 0; g < R_GROUPS; ++g) {
+                    const int nslot = R_GROUPS * tile_seq + g;
+                    if (!r_wait(&ctl->slot_empty[nslot % R_SLOTS], ((nslot / R_SLOTS) & 1) ^ 1,
+                                abort, a.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t d = tmem + (uint32_t)((nslot % R_SLOTS) * H);
+                        bool first = true;
+                        // key limb i times query limb g - i, scale 64^g
+                        for (int i = 0; i < NLIMB; ++i) {
+                            const int iq = g - i;
+                            if (iq < 0 || iq >= NLIMB) continue;
+#pragma unroll
+                            for (int kc = 0; kc < DK / 32; ++kc) {
+                                mma_i8(d, desc_k_sw128(abase + i * R_A_LIMB + kc * 32),
+                                       desc_k_sw128(qbase + iq * S::Q_LIMB + kc * 32), idesc,
+                                       first ? 0u : 1u);
+                                first = false;
+                                issued = true;
+                            }
+                        }
+                    }
+                    __syncwarp();
+                }
+                if (!ok) break;
+                if (lane == 0) {
+                    mma_commit(&ctl->a_empty[s]);
+                    mma_commit(&ctl->acc_full);
+                    if (ti == tiles - 1) mma_commit(&ctl->q_empty[qb]);
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok) {
+            if (lane == 0) r_abort(ctl, a.status);
+            // the MMAs issued (a tile may stop between groups) must finish
+            // before TMEM is freed: one more commit, and wait for it
+            if (__shfl_sync(0xffffffffu, issued ? 1 : 0, 0)) {
+                if (lane == 0) mma_commit(&ctl->drain);
+                __syncwarp();
+                mbar_wait_drain(&ctl->drain, 0);
+            }
+        }
+    } else if (warp >= 8) {
+        // ----------------------------------------------------------- epilogue
+        const int sub = warp & 3;
+        const int r = sub * 32 + lane;   // candidate row of the tile (TMEM lane)
+        int tile_seq = 0, tok_seq = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
+            const int n = a.cand_cnt[t];
+            if (n <= 0) continue;
+            const int qb = tok_seq & 1;
+            ++tok_seq;
+            const float* wq = Ws + qb * H;
+            const int tiles = (n + R_M - 1) / R_M;
+            for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
+                if (!r_wait(&ctl->acc_full, tile_seq & 1, abort, a.wait_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t col[R_GROUPS];
+#pragma unroll
+                for (int g = 0; g < R_GROUPS; ++g)
+                    col[g] = tmem + ((uint32_t)(sub * 32) << 16) +
+                             (uint32_t)(((R_GROUPS * tile_seq + g) % R_SLOTS) * H);
+                float total = 0.0f;
+#pragma unroll 1
+                for (int h0 = 0; h0 < H; h0 += 16) {
+                    uint32_t d[R_GROUPS][16];
+#pragma unroll
+                    for (int g = 0; g < R_GROUPS; ++g) tmem_ld_x16(col[g] + (uint32_t)h0, d[g]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < 16; ++h) {
+                        // v = D0 + 64 D1 + 64^2 D2 + 64^3 D3 + 64^4 D4, exactly
+                        const int A = (int)d[0][h] + 64 * (int)d[1][h];   // |A| < 2^27
+                        const int B = (int)d[2][h] + 64 * (int)d[3][h];   // |B| < 2^27
+                        const long long v = (long long)A + ((long long)B << 12) +
+                                            ((long long)(int)d[4][h] << 24);
+                        const float x = fmaxf(__ll2float_rn(v) * (1.0f / 262144.0f), 0.0f);
+                        total = __fadd_rn(total, __fmul_rn(wq[h0 + h], x));
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+#pragma unroll
+                    for (int g = 0; g < R_GROUPS; ++g)
+                        mbar_arrive(&ctl->slot_empty[(R_GROUPS * tile_seq + g) % R_SLOTS]);
+                const int row = ti * R_M + r;
+                if (row < n) a.exact[t * CAP_C + row] = total;
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->q_empty[qb]);   // weights of this token read
+        }
+        if (!ok && lane == 0) r_abort(ctl, a.status);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 5) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// K4: exact top-k of each token's candidates, best first, ties to the lowest
+// key; fewer visible keys than k pad with -1 / -inf.
+__global__ void __launch_bounds__(SEL_THREADS) dsa_select_kernel(
+    const int32_t* __restrict__ cand, const float* __restrict__ exact,
+    const int* __restrict__ cand_cnt, int64_t L, int64_t pos0, int k,
+    int32_t* __restrict__ out_idx, float* __restrict__ out_sc) {
+    extern __shared__ uint64_t ssm[];
+    uint64_t* keys = ssm;               // CAP_C
+    uint64_t* best = ssm + CAP_C;       // KMAX
+    __shared__ unsigned sm[256 + SEL_THREADS / 32 + 4];
+    __shared__ int nb;
+    const int64_t t = blockIdx.x;
+    const int n = cand_cnt[t];
+    const int64_t vis = max((int64_t)0, min(L, pos0 + t + 1));
+    if (n <= 0 && vis > 0) return;   // flagged: the exact-row fallback writes this token
+    const int m = (int)min((int64_t)k, (int64_t)n);
+    for (int i = threadIdx.x; i < n; i += SEL_THREADS)
+        keys[i] = make_cand(f32_key(exact[t * CAP_C + i]), (uint32_t)cand[t * CAP_C + i]);
+    const int kp = next_pow2(max(m, 1));
+    for (int i = threadIdx.x; i < kp; i += SEL_THREADS) best[i] = 0ull;
+    if (threadIdx.x == 0) nb = 0;
+    __syncthreads();
+    const uint64_t T = band_select<SEL_THREADS>(keys, n, m, sm);
+    for (int i = threadIdx.x; i < n; i += SEL_THREADS)
+        if (keys[i] >= T) best[atomicAdd(&nb, 1)] = keys[i];
+    __syncthreads();
+    block_bitonic_sort_desc(best, kp);
+    for (int i = threadIdx.x; i < k; i += SEL_THREADS) {
+        const uint64_t c = i < m ? best[i] : 0ull;
+        out_idx[t * k + i] = c ? (int32_t)cand_row(c) : -1;
+        out_sc[t * k + i] = c ? cand_score(c) : -INFINITY;
+    }
+}
+
+constexpr size_t SEL_SMEM = sizeof(uint64_t) * (CAP_C + KMAX);
+
+// ---------------------------------------------------------------------------
+// Fallback: every visible key's exact score for one token, on CUDA cores, in
+// the reference's arithmetic (exact integer dots, fp32 head sum in order),
+// written over the token's row of approximate scores.
+__global__ void dsa_exact_row_kernel(const uint8_t* __restrict__ q, const float* __restrict__ w,
+                                     const uint8_t* __restrict__ keys, int64_t L, int64_t t,
+                                     int64_t pos0, int H, float* __restrict__ row) {
+    __shared__ int qv[64 * DK];
+    __shared__ float ws[64];
+    const uint8_t* qt = q + t * (int64_t)H * DK;
+    for (int i = threadIdx.x; i < H * DK; i += blockDim.x) qv[i] = e4m3_scaled(qt[i]);
+    for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = w[t * H + h];
+    __syncthreads();
+    const int64_t vis = max((int64_t)0, min(L, pos0 + t + 1));
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < vis;
+         j += (int64_t)gridDim.x * blockDim.x) {
+        int kv[DK];
+#pragma unroll 8
+        for (int d = 0; d < DK; ++d) kv[d] = e4m3_scaled(keys[j * DK + d]);
+        float total = 0.0f;
+        for (int h = 0; h < H; ++h) {
+            long long acc = 0;
+#pragma unroll 8
+            for (int d = 0; d < DK; ++d) acc += (long long)qv[h * DK + d] * kv[d];
+            const float x = acc > 0 ? __ll2float_rn(acc) * (1.0f / 262144.0f) : 0.0f;
+            total = __fadd_rn(total, __fmul_rn(ws[h], x));
+        }
+        row[j] = total;
+    }
+}
+
+size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+// Workspace of the exact selection: status words and flagged tokens, key
+// limbs and norms, candidate lists and their exact scores.
+struct DsaExactLayout {
+    size_t status, limbs, knorm, cand, cand_cnt, exact, total;
+};
+
+static DsaExactLayout dsa_exact_layout(int64_t T, int64_t L) {
+    DsaExactLayout d;
+    size_t o = 0;
+    d.status = o; o += up256(sizeof(int) * (size_t)(ST_FLAGS + T));
+    d.limbs = o; o += up256((size_t)L * KEY_LIMB_BYTES);
+    d.knorm = o; o += up256(sizeof(float) * (size_t)L);
+    d.cand = o; o += up256(sizeof(int32_t) * (size_t)T * CAP_C);
+    d.cand_cnt = o; o += up256(sizeof(int) * (size_t)T);
+    d.exact = o; o += up256(sizeof(float) * (size_t)T * CAP_C);
+    d.total = o;
+    return d;
+}
+
+size_t dsa_exact_ws_bytes(int64_t T, int64_t L) { return dsa_exact_layout(T, L).total; }
+
+// Clears the status words and prepares the key limbs and norms; runs before
+// the scoring pass so that its timeout flag lands in status[ST_TIMEOUT].
+hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* ws,
+                               cudaStream_t st, int** status_out) {
+    const DsaExactLayout d = dsa_exact_layout(T, L);
+    unsigned char* w = static_cast<unsigned char*>(ws);
+    int* status = reinterpret_cast<int*>(w + d.status);
+    *status_out = status;
+    HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int) * ST_FLAGS, st));
+    if (L > 0) {
+        const int64_t threads = L * 32;
+        dsa_key_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+            keys, L, w + d.limbs, reinterpret_cast<float*>(w + d.knorm), status);
+        return check_launch("dsa_key_prep_kernel");
+    }
+    return HMM_OK;
+}
+
+// Band, exact rescoring and selection of every token; then the host reads the
+// status words and recomputes flagged tokens from their exact rows.
+hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float* w, int64_t T,
+                              int64_t H, int64_t L, int64_t pos0, int64_t topk,
+                              float* scores, int32_t* out_idx, float* out_sc, void* ws,
+                              void* topk_ws, size_t topk_ws_bytes, cudaStream_t st) {
+    const DsaExactLayout d = dsa_exact_layout(T, L);
+    unsigned char* wb = static_cast<unsigned char*>(ws);
+    int* status = reinterpret_cast<int*>(wb + d.status);
+    int32_t* cand = reinterpret_cast<int32_t*>(wb + d.cand);
+    int* cand_cnt = reinterpret_cast<int*>(wb + d.cand_cnt);
+    float* exact = reinterpret_cast<float*>(wb + d.exact);
+    hmm_status_t s;
+
+    BandArgs ba;
+    ba.scores = scores; ba.q = q; ba.w = w;
+    ba.knorm = reinterpret_cast<const float*>(wb + d.knorm);
+    ba.cand = cand; ba.cand_cnt = cand_cnt; ba.status = status;
+    ba.T = T; ba.L = L; ba.pos0 = pos0; ba.H = (int)H; ba.k = (int)topk;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_band_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)BAND_SMEM));
+    dsa_band_kernel<<<(unsigned)T, BAND_THREADS, BAND_SMEM, st>>>(ba);
+    s = check_launch("dsa_band_kernel");
+    if (s != HMM_OK) return s;
+
+    RescoreArgs ra;
+    ra.q = q; ra.w = w; ra.klimbs = wb + d.limbs; ra.cand = cand; ra.cand_cnt = cand_cnt;
+    ra.exact = exact; ra.status = status; ra.T = T; ra.wait_ns = wait_limit_ns();
+    const int grid = std::max(1, (int)std::min<int64_t>(device_sm_count(), T));
+    const ProfileMark pm = profile_begin(st);
+    if (H == 64) {
+        HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_rescore_kernel<64>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)RescoreSmem<64>::BYTES));
+        dsa_rescore_kernel<64><<<grid, R_THREADS, RescoreSmem<64>::BYTES, st>>>(ra);
+    } else if (H == 32) {
+        HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_rescore_kernel<32>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)RescoreSmem<32>::BYTES));
+        dsa_rescore_kernel<32><<<grid, R_THREADS, RescoreSmem<32>::BYTES, st>>>(ra);
+    } else {
+        HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_rescore_kernel<16>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)RescoreSmem<16>::BYTES));
+        dsa_rescore_kernel<16><<<grid, R_THREADS, RescoreSmem<16>::BYTES, st>>>(ra);
+    }
+    s = check_launch("dsa_rescore_kernel");
+    profile_end(pm, st);
+    if (s != HMM_OK) return s;
+
+    HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)SEL_SMEM));
+    dsa_select_kernel<<<(unsigned)T, SEL_THREADS, SEL_SMEM, st>>>(cand, exact, cand_cnt, L, pos0,
+                                                                  (int)topk, out_idx, out_sc);
+    s = check_launch("dsa_select_kernel");
+    if (s != HMM_OK) return s;
+
+    int h[ST_FLAGS] = {0, 0, 0, 0};
+    HMM_CUDA_TRY(cudaMemcpyAsync(h, status, sizeof(h), cudaMemcpyDeviceToHost, st));
+    HMM_CUDA_TRY(cudaStreamSynchronize(st));
+    if (h[ST_TIMEOUT])
+        return set_error(HMM_ERR_TIMEOUT,
+                         "dsa indexer: a bounded pipeline wait gave up; outputs invalid");
+    if (h[ST_NAN])
+        return set_error(HMM_ERR_INVALID,
+                         "q or keys hold an e4m3 NaN encoding (0x7f / 0xff), which has no "
+                         "exact score");
+    const int nflag = std::min<int64_t>(h[ST_NFLAG], T);
+    if (nflag > 0) {
+        std::vector<int> flagged(nflag);
+        HMM_CUDA_TRY(cudaMemcpyAsync(flagged.data(), status + ST_FLAGS, sizeof(int) * nflag,
+                                     cudaMemcpyDeviceToHost, st));
+        HMM_CUDA_TRY(cudaStreamSynchronize(st));
+        for (int t : flagged) {
+            const int64_t vis = std::max<int64_t>(0, std::min<int64_t>(L, pos0 + t + 1));
+            const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(
+                                   (vis + 127) / 128, 4 * (int64_t)device_sm_count()));
+            dsa_exact_row_kernel<<<blocks, 128, 0, st>>>(q, w, keys, L, t, pos0, (int)H,
+                                                         scores + (int64_t)t * L);
+            s = check_launch("dsa_exact_row_kernel");
+            if (s != HMM_OK) return s;
+            s = hmm_topk_f32(scores + (int64_t)t * L, L, 1, topk, out_idx + (int64_t)t * topk,
+                             out_sc + (int64_t)t * topk, topk_ws, topk_ws_bytes, st);
+            if (s != HMM_OK) return s;
+        }
+    }
+    return HMM_OK;
+}
+
+}  // namespace hmm

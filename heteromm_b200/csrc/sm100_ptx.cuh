@@ -71,13 +71,28 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Non-blocking test of the phase with `parity` (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with `parity`; gives up after `limit_ns` nanoseconds of
 // wall time or when *abort becomes nonzero.  Returns false when it gave up.
 // The limit and the abort flag are checked before the first suspended
-// try_wait and then every eighth, so a limit of 0 gives up the first time the
-// phase is found incomplete.
+// try_wait and then every eighth.  A limit of 0 (a test setting) never
+// blocks: the wait gives up whenever the phase is not already complete
+// (try_wait itself may suspend for a while before it reports that).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort, uint64_t limit_ns) {
+    if (limit_ns == 0) return mbar_test_wait(bar, parity);
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 0;; ++i) {

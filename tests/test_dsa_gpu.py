@@ -1,19 +1,22 @@
-"""GPU FP8 DSA lightning indexer (hmm_dsa_indexer_fp8) against the oracle's
-exact scores.
+"""GPU FP8 DSA lightning indexer (hmm_dsa_indexer_fp8) against the oracle.
 
-The tensor core multiplies e4m3 values exactly but accumulates the 128
-products of a head in fp32 with an undocumented order and width, and the
-head sum is fp32 FMA.  The stated tolerance per score is
-    GAMMA * sum_h w_h * sum_d |q_hd| |k_d|  +  HEADSUM_REL * |score|
-with GAMMA = 2^-10 (128x the worst fp32 sequential rounding of 128 terms)
-and HEADSUM_REL = 64 * 2^-23.  Selections must equal the exact top-k except
-among keys whose exact scores lie within twice the tolerance of the k-th."""
+The oracle restates indexer_top_ref (kernels/dsa_indexer/indexer_tb.cpp:27-56)
+for e4m3 inputs: exact integer dots, ReLU, fp32 w_h * x in head order, then
+the top-k best first (ties to the lowest key).  The selection must equal it
+bit for bit: the indices in order and the scores.
+
+The tensor-core pass's own scores (returned by want_all_scores) are
+approximations whose error the selection relies on being within
+    GAMMA * sum_h |w_h| sum_d |q_hd| |k_d|  +  HEADSUM_REL * |score|
+(GAMMA = 2^-10 for the tensor core's fp32 accumulation, 128x the worst case of
+sequential fp32; HEADSUM_REL = 64 * 2^-23); that assumption is checked too."""
 import numpy as np
 import pytest
 import torch
 
 import gen
 import heteromm_b200 as hmm
+from heteromm_b200 import _abi
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -40,52 +43,88 @@ def inputs(seed, T, H, L):
     return q, k, w
 
 
+def dev(a, cuda):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def check_exact(cuda, q, k, w, pos0, topk):
+    idx, sc = hmm.dsa_indexer_fp8(dev(q, cuda), dev(k, cuda), dev(w, cuda), pos0, topk)
+    oi, osc = O.dsa_indexer_fp8(q, k, w, pos0, topk)
+    idx, sc = idx.cpu().numpy(), sc.cpu().numpy()
+    bad = [t for t in range(q.shape[0]) if not np.array_equal(idx[t], oi[t])]
+    assert not bad, f"tokens {bad[:8]} differ from the oracle's ranking"
+    assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
+    return idx, sc
+
+
 @pytest.mark.parametrize("T,H,L,pos0,topk", [
-    (32, 64, 2048, 2048 - 32, 256),    # the config-4 shape, scaled down
+    (32, 64, 2048, 2048 - 32, 256),    # the config-4 shape, scaled down (every row fits the band)
     (37, 16, 1000, -1, 64),            # early tokens see fewer keys than k; ragged group
     (24, 32, 1500, 2000, 100),         # every key visible
-    (16, 64, 8192, 8192 - 16, 256),    # long rows: the sampled per-row selection
+    (16, 64, 20000, 20000 - 16, 256),  # long rows: the candidate band of each token
+    (40, 64, 30000, 30000 - 40, 2048), # long rows, the config's top-2,048
 ])
-def test_dsa_fp8_matches_exact_within_tolerance(cuda, T, H, L, pos0, topk):
+def test_dsa_fp8_equals_oracle(cuda, T, H, L, pos0, topk):
     q, k, w = inputs(800 + T, T, H, L)
-    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)   # noqa: E731
-    idx, sc, full = hmm.dsa_indexer_fp8(dev(q), dev(k), dev(w), pos0, topk, want_all_scores=True)
-    idx, sc, full = idx.cpu().numpy(), sc.cpu().numpy(), full.cpu().numpy()
-    exact = O.dsa_scores_fp8(q, k, w, pos0)
+    check_exact(cuda, q, k, w, pos0, topk)
 
+
+def test_dsa_fp8_config4_first_and_last_tokens(cuda):
+    """131,072 keys, 64 heads, top-2,048, at the positions of config 4's first
+    eight and last eight query tokens (token t at 126,976 + t)."""
+    L, H, topk = 131072, 64, 2048
+    p0 = L - 4096
+    x = gen.normal_f32(901, (16, H, 128))
+    y = gen.normal_f32(902, (L, 128))
+    q = gen.e4m3_bits(x * (448.0 / np.abs(x).max()))
+    k = gen.e4m3_bits(y * (448.0 / np.abs(y).max()))
+    w = gen.uniform01_f32(903, (16, H))
+    check_exact(cuda, q[:8], k, w[:8], p0, topk)
+    check_exact(cuda, q[8:], k, w[8:], p0 + 4088, topk)
+
+
+def test_dsa_tensor_core_scores_within_stated_bound(cuda):
+    T, H, L, pos0, topk = 32, 64, 4096, 4096 - 32, 256
+    q, k, w = inputs(950, T, H, L)
+    _, _, full = hmm.dsa_indexer_fp8(dev(q, cuda), dev(k, cuda), dev(w, cuda), pos0, topk,
+                                     want_all_scores=True)
+    full = full.cpu().numpy()
+    exact = O.dsa_scores_fp8(q, k, w, pos0)
     vals = e4m3_values()
-    qa, ka = np.abs(vals[q]), np.abs(vals[k])
-    l1 = np.einsum("thd,ld->thl", qa, ka)                     # sum_d |q||k| per head
-    tol = GAMMA * np.einsum("th,thl->tl", w.astype(np.float64), l1) + HEADSUM_REL * np.abs(exact)
+    l1 = np.einsum("thd,ld->thl", np.abs(vals[q]), np.abs(vals[k]))
+    tol = GAMMA * np.einsum("th,thl->tl", np.abs(w).astype(np.float64), l1) + \
+        HEADSUM_REL * np.abs(exact)
     vis = np.isfinite(exact)
     assert np.array_equal(vis, np.isfinite(full))
-    err = np.abs(full[vis].astype(np.float64) - exact[vis])
-    ratio = (err / tol[vis]).max()
-    print(f"max |gpu - exact| / tolerance = {ratio:.3g}")
+    ratio = (np.abs(full[vis].astype(np.float64) - exact[vis]) / tol[vis]).max()
+    print(f"max |tensor-core score - exact| / bound = {ratio:.3g}")
     assert ratio <= 1.0
 
-    for t in range(T):
-        n_vis = int(vis[t].sum())
-        m = min(topk, n_vis)
-        assert (idx[t, m:] == -1).all() and (idx[t, :m] >= 0).all()
-        got = idx[t, :m]
-        assert np.array_equal(sc[t, :m], full[t, got])             # reported = computed scores
-        assert (np.diff(sc[t, :m]) <= 0).all()                     # best first
-        assert (got <= pos0 + t).all()                              # causal
-        # the selection is exact over the kernel's own scores
-        own = np.lexsort((np.arange(L), -full[t].astype(np.float64)))[:m]
-        assert np.array_equal(got, own)
-        if m == 0:
-            continue
-        order = np.lexsort((np.arange(L), -exact[t]))               # exact ranking, ties lowest
-        want = order[:m]
-        kth = exact[t, want[-1]]
-        slack = 2 * tol[t, vis[t]].max()
-        extra = np.setdiff1d(got, want)
-        missing = np.setdiff1d(want, got)
-        assert len(extra) == len(missing)
-        assert (exact[t, extra] >= kth - slack).all()
-        assert (exact[t, missing] <= kth + slack).all()
+
+def test_dsa_duplicate_keys_take_the_exact_row_path(cuda):
+    """Keys drawn from only six distinct rows: 10,000 scores tie with each
+    other, so the band of a token does not fit and every token is recomputed
+    from its exact row; ties go to the lowest key index."""
+    T, H, L, topk = 6, 32, 60000, 512
+    q, kd, w = inputs(970, T, H, 6)
+    k = kd[np.arange(L) % 6]
+    check_exact(cuda, q, k, w, L - T, topk)
+
+
+def test_dsa_identical_keys(cuda):
+    T, H, L, topk = 5, 64, 9000, 64
+    q, kd, w = inputs(980, T, H, 1)
+    k = np.repeat(kd, L, axis=0)
+    idx, _ = check_exact(cuda, q, k, w, L - T, topk)
+    assert (idx == np.arange(topk)).all()
+
+
+def test_dsa_rejects_nan_encoding(cuda):
+    q, k, w = inputs(990, 8, 64, 3000)
+    k[17, 5] = 0x7f
+    with pytest.raises(hmm.HmmError) as e:
+        hmm.dsa_indexer_fp8(dev(q, cuda), dev(k, cuda), dev(w, cuda), 3000 - 8, 64)
+    assert e.value.status == _abi.HMM_ERR_INVALID
 
 
 @pytest.mark.parametrize("T,chunks", [(700, 1), (700, 3), (700, None), (1500, None)])
