@@ -364,16 +364,14 @@ hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* 
                                cudaStream_t st, int** status_out);
 hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float* w, int64_t T,
                               int64_t H, int64_t L, int64_t pos0, int64_t topk, float* scores,
-                              int32_t* out_idx, float* out_sc, void* ws, void* topk_ws,
-                              size_t topk_ws_bytes, cudaStream_t st);
+                              int32_t* out_idx, float* out_sc, void* ws, cudaStream_t st);
 }  // namespace hmm
 
 extern "C" size_t hmm_dsa_indexer_fp8_workspace_size(int64_t T, int64_t H, int64_t L,
                                                      int64_t topk) {
     if (T < 0 || H < 1 || L < 0 || topk < 1) return 0;
     return up256(sizeof(float) * (size_t)T * (size_t)L) + up256(dsa_exact_ws_bytes(T, L)) +
-           up256(sizeof(float) * (size_t)T * (size_t)topk) +
-           hmm_topk_f32_workspace_size(L, 1, topk);
+           up256(sizeof(float) * (size_t)T * (size_t)topk);
 }
 
 extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* keys,
@@ -400,14 +398,12 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
     const size_t sc_bytes = all_scores ? 0 : up256(sizeof(float) * (size_t)T * (size_t)L);
     const size_t ex_bytes = up256(dsa_exact_ws_bytes(T, L));
     const size_t sel_bytes = up256(sizeof(float) * (size_t)T * (size_t)topk);
-    const size_t tk_bytes = hmm_topk_f32_workspace_size(L, 1, topk);
-    const size_t need = sc_bytes + ex_bytes + sel_bytes + tk_bytes;
+    const size_t need = sc_bytes + ex_bytes + sel_bytes;
     if (!ws || workspace_bytes < need)
         return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", workspace_bytes, need);
     float* scores = all_scores ? all_scores : reinterpret_cast<float*>(ws);
     void* ex_ws = ws + sc_bytes;
     float* sel_sc = out_scores ? out_scores : reinterpret_cast<float*>(ws + sc_bytes + ex_bytes);
-    void* tk_ws = ws + sc_bytes + ex_bytes + sel_bytes;
     const int64_t n_sel = T * topk;
 
     if (L == 0) {   // no key is visible to any token
@@ -451,8 +447,7 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
     if (s != HMM_OK) return s;
     // exact selection over the approximate scores (reads the status words, so
     // this waits for the stream), then -1 for the slots of keys nobody sees
-    s = dsa_exact_select(q, keys, w, T, H, L, pos0, topk, scores, out_idx, sel_sc, ex_ws, tk_ws,
-                         tk_bytes, st);
+    s = dsa_exact_select(q, keys, w, T, H, L, pos0, topk, scores, out_idx, sel_sc, ex_ws, st);
     if (s != HMM_OK) return s;
     dsa_pad_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(out_idx, sel_sc, n_sel);
     return check_launch("dsa_pad_kernel");

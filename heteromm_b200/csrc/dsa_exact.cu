@@ -32,7 +32,6 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <vector>
 
 #include "heteromm_cuda.h"
 #include "hmm_common.cuh"
@@ -57,7 +56,8 @@ constexpr int KMAX = 4096;
 constexpr double C_TOL = 1.0 / 1024.0 + 1.0 / 65536.0;
 
 // Status words (int) at the start of the selection workspace.
-enum { ST_TIMEOUT = 0, ST_NAN = 1, ST_NFLAG = 2, ST_FLAGS = 4 };   // ST_FLAGS: T token ids
+// ST_KMAX: max_j ||k_j|| as float bits; ST_FLAGS: up to T flagged token ids.
+enum { ST_TIMEOUT = 0, ST_NAN = 1, ST_NFLAG = 2, ST_KMAX = 3, ST_FLAGS = 4 };
 
 // e4m3 (OCP FP8: bias 7, no infinities, S.1111.111 = NaN) times 2^9 as an
 // integer; the NaN encodings give 0 and are reported by the callers.
@@ -116,11 +116,37 @@ __global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(&status[ST_NAN], 1);
-    if (lane == 0) knorm[j] = __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0));
+    if (lane == 0) {
+        const float nrm = __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0));
+        knorm[j] = nrm;
+        atomicMax(&status[ST_KMAX], __float_as_int(nrm));   // nrm >= 0: int order = float order
+    }
 }
 
 // ---------------------------------------------------------------------------
 // K2: the candidate band of each token (one block per token).
+
+// Histogram add of `bucket` (when `act`) by a whole warp, one shared atomic
+// per distinct bucket (scores of one token crowd into few buckets).  All 32
+// lanes must call it.
+__device__ __forceinline__ void warp_hist_add(unsigned* hist, bool act, unsigned bucket) {
+    const int lane = threadIdx.x & 31;
+    const unsigned b = act ? bucket : 256u + (unsigned)lane;   // inactive lanes match nobody
+    const unsigned peers = __match_any_sync(0xffffffffu, b);
+    if (act && lane == __ffs(peers) - 1) atomicAdd(&hist[b], (unsigned)__popc(peers));
+}
+
+// Slot of this lane in a list grown by counter (when `take`), one shared
+// atomic per warp; -1 if the lane takes none.  All 32 lanes must call it.
+__device__ __forceinline__ int warp_append(bool take, int* counter) {
+    const int lane = threadIdx.x & 31;
+    const unsigned bal = __ballot_sync(0xffffffffu, take);
+    if (bal == 0u) return -1;
+    int base = 0;
+    if (lane == __ffs(bal) - 1) base = atomicAdd(counter, __popc(bal));
+    base = __shfl_sync(0xffffffffu, base, __ffs(bal) - 1);
+    return take ? base + __popc(bal & ((1u << lane) - 1u)) : -1;
+}
 
 template <int NT>
 __device__ __forceinline__ unsigned band_scan_incl(unsigned v, unsigned* warp_tot) {
@@ -148,10 +174,11 @@ __device__ __forceinline__ unsigned band_scan_incl(unsigned v, unsigned* warp_to
 }
 
 // Threshold T such that exactly min(k, M) of the distinct nonzero composites
-// keys[0, M) are >= T (0 if k >= M); NT threads; sm >= 256 + NT/32 + 3 words.
-template <int NT>
-__device__ __forceinline__ uint64_t band_select(const uint64_t* keys, int64_t M, int64_t k,
-                                                unsigned* sm) {
+// key_at(0 .. M-1) are >= T (0 if k >= M); NT threads; sm >= 256 + NT/32 + 3
+// words.
+template <int NT, class KeyAt>
+__device__ __forceinline__ uint64_t band_select_fn(KeyAt key_at, int64_t M, int64_t k,
+                                                   unsigned* sm) {
     unsigned* hist = sm;
     unsigned* wt = sm + 256;
     unsigned* res = sm + 256 + NT / 32;
@@ -161,9 +188,10 @@ __device__ __forceinline__ uint64_t band_select(const uint64_t* keys, int64_t M,
     for (int shift = 56; shift >= 0; shift -= 8) {
         if (threadIdx.x < 256) hist[threadIdx.x] = 0;
         __syncthreads();
-        for (int64_t i = threadIdx.x; i < M; i += NT) {
-            const uint64_t key = keys[i];
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1u);
+        for (int64_t i0 = threadIdx.x & ~31; i0 < M; i0 += NT) {
+            const int64_t i = i0 + (threadIdx.x & 31);
+            const uint64_t key = i < M ? key_at(i) : 0ull;
+            warp_hist_add(hist, i < M && (key & mask) == prefix, (unsigned)(key >> shift) & 255u);
         }
         __syncthreads();
         const unsigned c = threadIdx.x < 256 ? hist[255 - threadIdx.x] : 0u;
@@ -183,6 +211,12 @@ __device__ __forceinline__ uint64_t band_select(const uint64_t* keys, int64_t M,
     return prefix;
 }
 
+template <int NT>
+__device__ __forceinline__ uint64_t band_select(const uint64_t* keys, int64_t M, int64_t k,
+                                                unsigned* sm) {
+    return band_select_fn<NT>([keys](int64_t i) { return keys[i]; }, M, k, sm);
+}
+
 struct BandArgs {
     const float* scores;     // [T][L] approximate scores (tensor-core pass)
     const uint8_t* q;        // [T][H][128] e4m3
@@ -200,12 +234,59 @@ __device__ __forceinline__ void band_flag(const BandArgs& a, int64_t t) {
     if (pos < a.T) a.status[ST_FLAGS + pos] = (int)t;
 }
 
+// Largest P = (24-bit prefix << 8) such that at least `need` (>= 1, <= M) of
+// the 32-bit keys key_at(0 .. M-1) are >= P: a floor of the need-th largest
+// key, three 8-bit histogram passes.  NT threads; sm >= 256 + NT/32 + 3.
+template <int NT, class KeyAt>
+__device__ __forceinline__ uint32_t key_floor(KeyAt key_at, int64_t M, int64_t need_in,
+                                              unsigned* sm) {
+    unsigned* hist = sm;
+    unsigned* wt = sm + 256;
+    unsigned* res = sm + 256 + NT / 32;
+    uint32_t prefix = 0, mask = 0;
+    unsigned need = (unsigned)need_in;
+    for (int shift = 24; shift >= 8; shift -= 8) {
+        if (threadIdx.x < 256) hist[threadIdx.x] = 0;
+        __syncthreads();
+        for (int64_t i0 = threadIdx.x & ~31; i0 < M; i0 += NT) {
+            const int64_t i = i0 + (threadIdx.x & 31);
+            const uint32_t key = i < M ? key_at(i) : 0u;
+            warp_hist_add(hist, i < M && (key & mask) == prefix, (key >> shift) & 255u);
+        }
+        __syncthreads();
+        const unsigned c = threadIdx.x < 256 ? hist[255 - threadIdx.x] : 0u;
+        const unsigned incl = band_scan_incl<NT>(c, wt);
+        const unsigned excl = incl - c;
+        if (threadIdx.x < 256 && excl < need && need <= incl) {
+            res[0] = 255 - threadIdx.x; res[1] = excl;
+        }
+        __syncthreads();
+        need -= res[1];
+        prefix |= res[0] << shift;
+        mask |= 0xffu << shift;
+        __syncthreads();
+    }
+    return prefix;
+}
+
+// One block per token.  Bounds: tol_j = E_t * ||k_j|| (E_t = C_TOL * ||u_t||),
+// lo_j = s~_j - tol_j, hi_j = s~_j + tol_j, all rounded outwards.
+//   1. tau: a floor of the r1-th largest lo of a strided sample, r1 chosen so
+//      that at least m keys have lo >= tau except with negligible probability
+//   2. one read of the row collects every key with s~ + E_t * max_j ||k_j|| >=
+//      tau (so every key with lo >= tau; a miss of the sample only costs the
+//      exact-row path)
+//   3. Lambda: a floor of the m-th largest lo among the collected keys (all
+//      keys with lo >= tau are there, at least m of them), so Lambda <= the
+//      exact k-th score
+//   4. candidates: the collected keys with hi_j >= Lambda
 __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a) {
     extern __shared__ uint64_t bsm[];
-    uint64_t* col = bsm;                    // BAND_COLLECT: (f32_key(s~) << 32) | j
-    uint64_t* lok = bsm + BAND_COLLECT;     // BAND_COLLECT: lo composites; first the sample
+    uint64_t* col = bsm;                                         // BAND_COLLECT: (s~ bits << 32) | j
+    uint32_t* samp = reinterpret_cast<uint32_t*>(bsm + BAND_COLLECT);   // BAND_SAMPLE lo keys
     __shared__ unsigned sm[256 + BAND_THREADS / 32 + 4];
-    __shared__ double ured[BAND_THREADS / 32];
+    __shared__ float ured[4][DK];
+    __shared__ float nred[BAND_THREADS / 32];
     __shared__ int cnt, cnt_lo, out_n, nan_seen;
     __shared__ float e_t;
     const int64_t t = blockIdx.x;
@@ -213,34 +294,37 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
     const int m = (int)min((int64_t)a.k, vis);
     int32_t* cand = a.cand + t * CAP_C;
     if (threadIdx.x == 0) { cnt = 0; cnt_lo = 0; out_n = 0; nan_seen = 0; }
-    __syncthreads();
 
-    // E_t = C_TOL * ||u_t||_2 (rounded up), u_t[d] = sum_h |w_h| |q_hd|
+    // E_t = C_TOL * ||u_t||_2 rounded up, u_t[d] = sum_h |w_h| |q_hd| (real units)
     {
-        double part = 0.0;
         const uint8_t* qt = a.q + t * (int64_t)a.H * DK;
         const float* wt = a.w + t * a.H;
+        const int d = threadIdx.x & (DK - 1), hq = threadIdx.x >> 7;   // 4 head quarters
+        float u = 0.0f;
         bool nan = false;
-        for (int d = threadIdx.x; d < DK; d += BAND_THREADS) {
-            double u = 0.0;
-            for (int h = 0; h < a.H; ++h) {
-                const uint32_t b = qt[h * DK + d];
-                nan |= e4m3_is_nan(b);
-                const int v = e4m3_scaled(b);
-                u = __dadd_ru(u, __dmul_ru(fabs((double)wt[h]), (double)(v < 0 ? -v : v)));
-            }
-            part = __dadd_ru(part, __dmul_ru(u, u));
+        for (int h = hq; h < a.H; h += BAND_THREADS / DK) {
+            const uint32_t b = qt[h * DK + d];
+            nan |= e4m3_is_nan(b);
+            const int v = e4m3_scaled(b);
+            u = __fmaf_ru(fabsf(wt[h]), (float)(v < 0 ? -v : v) * (1.0f / 512.0f), u);
         }
+        ured[hq][d] = u;
         if (nan) atomicOr(&nan_seen, 1);
+        __syncthreads();
+        float sq = 0.0f;
+        if (threadIdx.x < DK) {
+            const float ud = __fadd_ru(__fadd_ru(ured[0][d], ured[1][d]),
+                                       __fadd_ru(ured[2][d], ured[3][d]));
+            sq = __fmul_ru(ud, ud);
+        }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) part = __dadd_ru(part, __shfl_xor_sync(0xffffffffu, part, o));
-        if ((threadIdx.x & 31) == 0) ured[threadIdx.x >> 5] = part;
+        for (int o = 16; o > 0; o >>= 1) sq = __fadd_ru(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+        if ((threadIdx.x & 31) == 0) nred[threadIdx.x >> 5] = sq;
         __syncthreads();
         if (threadIdx.x == 0) {
-            double s = 0.0;
-            for (int i = 0; i < BAND_THREADS / 32; ++i) s = __dadd_ru(s, ured[i]);
-            // ||u|| in real units: v = value * 2^9
-            e_t = __double2float_ru(__dmul_ru(__dmul_ru(__dsqrt_ru(s), 1.0 / 512.0), C_TOL));
+            float s2 = 0.0f;
+            for (int i = 0; i < BAND_THREADS / 32; ++i) s2 = __fadd_ru(s2, nred[i]);
+            e_t = __fmul_ru(__fsqrt_ru(s2), (float)C_TOL * (1.0f + 1.0f / 4096.0f));
             if (nan_seen) atomicOr(&a.status[ST_NAN], 1);
         }
         __syncthreads();
@@ -253,56 +337,85 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
         return;
     }
     const float* row = a.scores + t * a.L;
-    auto lo_of = [&](float s, int64_t j) { return __fsub_rd(s, __fmul_ru(E, a.knorm[j])); };
-    auto hi_of = [&](float s, int64_t j) { return __fadd_ru(s, __fmul_ru(E, a.knorm[j])); };
+    const float tol_max = __fmul_ru(E, __int_as_float(a.status[ST_KMAX]));
+    auto lo_key = [&](float s, int64_t j) { return f32_key(__fsub_rd(s, __fmul_ru(E, a.knorm[j]))); };
+    auto hi_key = [&](float s, int64_t j) { return f32_key(__fadd_ru(s, __fmul_ru(E, a.knorm[j]))); };
 
-    // 1. a threshold tau on lo, from a strided sample, expected to leave about
-    //    2k keys above it
+    // 1. tau from the sample: it holds Binomial(S, m / vis) keys whose lo
+    //    reaches the k-th; take the (mean + 5 sd + 8)-th largest
     for (int i = threadIdx.x; i < BAND_SAMPLE; i += BAND_THREADS) {
         const int64_t j = (int64_t)i * vis / BAND_SAMPLE;
-        lok[i] = make_cand(f32_key(lo_of(row[j], j)), (uint32_t)j);
+        samp[i] = lo_key(row[j], j);
     }
     __syncthreads();
-    const int64_t r = min((int64_t)BAND_SAMPLE - 1, 2 * (int64_t)m * BAND_SAMPLE / vis + 32);
-    const uint64_t tau = band_select<BAND_THREADS>(lok, BAND_SAMPLE, r + 1, sm);
-    const uint32_t tau_key = (uint32_t)(tau >> 32);
-    __syncthreads();
+    const double p_k = (double)m / (double)vis;
+    const double mean_k = BAND_SAMPLE * p_k;
+    const int64_t r1 = min((int64_t)BAND_SAMPLE,
+                           (int64_t)ceil(mean_k + 5.0 * sqrt(mean_k * (1.0 - p_k)) + 8.0));
+    const uint32_t tau = key_floor<BAND_THREADS>([samp](int64_t i) { return samp[i]; },
+                                                 BAND_SAMPLE, r1, sm);
 
-    // 2. one read of the row: collect every key whose hi reaches tau; count the
-    //    keys whose lo does (all of those are collected, as hi >= lo)
-    for (int64_t j = threadIdx.x; j < vis; j += BAND_THREADS) {
-        const float s = row[j];
-        if (f32_key(hi_of(s, j)) >= tau_key) {
-            const int pos = atomicAdd(&cnt, 1);
-            if (pos < BAND_COLLECT) col[pos] = ((uint64_t)f32_key(s) << 32) | (uint64_t)j;
-            if (make_cand(f32_key(lo_of(s, j)), (uint32_t)j) >= tau) atomicAdd(&cnt_lo, 1);
+    // 2. one read of the row (each lane 4 consecutive scores; warp-uniform loop)
+    const int lane = threadIdx.x & 31;
+    auto take = [&](float s, int64_t j, bool valid) {
+        const bool hit = valid && f32_key(__fadd_ru(s, tol_max)) >= tau;
+        const int pos = warp_append(hit, &cnt);
+        if (pos >= 0 && pos < BAND_COLLECT)
+            col[pos] = ((uint64_t)__float_as_uint(s) << 32) | (uint64_t)j;
+    };
+    if ((a.L & 3) == 0) {
+        const float4* row4 = reinterpret_cast<const float4*>(row);
+        const int64_t n4 = (vis + 3) >> 2;   // the last float4 may hold invisible (-inf) keys
+        for (int64_t b0 = threadIdx.x & ~31; b0 < n4; b0 += BAND_THREADS) {
+            const int64_t i4 = b0 + lane;
+            const float4 v = i4 < n4 ? __ldg(row4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            take(v.x, 4 * i4 + 0, 4 * i4 + 0 < vis);
+            take(v.y, 4 * i4 + 1, 4 * i4 + 1 < vis);
+            take(v.z, 4 * i4 + 2, 4 * i4 + 2 < vis);
+            take(v.w, 4 * i4 + 3, 4 * i4 + 3 < vis);
+        }
+    } else {
+        for (int64_t j0 = threadIdx.x & ~31; j0 < vis; j0 += BAND_THREADS) {
+            const int64_t j = j0 + lane;
+            take(j < vis ? row[j] : 0.0f, j, j < vis);
         }
     }
     __syncthreads();
     const int C = cnt;
+    if (C <= BAND_COLLECT)
+        for (int i0 = threadIdx.x & ~31; i0 < C; i0 += BAND_THREADS) {
+            const int i = i0 + lane;
+            bool hit = false;
+            if (i < C) {
+                const uint64_t e = col[i];
+                hit = lo_key(__uint_as_float((uint32_t)(e >> 32)), (int64_t)(uint32_t)e) >= tau;
+            }
+            warp_append(hit, &cnt_lo);
+        }
+    __syncthreads();
     if (C > BAND_COLLECT || cnt_lo < m) {   // the sample's threshold was off: exact row instead
         if (threadIdx.x == 0) { band_flag(a, t); a.cand_cnt[t] = 0; }
         return;
     }
-    // 3. L_k: the m-th largest lo composite among the collected keys (every key
-    //    with lo >= tau is among them, and at least m are)
-    for (int i = threadIdx.x; i < C; i += BAND_THREADS) {
-        const uint64_t e = col[i];
-        const int64_t j = (int64_t)(uint32_t)e;
-        lok[i] = make_cand(f32_key(lo_of(key_to_f32((uint32_t)(e >> 32)), j)), (uint32_t)j);
-    }
-    __syncthreads();
-    const uint64_t Lk = band_select<BAND_THREADS>(lok, C, m, sm);
-    const uint32_t lk_key = (uint32_t)(Lk >> 32);
-    __syncthreads();
-    // 4. the candidates: hi_j >= L_k's lo score
-    for (int i = threadIdx.x; i < C; i += BAND_THREADS) {
-        const uint64_t e = col[i];
-        const int64_t j = (int64_t)(uint32_t)e;
-        if (f32_key(hi_of(key_to_f32((uint32_t)(e >> 32)), j)) >= lk_key) {
-            const int pos = atomicAdd(&out_n, 1);
-            if (pos < CAP_C) cand[pos] = (int32_t)j;
+    // 3. Lambda
+    const uint32_t lam = key_floor<BAND_THREADS>(
+        [&](int64_t i) {
+            const uint64_t e = col[i];
+            return lo_key(__uint_as_float((uint32_t)(e >> 32)), (int64_t)(uint32_t)e);
+        },
+        C, m, sm);
+    // 4. the candidates
+    for (int i0 = threadIdx.x & ~31; i0 < C; i0 += BAND_THREADS) {
+        const int i = i0 + lane;
+        bool hit = false;
+        int64_t j = 0;
+        if (i < C) {
+            const uint64_t e = col[i];
+            j = (int64_t)(uint32_t)e;
+            hit = hi_key(__uint_as_float((uint32_t)(e >> 32)), j) >= lam;
         }
+        const int pos = warp_append(hit, &out_n);
+        if (pos >= 0 && pos < CAP_C) cand[pos] = (int32_t)j;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -315,7 +428,7 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
     }
 }
 
-constexpr size_t BAND_SMEM = sizeof(uint64_t) * 2 * BAND_COLLECT;
+constexpr size_t BAND_SMEM = sizeof(uint64_t) * BAND_COLLECT + sizeof(uint32_t) * BAND_SAMPLE;
 
 // ---------------------------------------------------------------------------
 // K3: exact scores of the candidates on the tensor cores.
@@ -325,7 +438,7 @@ constexpr int R_STAGES = 3;
 constexpr int R_A_LIMB = R_M * DK;               // 16 KB: one limb of a tile
 constexpr int R_A_STAGE = NLIMB * R_A_LIMB;      // 48 KB
 constexpr int R_PROD_WARPS = 4;
-constexpr int R_THREADS = 32 * 12;               // producers 0-3, MMA 4, TMEM 5, epilogue 8-11
+constexpr int R_THREADS = 32 * 16;               // producers 0-3, MMA 4, TMEM 5, epilogue 8-15
 constexpr int R_SLOTS = 8;                       // accumulator slots of H columns (a ring)
 constexpr int R_GROUPS = 5;                      // limb scales 64^0 .. 64^4
 
@@ -343,7 +456,7 @@ struct RescoreSmem {
 struct RescoreCtrl {
     uint64_t a_full[R_STAGES], a_empty[R_STAGES];
     uint64_t q_full[2], q_empty[2];
-    uint64_t acc_full;
+    uint64_t acc_full[2];            // by tile parity: one epilogue warpgroup each
     uint64_t slot_empty[R_SLOTS];
     uint64_t drain;                  // MMA warp: every MMA issued has completed (abort path)
     uint32_t tmem_base;
@@ -389,12 +502,39 @@ __device__ __forceinline__ void r_abort(RescoreCtrl* c, int* status) {
     atomicExch(&status[ST_TIMEOUT], 1);
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only), and its groups.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Byte offset of 16-byte chunk c of row r in a K-major tile of 128-byte rows
 // with the 128-byte swizzle (the layout the UMMA descriptor expects).
 __device__ __forceinline__ uint32_t sw128(int r, int c) {
     return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
+// One persistent CTA per SM over the tokens.  Roles (16 warps):
+//   warps 0-3   producers: per token, its query limbs (B operand, H rows x 3
+//               limbs of 128 B) and weights; per tile, the 128 candidates' key
+//               limbs gathered by cp.async (A operand, 3 x 16 KB, 128-byte
+//               swizzle), one tile's copies in flight while the previous
+//               tile's complete
+//   warp 4      MMA issuer: per tile, 9 limb pairs x 4 K-steps of
+//               tcgen05.mma kind::i8 (M = 128 candidates, N = H heads, K = 32)
+//               into 5 accumulators of H columns (one per scale 64^g), taken
+//               from a ring of 8 TMEM slots so that the next tile's first
+//               groups start while the epilogue drains the last
+//   warp 5      TMEM allocator
+//   warps 8-15  epilogue, two warpgroups (tile parity): thread = candidate;
+//               joins the 5 groups exactly and sums the heads in order
 template <int H>
 __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const RescoreArgs a) {
     using S = RescoreSmem<H>;
@@ -415,9 +555,9 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->q_full[b], 32 * R_PROD_WARPS);
-            mbar_init(&ctl->q_empty[b], 1 + 4);   // the MMAs' commit + the epilogue warps
+            mbar_init(&ctl->q_empty[b], 1 + 8);   // the MMAs' commit + the 8 epilogue warps
+            mbar_init(&ctl->acc_full[b], 1);
         }
-        mbar_init(&ctl->acc_full, 1);
         for (int s = 0; s < R_SLOTS; ++s) mbar_init(&ctl->slot_empty[s], 4);
         mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
@@ -435,13 +575,25 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
 
     if (warp < R_PROD_WARPS) {
         // ---------------------------------------------------------- producers
-        const int p = threadIdx.x;   // 0..127
+        const int p = threadIdx.x;   // 0..127: the tile row this thread copies
         int tile_seq = 0, tok_seq = 0;
+        int pending = -1;            // stage whose copies are still in flight
         bool ok = true;
+        // completes the copies of the stage `pending`: wait for this thread's
+        // copies, make them visible to the tensor core, arrive
+        auto complete = [&](int keep) {
+            if (pending < 0) return;
+            if (keep) cp_async_wait<1>(); else cp_async_wait<0>();
+            fence_proxy_async_smem();
+            mbar_arrive(&ctl->a_full[pending]);
+            pending = -1;
+        };
         for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
             const int n = a.cand_cnt[t];
             if (n <= 0) continue;
             const int qb = tok_seq & 1;
+            const int32_t* cl = a.cand + t * CAP_C;
+            int j_next = p < n ? cl[p] : 0;   // candidate of this thread's row in tile 0
             if (!r_wait(&ctl->q_empty[qb], ((tok_seq >> 1) & 1) ^ 1, abort, a.wait_ns)) {
                 ok = false;
                 break;
@@ -466,32 +618,32 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             mbar_arrive(&ctl->q_full[qb]);
             ++tok_seq;
             // the candidates' key limbs, 128 per tile (A operand)
-            const int32_t* cl = a.cand + t * CAP_C;
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
                 const int s = tile_seq % R_STAGES;
+                const int j = j_next;
+                const int row = ti * R_M + p;
                 if (!r_wait(&ctl->a_empty[s], ((tile_seq / R_STAGES) & 1) ^ 1, abort, a.wait_ns)) {
                     ok = false;
                     break;
                 }
-                unsigned char* Ab = As + s * R_A_STAGE;
-                const int row = ti * R_M + p;
                 if (row < n) {
-                    const int64_t j = cl[row];
-                    const uint4* src = reinterpret_cast<const uint4*>(a.klimbs + j * KEY_LIMB_BYTES);
-                    uint4 v[NLIMB * 8];
-#pragma unroll
-                    for (int e = 0; e < NLIMB * 8; ++e) v[e] = __ldg(src + e);
+                    unsigned char* Ab = As + s * R_A_STAGE;
+                    const unsigned char* src = a.klimbs + (int64_t)j * KEY_LIMB_BYTES;
 #pragma unroll
                     for (int i = 0; i < NLIMB; ++i)
 #pragma unroll
                         for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4*>(Ab + i * R_A_LIMB + sw128(p, c)) = v[i * 8 + c];
+                            cp_async16(Ab + i * R_A_LIMB + sw128(p, c), src + i * DK + c * 16);
                 }
-                fence_proxy_async_smem();
-                mbar_arrive(&ctl->a_full[s]);
+                cp_async_commit();
+                if (row + R_M < n) j_next = cl[row + R_M];   // next tile's candidate, early
+                complete(1);                                   // the previous tile
+                pending = s;
             }
+            complete(0);
         }
+        complete(0);
         if (!ok && lane == 0) r_abort(ctl, a.status);
     } else if (warp == 4) {
         // --------------------------------------------------------- MMA issuer
@@ -546,7 +698,7 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                 if (!ok) break;
                 if (lane == 0) {
                     mma_commit(&ctl->a_empty[s]);
-                    mma_commit(&ctl->acc_full);
+                    mma_commit(&ctl->acc_full[tile_seq & 1]);
                     if (ti == tiles - 1) mma_commit(&ctl->q_empty[qb]);
                 }
                 __syncwarp();
@@ -564,6 +716,7 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
         }
     } else if (warp >= 8) {
         // ----------------------------------------------------------- epilogue
+        const int wg = (warp - 8) >> 2;  // tiles with tile_seq % 2 == wg
         const int sub = warp & 3;
         const int r = sub * 32 + lane;   // candidate row of the tile (TMEM lane)
         int tile_seq = 0, tok_seq = 0;
@@ -576,7 +729,8 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const float* wq = Ws + qb * H;
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
-                if (!r_wait(&ctl->acc_full, tile_seq & 1, abort, a.wait_ns)) {
+                if ((tile_seq & 1) != wg) continue;
+                if (!r_wait(&ctl->acc_full[wg], (tile_seq >> 1) & 1, abort, a.wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -649,8 +803,12 @@ __global__ void __launch_bounds__(SEL_THREADS) dsa_select_kernel(
     if (threadIdx.x == 0) nb = 0;
     __syncthreads();
     const uint64_t T = band_select<SEL_THREADS>(keys, n, m, sm);
-    for (int i = threadIdx.x; i < n; i += SEL_THREADS)
-        if (keys[i] >= T) best[atomicAdd(&nb, 1)] = keys[i];
+    for (int i0 = threadIdx.x & ~31; i0 < n; i0 += SEL_THREADS) {
+        const int i = i0 + (threadIdx.x & 31);
+        const uint64_t c = i < n ? keys[i] : 0ull;
+        const int pos = warp_append(i < n && c >= T, &nb);
+        if (pos >= 0) best[pos] = c;
+    }
     __syncthreads();
     block_bitonic_sort_desc(best, kp);
     for (int i = threadIdx.x; i < k; i += SEL_THREADS) {
@@ -663,18 +821,22 @@ __global__ void __launch_bounds__(SEL_THREADS) dsa_select_kernel(
 constexpr size_t SEL_SMEM = sizeof(uint64_t) * (CAP_C + KMAX);
 
 // ---------------------------------------------------------------------------
-// Fallback: every visible key's exact score for one token, on CUDA cores, in
-// the reference's arithmetic (exact integer dots, fp32 head sum in order),
-// written over the token's row of approximate scores.
-__global__ void dsa_exact_row_kernel(const uint8_t* __restrict__ q, const float* __restrict__ w,
-                                     const uint8_t* __restrict__ keys, int64_t L, int64_t t,
-                                     int64_t pos0, int H, float* __restrict__ row) {
+// Fallback: every visible key's exact score of each flagged token (blockIdx.y
+// picks the token from the flagged list), on CUDA cores, in the reference's
+// arithmetic (exact integer dots, fp32 head sum in order), written over the
+// token's row of approximate scores.
+__global__ void dsa_exact_rows_kernel(const uint8_t* __restrict__ q, const float* __restrict__ w,
+                                      const uint8_t* __restrict__ keys, int64_t L, int64_t pos0,
+                                      int H, const int* __restrict__ flagged,
+                                      float* __restrict__ scores) {
     __shared__ int qv[64 * DK];
     __shared__ float ws[64];
+    const int64_t t = flagged[blockIdx.y];
     const uint8_t* qt = q + t * (int64_t)H * DK;
     for (int i = threadIdx.x; i < H * DK; i += blockDim.x) qv[i] = e4m3_scaled(qt[i]);
     for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = w[t * H + h];
     __syncthreads();
+    float* row = scores + t * L;
     const int64_t vis = max((int64_t)0, min(L, pos0 + t + 1));
     for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < vis;
          j += (int64_t)gridDim.x * blockDim.x) {
@@ -690,6 +852,40 @@ __global__ void dsa_exact_row_kernel(const uint8_t* __restrict__ q, const float*
             total = __fadd_rn(total, __fmul_rn(ws[h], x));
         }
         row[j] = total;
+    }
+}
+
+// Fallback: the exact top-k of each flagged token's exact row (one block per
+// flagged token): a block radix select over the visible scores, then the k
+// best sorted, ties to the lowest key.
+__global__ void __launch_bounds__(SEL_THREADS) dsa_row_select_kernel(
+    const float* __restrict__ scores, int64_t L, int64_t pos0, int k,
+    const int* __restrict__ flagged, int32_t* __restrict__ out_idx, float* __restrict__ out_sc) {
+    extern __shared__ uint64_t fsm[];   // KMAX
+    __shared__ unsigned sm[256 + SEL_THREADS / 32 + 4];
+    __shared__ int nb;
+    const int64_t t = flagged[blockIdx.x];
+    const float* row = scores + t * L;
+    const int64_t vis = max((int64_t)0, min(L, pos0 + t + 1));
+    const int m = (int)min((int64_t)k, vis);
+    auto key_at = [row](int64_t j) { return make_cand(f32_key(row[j]), (uint32_t)j); };
+    const int kp = next_pow2(max(m, 1));
+    for (int i = threadIdx.x; i < kp; i += SEL_THREADS) fsm[i] = 0ull;
+    if (threadIdx.x == 0) nb = 0;
+    __syncthreads();
+    const uint64_t T = band_select_fn<SEL_THREADS>(key_at, vis, m, sm);
+    for (int64_t j0 = threadIdx.x & ~31; j0 < vis; j0 += SEL_THREADS) {
+        const int64_t j = j0 + (threadIdx.x & 31);
+        const uint64_t c = j < vis ? key_at(j) : 0ull;
+        const int pos = warp_append(j < vis && c >= T, &nb);
+        if (pos >= 0) fsm[pos] = c;
+    }
+    __syncthreads();
+    block_bitonic_sort_desc(fsm, kp);
+    for (int i = threadIdx.x; i < k; i += SEL_THREADS) {
+        const uint64_t c = i < m ? fsm[i] : 0ull;
+        out_idx[t * k + i] = c ? (int32_t)cand_row(c) : -1;
+        out_sc[t * k + i] = c ? cand_score(c) : -INFINITY;
     }
 }
 
@@ -741,7 +937,7 @@ hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* 
 hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float* w, int64_t T,
                               int64_t H, int64_t L, int64_t pos0, int64_t topk,
                               float* scores, int32_t* out_idx, float* out_sc, void* ws,
-                              void* topk_ws, size_t topk_ws_bytes, cudaStream_t st) {
+                              cudaStream_t st) {
     const DsaExactLayout d = dsa_exact_layout(T, L);
     unsigned char* wb = static_cast<unsigned char*>(ws);
     int* status = reinterpret_cast<int*>(wb + d.status);
@@ -803,24 +999,20 @@ hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float
         return set_error(HMM_ERR_INVALID,
                          "q or keys hold an e4m3 NaN encoding (0x7f / 0xff), which has no "
                          "exact score");
-    const int nflag = std::min<int64_t>(h[ST_NFLAG], T);
-    if (nflag > 0) {
-        std::vector<int> flagged(nflag);
-        HMM_CUDA_TRY(cudaMemcpyAsync(flagged.data(), status + ST_FLAGS, sizeof(int) * nflag,
-                                     cudaMemcpyDeviceToHost, st));
-        HMM_CUDA_TRY(cudaStreamSynchronize(st));
-        for (int t : flagged) {
-            const int64_t vis = std::max<int64_t>(0, std::min<int64_t>(L, pos0 + t + 1));
-            const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(
-                                   (vis + 127) / 128, 4 * (int64_t)device_sm_count()));
-            dsa_exact_row_kernel<<<blocks, 128, 0, st>>>(q, w, keys, L, t, pos0, (int)H,
-                                                         scores + (int64_t)t * L);
-            s = check_launch("dsa_exact_row_kernel");
-            if (s != HMM_OK) return s;
-            s = hmm_topk_f32(scores + (int64_t)t * L, L, 1, topk, out_idx + (int64_t)t * topk,
-                             out_sc + (int64_t)t * topk, topk_ws, topk_ws_bytes, st);
-            if (s != HMM_OK) return s;
-        }
+    const int nflag = (int)std::min<int64_t>(h[ST_NFLAG], T);
+    if (nflag > 0) {   // tokens whose band did not fit: exact rows, then their top-k
+        const int* flagged = status + ST_FLAGS;
+        const int bx = (int)std::max<int64_t>(1, std::min<int64_t>((L + 127) / 128,
+                                                                   2 * device_sm_count()));
+        dsa_exact_rows_kernel<<<dim3(bx, nflag), 128, 0, st>>>(q, w, keys, L, pos0, (int)H,
+                                                              flagged, scores);
+        s = check_launch("dsa_exact_rows_kernel");
+        if (s != HMM_OK) return s;
+        const size_t fsm = sizeof(uint64_t) * KMAX;
+        dsa_row_select_kernel<<<nflag, SEL_THREADS, fsm, st>>>(scores, L, pos0, (int)topk,
+                                                               flagged, out_idx, out_sc);
+        s = check_launch("dsa_row_select_kernel");
+        if (s != HMM_OK) return s;
     }
     return HMM_OK;
 }
