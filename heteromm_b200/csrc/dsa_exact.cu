@@ -44,7 +44,6 @@ namespace {
 
 constexpr int DK = 128;                    // head dim: bytes per fp8 row and per limb row
 constexpr int NLIMB = 3;
-constexpr int KEY_LIMB_BYTES = NLIMB * DK; // 384 bytes of limbs per key
 constexpr int CAP_C = 8192;                // candidates per token
 constexpr int BAND_THREADS = 512;
 constexpr int BAND_SAMPLE = 4096;
@@ -77,50 +76,35 @@ __device__ __forceinline__ uint32_t limb_byte(int v, int i) {
     return (uint32_t)(l & 0xff);
 }
 
-// Limbs of 4 e4m3 bytes packed in w: three 32-bit words (limb 0, 1, 2), byte
-// order kept.  *nan is set if a byte is a NaN encoding.
-__device__ __forceinline__ void limbs4(uint32_t w, uint32_t out[3], bool* nan) {
-    out[0] = out[1] = out[2] = 0u;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const uint32_t byte = (w >> (8 * b)) & 0xffu;
-        *nan |= e4m3_is_nan(byte);
-        const int v = e4m3_scaled(byte);
-#pragma unroll
-        for (int i = 0; i < NLIMB; ++i) out[i] |= limb_byte(v, i) << (8 * b);
-    }
-}
-
 // ---------------------------------------------------------------------------
-// K0: per key, its limb rows [3][128] (int8) and ||k_j||_2 rounded up; flags
-// NaN encodings.  One warp per key, 4 bytes per lane.
+// K0: per key, ||k_j||_2 rounded up, and the maximum over keys; flags NaN
+// encodings.  One warp per key (4 bytes per lane), warps striding over keys.
 __global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
-                                    uint8_t* __restrict__ limbs, float* __restrict__ knorm,
-                                    int* __restrict__ status) {
-    const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                                    float* __restrict__ knorm, int* __restrict__ status) {
     const int lane = threadIdx.x & 31;
-    if (j >= L) return;
-    const uint32_t w = reinterpret_cast<const uint32_t*>(keys + j * DK)[lane];
-    uint32_t l[3];
+    const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    float kmax = 0.0f;
     bool nan = false;
-    limbs4(w, l, &nan);
+    for (int64_t j = w0; j < L; j += nw) {
+        const uint32_t w = reinterpret_cast<const uint32_t*>(keys + j * DK)[lane];
+        long long sq = 0;   // sum of v^2 (v = value * 2^9): exact in 64 bits
 #pragma unroll
-    for (int i = 0; i < NLIMB; ++i)
-        reinterpret_cast<uint32_t*>(limbs + j * KEY_LIMB_BYTES + i * DK)[lane] = l[i];
-    long long sq = 0;   // sum of v^2 (v = value * 2^9): exact in 64 bits
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t byte = (w >> (8 * b)) & 0xffu;
+            nan |= e4m3_is_nan(byte);
+            const long long v = e4m3_scaled(byte);
+            sq += v * v;
+        }
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const long long v = e4m3_scaled((w >> (8 * b)) & 0xffu);
-        sq += v * v;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(&status[ST_NAN], 1);
-    if (lane == 0) {
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         const float nrm = __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0));
-        knorm[j] = nrm;
-        atomicMax(&status[ST_KMAX], __float_as_int(nrm));   // nrm >= 0: int order = float order
+        if (lane == 0) knorm[j] = nrm;
+        kmax = fmaxf(kmax, nrm);
     }
+    if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(&status[ST_NAN], 1);
+    if (lane == 0 && kmax > 0.0f)
+        atomicMax(&status[ST_KMAX], __float_as_int(kmax));   // >= 0: int order = float order
 }
 
 // ---------------------------------------------------------------------------
@@ -449,7 +433,8 @@ struct RescoreSmem {
     static constexpr size_t A_OFF = 0;
     static constexpr size_t Q_OFF = A_OFF + (size_t)R_STAGES * R_A_STAGE;
     static constexpr size_t W_OFF = Q_OFF + 2 * (size_t)Q_BUF;
-    static constexpr size_t CTRL_OFF = W_OFF + 2 * H * sizeof(float);
+    static constexpr size_t LUT_OFF = W_OFF + 2 * H * sizeof(float);   // 256 limb entries
+    static constexpr size_t CTRL_OFF = LUT_OFF + 256 * sizeof(uint32_t);
     static constexpr size_t BYTES = CTRL_OFF + 256 + 1024;   // + barriers, + alignment slack
 };
 
@@ -466,7 +451,7 @@ struct RescoreCtrl {
 struct RescoreArgs {
     const uint8_t* q;          // [T][H][128] e4m3
     const float* w;            // [T][H]
-    const uint8_t* klimbs;     // [L][3][128]
+    const uint8_t* keys;       // [L][128] e4m3
     const int32_t* cand;       // [T][CAP_C]
     const int* cand_cnt;       // [T]
     float* exact;              // [T][CAP_C] exact scores of the candidates
@@ -502,17 +487,29 @@ __device__ __forceinline__ void r_abort(RescoreCtrl* c, int* status) {
     atomicExch(&status[ST_TIMEOUT], 1);
 }
 
-// 16-byte asynchronous copy global -> shared (L2 only), and its groups.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
+// Limb bytes of one e4m3 byte packed as (l0 | l1 << 8 | l2 << 16).
+__device__ __forceinline__ uint32_t limb_entry(uint32_t b) {
+    const int v = e4m3_scaled(b);
+    return limb_byte(v, 0) | (limb_byte(v, 1) << 8) | (limb_byte(v, 2) << 16);
 }
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+
+// Limbs of 16 e4m3 bytes through the table: out[i] = 16 bytes of limb i.
+__device__ __forceinline__ void limbs16_lut(const uint4 raw, const uint32_t* lut, uint4 out[3]) {
+    const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[3][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t x = wv[q];
+        const uint32_t e0 = lut[x & 255u], e1 = lut[(x >> 8) & 255u];
+        const uint32_t e2 = lut[(x >> 16) & 255u], e3 = lut[x >> 24];
+#pragma unroll
+        for (int i = 0; i < NLIMB; ++i) {
+            const uint32_t sel = 0x0040u + (uint32_t)i * 0x0011u;   // bytes i of (e_a, e_b)
+            o[i][q] = __byte_perm(__byte_perm(e0, e1, sel), __byte_perm(e2, e3, sel), 0x5410u);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NLIMB; ++i) out[i] = make_uint4(o[i][0], o[i][1], o[i][2], o[i][3]);
 }
 
 // Byte offset of 16-byte chunk c of row r in a K-major tile of 128-byte rows
@@ -575,25 +572,28 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
 
     if (warp < R_PROD_WARPS) {
         // ---------------------------------------------------------- producers
-        const int p = threadIdx.x;   // 0..127: the tile row this thread copies
+        // Each thread copies one candidate row per tile: the key's 128 e4m3
+        // bytes (loaded one tile ahead, its index two tiles ahead) become three
+        // limb rows through a 256-entry table.
+        const int p = threadIdx.x;   // 0..127
+        uint32_t* lut = reinterpret_cast<uint32_t*>(smem + S::LUT_OFF);
+        for (int b = p; b < 256; b += 32 * R_PROD_WARPS) lut[b] = limb_entry((uint32_t)b);
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * R_PROD_WARPS));   // producers only
         int tile_seq = 0, tok_seq = 0;
-        int pending = -1;            // stage whose copies are still in flight
         bool ok = true;
-        // completes the copies of the stage `pending`: wait for this thread's
-        // copies, make them visible to the tensor core, arrive
-        auto complete = [&](int keep) {
-            if (pending < 0) return;
-            if (keep) cp_async_wait<1>(); else cp_async_wait<0>();
-            fence_proxy_async_smem();
-            mbar_arrive(&ctl->a_full[pending]);
-            pending = -1;
+        auto load_key = [&](int j, uint4 raw[8]) {
+            const uint4* src = reinterpret_cast<const uint4*>(a.keys + (int64_t)j * DK);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) raw[c] = __ldg(src + c);
         };
         for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
             const int n = a.cand_cnt[t];
             if (n <= 0) continue;
             const int qb = tok_seq & 1;
             const int32_t* cl = a.cand + t * CAP_C;
-            int j_next = p < n ? cl[p] : 0;   // candidate of this thread's row in tile 0
+            int j1 = p + R_M < n ? cl[p + R_M] : -1;       // row p of tile 1
+            uint4 raw[8];
+            if (p < n) load_key(cl[p], raw);                // row p of tile 0
             if (!r_wait(&ctl->q_empty[qb], ((tok_seq >> 1) & 1) ^ 1, abort, a.wait_ns)) {
                 ok = false;
                 break;
@@ -603,15 +603,11 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const uint8_t* qt = a.q + t * (int64_t)H * DK;
             for (int e = p; e < H * 8; e += 32 * R_PROD_WARPS) {   // (row, 16-byte chunk)
                 const int r = e >> 3, c = e & 7;
-                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(qt + r * DK + c * 16));
-                uint32_t l[4][3];
-                bool nan = false;
-                limbs4(raw.x, l[0], &nan); limbs4(raw.y, l[1], &nan);
-                limbs4(raw.z, l[2], &nan); limbs4(raw.w, l[3], &nan);
+                uint4 l[3];
+                limbs16_lut(__ldg(reinterpret_cast<const uint4*>(qt + r * DK + c * 16)), lut, l);
 #pragma unroll
                 for (int i = 0; i < NLIMB; ++i)
-                    *reinterpret_cast<uint4*>(Qb + i * S::Q_LIMB + sw128(r, c)) =
-                        make_uint4(l[0][i], l[1][i], l[2][i], l[3][i]);
+                    *reinterpret_cast<uint4*>(Qb + i * S::Q_LIMB + sw128(r, c)) = l[i];
             }
             for (int h = p; h < H; h += 32 * R_PROD_WARPS) Ws[qb * H + h] = a.w[t * H + h];
             fence_proxy_async_smem();
@@ -621,29 +617,32 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
                 const int s = tile_seq % R_STAGES;
-                const int j = j_next;
                 const int row = ti * R_M + p;
+                const int j2 = row + 2 * R_M < n ? cl[row + 2 * R_M] : -1;
+                uint4 nxt[8];
+                if (j1 >= 0) load_key(j1, nxt);
                 if (!r_wait(&ctl->a_empty[s], ((tile_seq / R_STAGES) & 1) ^ 1, abort, a.wait_ns)) {
                     ok = false;
                     break;
                 }
                 if (row < n) {
                     unsigned char* Ab = As + s * R_A_STAGE;
-                    const unsigned char* src = a.klimbs + (int64_t)j * KEY_LIMB_BYTES;
 #pragma unroll
-                    for (int i = 0; i < NLIMB; ++i)
+                    for (int c = 0; c < 8; ++c) {
+                        uint4 l[3];
+                        limbs16_lut(raw[c], lut, l);
 #pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            cp_async16(Ab + i * R_A_LIMB + sw128(p, c), src + i * DK + c * 16);
+                        for (int i = 0; i < NLIMB; ++i)
+                            *reinterpret_cast<uint4*>(Ab + i * R_A_LIMB + sw128(p, c)) = l[i];
+                    }
                 }
-                cp_async_commit();
-                if (row + R_M < n) j_next = cl[row + R_M];   // next tile's candidate, early
-                complete(1);                                   // the previous tile
-                pending = s;
+                fence_proxy_async_smem();
+                mbar_arrive(&ctl->a_full[s]);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) raw[c] = nxt[c];
+                j1 = j2;
             }
-            complete(0);
         }
-        complete(0);
         if (!ok && lane == 0) r_abort(ctl, a.status);
     } else if (warp == 4) {
         // --------------------------------------------------------- MMA issuer
@@ -896,14 +895,13 @@ size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 // Workspace of the exact selection: status words and flagged tokens, key
 // limbs and norms, candidate lists and their exact scores.
 struct DsaExactLayout {
-    size_t status, limbs, knorm, cand, cand_cnt, exact, total;
+    size_t status, knorm, cand, cand_cnt, exact, total;
 };
 
 static DsaExactLayout dsa_exact_layout(int64_t T, int64_t L) {
     DsaExactLayout d;
     size_t o = 0;
     d.status = o; o += up256(sizeof(int) * (size_t)(ST_FLAGS + T));
-    d.limbs = o; o += up256((size_t)L * KEY_LIMB_BYTES);
     d.knorm = o; o += up256(sizeof(float) * (size_t)L);
     d.cand = o; o += up256(sizeof(int32_t) * (size_t)T * CAP_C);
     d.cand_cnt = o; o += up256(sizeof(int) * (size_t)T);
@@ -924,9 +922,9 @@ hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* 
     *status_out = status;
     HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int) * ST_FLAGS, st));
     if (L > 0) {
-        const int64_t threads = L * 32;
-        dsa_key_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
-            keys, L, w + d.limbs, reinterpret_cast<float*>(w + d.knorm), status);
+        const int64_t blocks = std::min<int64_t>((L + 7) / 8, 8 * (int64_t)device_sm_count());
+        dsa_key_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(
+            keys, L, reinterpret_cast<float*>(w + d.knorm), status);
         return check_launch("dsa_key_prep_kernel");
     }
     return HMM_OK;
@@ -958,7 +956,7 @@ hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float
     if (s != HMM_OK) return s;
 
     RescoreArgs ra;
-    ra.q = q; ra.w = w; ra.klimbs = wb + d.limbs; ra.cand = cand; ra.cand_cnt = cand_cnt;
+    ra.q = q; ra.w = w; ra.keys = keys; ra.cand = cand; ra.cand_cnt = cand_cnt;
     ra.exact = exact; ra.status = status; ra.T = T; ra.wait_ns = wait_limit_ns();
     const int grid = std::max(1, (int)std::min<int64_t>(device_sm_count(), T));
     const ProfileMark pm = profile_begin(st);
