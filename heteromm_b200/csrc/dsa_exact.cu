@@ -350,13 +350,22 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
     if ((a.L & 3) == 0) {
         const float4* row4 = reinterpret_cast<const float4*>(row);
         const int64_t n4 = (vis + 3) >> 2;   // the last float4 may hold invisible (-inf) keys
-        for (int64_t b0 = threadIdx.x & ~31; b0 < n4; b0 += BAND_THREADS) {
-            const int64_t i4 = b0 + lane;
-            const float4 v = i4 < n4 ? __ldg(row4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            take(v.x, 4 * i4 + 0, 4 * i4 + 0 < vis);
-            take(v.y, 4 * i4 + 1, 4 * i4 + 1 < vis);
-            take(v.z, 4 * i4 + 2, 4 * i4 + 2 < vis);
-            take(v.w, 4 * i4 + 3, 4 * i4 + 3 < vis);
+        // four float4 per lane in flight per step
+        for (int64_t b0 = threadIdx.x & ~31; b0 < n4; b0 += 4 * BAND_THREADS) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t i4 = b0 + u * BAND_THREADS + lane;
+                v[u] = i4 < n4 ? __ldg(row4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t i4 = b0 + u * BAND_THREADS + lane;
+                take(v[u].x, 4 * i4 + 0, 4 * i4 + 0 < vis);
+                take(v[u].y, 4 * i4 + 1, 4 * i4 + 1 < vis);
+                take(v[u].z, 4 * i4 + 2, 4 * i4 + 2 < vis);
+                take(v[u].w, 4 * i4 + 3, 4 * i4 + 3 < vis);
+            }
         }
     } else {
         for (int64_t j0 = threadIdx.x & ~31; j0 < vis; j0 += BAND_THREADS) {
@@ -423,8 +432,8 @@ constexpr int R_A_LIMB = R_M * DK;               // 16 KB: one limb of a tile
 constexpr int R_A_STAGE = NLIMB * R_A_LIMB;      // 48 KB
 constexpr int R_PROD_WARPS = 4;
 constexpr int R_THREADS = 32 * 16;               // producers 0-3, MMA 4, TMEM 5, epilogue 8-15
-constexpr int R_SLOTS = 8;                       // accumulator slots of H columns (a ring)
 constexpr int R_GROUPS = 5;                      // limb scales 64^0 .. 64^4
+constexpr int R_HMAX = 32;                       // heads per MMA pass (N) at most
 
 template <int H>
 struct RescoreSmem {
@@ -441,8 +450,8 @@ struct RescoreSmem {
 struct RescoreCtrl {
     uint64_t a_full[R_STAGES], a_empty[R_STAGES];
     uint64_t q_full[2], q_empty[2];
-    uint64_t acc_full[2];            // by tile parity: one epilogue warpgroup each
-    uint64_t slot_empty[R_SLOTS];
+    uint64_t acc_full[8];            // per half-tile slot of TMEM (MMA commit)
+    uint64_t slot_empty[8];          // per slot: drained by its epilogue warpgroup
     uint64_t drain;                  // MMA warp: every MMA issued has completed (abort path)
     uint32_t tmem_base;
     int abort;
@@ -524,11 +533,12 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 //               limbs gathered by cp.async (A operand, 3 x 16 KB, 128-byte
 //               swizzle), one tile's copies in flight while the previous
 //               tile's complete
-//   warp 4      MMA issuer: per tile, 9 limb pairs x 4 K-steps of
-//               tcgen05.mma kind::i8 (M = 128 candidates, N = H heads, K = 32)
-//               into 5 accumulators of H columns (one per scale 64^g), taken
-//               from a ring of 8 TMEM slots so that the next tile's first
-//               groups start while the epilogue drains the last
+//   warp 4      MMA issuer: per tile and half of the heads (N = 32 heads,
+//               or all H if fewer), 9 limb pairs x 4 K-steps of tcgen05.mma
+//               kind::i8 (M = 128 candidates, K = 32) into 5 accumulators of
+//               N columns (one per scale 64^g): one TMEM slot of 5N columns,
+//               from a ring of slots, so MMAs run while both epilogue
+//               warpgroups drain earlier halves
 //   warp 5      TMEM allocator
 //   warps 8-15  epilogue, two warpgroups (tile parity): thread = candidate;
 //               joins the 5 groups exactly and sums the heads in order
@@ -543,7 +553,11 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
     RescoreCtrl* ctl = reinterpret_cast<RescoreCtrl*>(smem + S::CTRL_OFF);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort = &ctl->abort;
-    constexpr uint32_t TMEM_COLS = R_SLOTS * H < 32 ? 32 : R_SLOTS * H;
+    constexpr int HW = H < R_HMAX ? H : R_HMAX;        // heads per half (MMA N)
+    constexpr int NH = H / HW;                         // halves per tile
+    constexpr int SLOT_COLS = R_GROUPS * HW;
+    constexpr int NSLOT = 512 / SLOT_COLS < 8 ? 512 / SLOT_COLS : 8;   // 3 (HW 32), 6 (HW 16)
+    constexpr uint32_t TMEM_COLS = 512;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < R_STAGES; ++s) {
@@ -553,9 +567,11 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->q_full[b], 32 * R_PROD_WARPS);
             mbar_init(&ctl->q_empty[b], 1 + 8);   // the MMAs' commit + the 8 epilogue warps
-            mbar_init(&ctl->acc_full[b], 1);
         }
-        for (int s = 0; s < R_SLOTS; ++s) mbar_init(&ctl->slot_empty[s], 4);
+        for (int s = 0; s < NSLOT; ++s) {
+            mbar_init(&ctl->acc_full[s], 1);
+            mbar_init(&ctl->slot_empty[s], 4);
+        }
         mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
         fence_barrier_init();
@@ -646,7 +662,6 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
         if (!ok && lane == 0) r_abort(ctl, a.status);
     } else if (warp == 4) {
         // --------------------------------------------------------- MMA issuer
-        constexpr uint32_t idesc = idesc_i8(R_M, H);
         int tile_seq = 0, tok_seq = 0;
         bool ok = true, issued = false;
         for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
@@ -667,37 +682,41 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                     break;
                 }
                 const uint32_t abase = smem_u32(As + s * R_A_STAGE);
-                for (int g = 0; g < R_GROUPS; ++g) {
-                    const int nslot = R_GROUPS * tile_seq + g;
-                    if (!r_wait(&ctl->slot_empty[nslot % R_SLOTS], ((nslot / R_SLOTS) & 1) ^ 1,
-                                abort, a.wait_ns)) {
+                constexpr uint32_t idesc_h = idesc_i8(R_M, HW);
+                for (int h2 = 0; h2 < NH; ++h2) {
+                    const int u = tile_seq * NH + h2;   // half-tile sequence number
+                    const int slot = u % NSLOT;
+                    if (!r_wait(&ctl->slot_empty[slot], ((u / NSLOT) & 1) ^ 1, abort, a.wait_ns)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     if (lane == 0) {
-                        const uint32_t d = tmem + (uint32_t)((nslot % R_SLOTS) * H);
-                        bool first = true;
-                        // key limb i times query limb g - i, scale 64^g
-                        for (int i = 0; i < NLIMB; ++i) {
-                            const int iq = g - i;
-                            if (iq < 0 || iq >= NLIMB) continue;
+                        for (int g = 0; g < R_GROUPS; ++g) {
+                            const uint32_t d = tmem + (uint32_t)(slot * SLOT_COLS + g * HW);
+                            bool first = true;
+                            // key limb i times query limb g - i, scale 64^g
+                            for (int i = 0; i < NLIMB; ++i) {
+                                const int iq = g - i;
+                                if (iq < 0 || iq >= NLIMB) continue;
 #pragma unroll
-                            for (int kc = 0; kc < DK / 32; ++kc) {
-                                mma_i8(d, desc_k_sw128(abase + i * R_A_LIMB + kc * 32),
-                                       desc_k_sw128(qbase + iq * S::Q_LIMB + kc * 32), idesc,
-                                       first ? 0u : 1u);
-                                first = false;
-                                issued = true;
+                                for (int kc = 0; kc < DK / 32; ++kc) {
+                                    mma_i8(d, desc_k_sw128(abase + i * R_A_LIMB + kc * 32),
+                                           desc_k_sw128(qbase + iq * S::Q_LIMB + h2 * HW * DK +
+                                                        kc * 32),
+                                           idesc_h, first ? 0u : 1u);
+                                    first = false;
+                                    issued = true;
+                                }
                             }
                         }
+                        mma_commit(&ctl->acc_full[slot]);
                     }
                     __syncwarp();
                 }
                 if (!ok) break;
                 if (lane == 0) {
                     mma_commit(&ctl->a_empty[s]);
-                    mma_commit(&ctl->acc_full[tile_seq & 1]);
                     if (ti == tiles - 1) mma_commit(&ctl->q_empty[qb]);
                 }
                 __syncwarp();
@@ -729,40 +748,41 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
                 if ((tile_seq & 1) != wg) continue;
-                if (!r_wait(&ctl->acc_full[wg], (tile_seq >> 1) & 1, abort, a.wait_ns)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                uint32_t col[R_GROUPS];
-#pragma unroll
-                for (int g = 0; g < R_GROUPS; ++g)
-                    col[g] = tmem + ((uint32_t)(sub * 32) << 16) +
-                             (uint32_t)(((R_GROUPS * tile_seq + g) % R_SLOTS) * H);
                 float total = 0.0f;
-#pragma unroll 1
-                for (int h0 = 0; h0 < H; h0 += 16) {
-                    uint32_t d[R_GROUPS][16];
-#pragma unroll
-                    for (int g = 0; g < R_GROUPS; ++g) tmem_ld_x16(col[g] + (uint32_t)h0, d[g]);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int h = 0; h < 16; ++h) {
-                        // v = D0 + 64 D1 + 64^2 D2 + 64^3 D3 + 64^4 D4, exactly
-                        const int A = (int)d[0][h] + 64 * (int)d[1][h];   // |A| < 2^27
-                        const int B = (int)d[2][h] + 64 * (int)d[3][h];   // |B| < 2^27
-                        const long long v = (long long)A + ((long long)B << 12) +
-                                            ((long long)(int)d[4][h] << 24);
-                        const float x = fmaxf(__ll2float_rn(v) * (1.0f / 262144.0f), 0.0f);
-                        total = __fadd_rn(total, __fmul_rn(wq[h0 + h], x));
+                for (int h2 = 0; h2 < NH && ok; ++h2) {
+                    const int u = tile_seq * NH + h2;
+                    const int slot = u % NSLOT;
+                    if (!r_wait(&ctl->acc_full[slot], (u / NSLOT) & 1, abort, a.wait_ns)) {
+                        ok = false;
+                        break;
                     }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0)
+                    tc_fence_after();
+                    const uint32_t cbase = tmem + ((uint32_t)(sub * 32) << 16) +
+                                           (uint32_t)(slot * SLOT_COLS);
+#pragma unroll 1
+                    for (int h0 = 0; h0 < HW; h0 += 16) {
+                        uint32_t d[R_GROUPS][16];
 #pragma unroll
-                    for (int g = 0; g < R_GROUPS; ++g)
-                        mbar_arrive(&ctl->slot_empty[(R_GROUPS * tile_seq + g) % R_SLOTS]);
+                        for (int g = 0; g < R_GROUPS; ++g)
+                            tmem_ld_x16(cbase + (uint32_t)(g * HW + h0), d[g]);
+                        tmem_wait_ld();
+                        const float* wh = wq + h2 * HW + h0;
+#pragma unroll
+                        for (int h = 0; h < 16; ++h) {
+                            // v = D0 + 64 D1 + 64^2 D2 + 64^3 D3 + 64^4 D4, exactly
+                            const int A = (int)d[0][h] + 64 * (int)d[1][h];   // |A| < 2^27
+                            const int B = (int)d[2][h] + 64 * (int)d[3][h];   // |B| < 2^27
+                            const long long v = (long long)A + ((long long)B << 12) +
+                                                ((long long)(int)d[4][h] << 24);
+                            const float x = fmaxf(__ll2float_rn(v) * (1.0f / 262144.0f), 0.0f);
+                            total = __fadd_rn(total, __fmul_rn(wh[h], x));
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ctl->slot_empty[slot]);
+                }
+                if (!ok) break;
                 const int row = ti * R_M + r;
                 if (row < n) a.exact[t * CAP_C + row] = total;
             }
