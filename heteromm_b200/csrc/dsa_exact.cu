@@ -77,10 +77,10 @@ __device__ __forceinline__ uint32_t limb_byte(int v, int i) {
 }
 
 // ---------------------------------------------------------------------------
-// K0: per key, ||k_j||_2 rounded up, and the maximum over keys; flags NaN
-// encodings.  One warp per key (4 bytes per lane), warps striding over keys.
+// K0: max_j ||k_j||_2 rounded up; flags NaN encodings.  One warp per key (4
+// bytes per lane), warps striding over keys.
 __global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
-                                    float* __restrict__ knorm, int* __restrict__ status) {
+                                    int* __restrict__ status) {
     const int lane = threadIdx.x & 31;
     const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -98,9 +98,7 @@ __global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        const float nrm = __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0));
-        if (lane == 0) knorm[j] = nrm;
-        kmax = fmaxf(kmax, nrm);
+        kmax = fmaxf(kmax, __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0)));
     }
     if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(&status[ST_NAN], 1);
     if (lane == 0 && kmax > 0.0f)
@@ -205,7 +203,6 @@ struct BandArgs {
     const float* scores;     // [T][L] approximate scores (tensor-core pass)
     const uint8_t* q;        // [T][H][128] e4m3
     const float* w;          // [T][H]
-    const float* knorm;      // [L]
     int32_t* cand;           // [T][CAP_C] candidate keys
     int* cand_cnt;           // [T]
     int* status;
@@ -253,13 +250,13 @@ __device__ __forceinline__ uint32_t key_floor(KeyAt key_at, int64_t M, int64_t n
     return prefix;
 }
 
-// One block per token.  Bounds: tol_j = E_t * ||k_j|| (E_t = C_TOL * ||u_t||),
-// lo_j = s~_j - tol_j, hi_j = s~_j + tol_j, all rounded outwards.
+// One block per token.  Bounds: tol = E_t * max_j ||k_j|| (E_t = C_TOL *
+// ||u_t||), which is >= every key's C_TOL * ||u_t|| ||k_j||; lo_j = s~_j - tol,
+// hi_j = s~_j + tol, rounded outwards.
 //   1. tau: a floor of the r1-th largest lo of a strided sample, r1 chosen so
 //      that at least m keys have lo >= tau except with negligible probability
-//   2. one read of the row collects every key with s~ + E_t * max_j ||k_j|| >=
-//      tau (so every key with lo >= tau; a miss of the sample only costs the
-//      exact-row path)
+//   2. one read of the row collects every key with hi >= tau (so every key
+//      with lo >= tau; a miss of the sample only costs the exact-row path)
 //   3. Lambda: a floor of the m-th largest lo among the collected keys (all
 //      keys with lo >= tau are there, at least m of them), so Lambda <= the
 //      exact k-th score
@@ -286,6 +283,7 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
         const int d = threadIdx.x & (DK - 1), hq = threadIdx.x >> 7;   // 4 head quarters
         float u = 0.0f;
         bool nan = false;
+#pragma unroll 4
         for (int h = hq; h < a.H; h += BAND_THREADS / DK) {
             const uint32_t b = qt[h * DK + d];
             nan |= e4m3_is_nan(b);
@@ -321,16 +319,16 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
         return;
     }
     const float* row = a.scores + t * a.L;
-    const float tol_max = __fmul_ru(E, __int_as_float(a.status[ST_KMAX]));
-    auto lo_key = [&](float s, int64_t j) { return f32_key(__fsub_rd(s, __fmul_ru(E, a.knorm[j]))); };
-    auto hi_key = [&](float s, int64_t j) { return f32_key(__fadd_ru(s, __fmul_ru(E, a.knorm[j]))); };
+    // one tolerance for every key of the token: E_t * max_j ||k_j|| (>= tol_j)
+    const float tol = __fmul_ru(E, __int_as_float(a.status[ST_KMAX]));
+    auto lo_key = [tol](float s) { return f32_key(__fsub_rd(s, tol)); };
+    auto hi_key = [tol](float s) { return f32_key(__fadd_ru(s, tol)); };
 
     // 1. tau from the sample: it holds Binomial(S, m / vis) keys whose lo
     //    reaches the k-th; take the (mean + 5 sd + 8)-th largest
-    for (int i = threadIdx.x; i < BAND_SAMPLE; i += BAND_THREADS) {
-        const int64_t j = (int64_t)i * vis / BAND_SAMPLE;
-        samp[i] = lo_key(row[j], j);
-    }
+#pragma unroll 8
+    for (int i = threadIdx.x; i < BAND_SAMPLE; i += BAND_THREADS)
+        samp[i] = lo_key(row[(int64_t)i * vis / BAND_SAMPLE]);
     __syncthreads();
     const double p_k = (double)m / (double)vis;
     const double mean_k = BAND_SAMPLE * p_k;
@@ -342,7 +340,7 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
     // 2. one read of the row (each lane 4 consecutive scores; warp-uniform loop)
     const int lane = threadIdx.x & 31;
     auto take = [&](float s, int64_t j, bool valid) {
-        const bool hit = valid && f32_key(__fadd_ru(s, tol_max)) >= tau;
+        const bool hit = valid && hi_key(s) >= tau;
         const int pos = warp_append(hit, &cnt);
         if (pos >= 0 && pos < BAND_COLLECT)
             col[pos] = ((uint64_t)__float_as_uint(s) << 32) | (uint64_t)j;
@@ -379,10 +377,7 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
         for (int i0 = threadIdx.x & ~31; i0 < C; i0 += BAND_THREADS) {
             const int i = i0 + lane;
             bool hit = false;
-            if (i < C) {
-                const uint64_t e = col[i];
-                hit = lo_key(__uint_as_float((uint32_t)(e >> 32)), (int64_t)(uint32_t)e) >= tau;
-            }
+            if (i < C) hit = lo_key(__uint_as_float((uint32_t)(col[i] >> 32))) >= tau;
             warp_append(hit, &cnt_lo);
         }
     __syncthreads();
@@ -392,11 +387,7 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
     }
     // 3. Lambda
     const uint32_t lam = key_floor<BAND_THREADS>(
-        [&](int64_t i) {
-            const uint64_t e = col[i];
-            return lo_key(__uint_as_float((uint32_t)(e >> 32)), (int64_t)(uint32_t)e);
-        },
-        C, m, sm);
+        [&](int64_t i) { return lo_key(__uint_as_float((uint32_t)(col[i] >> 32))); }, C, m, sm);
     // 4. the candidates
     for (int i0 = threadIdx.x & ~31; i0 < C; i0 += BAND_THREADS) {
         const int i = i0 + lane;
@@ -405,7 +396,7 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
         if (i < C) {
             const uint64_t e = col[i];
             j = (int64_t)(uint32_t)e;
-            hit = hi_key(__uint_as_float((uint32_t)(e >> 32)), j) >= lam;
+            hit = hi_key(__uint_as_float((uint32_t)(e >> 32))) >= lam;
         }
         const int pos = warp_append(hit, &out_n);
         if (pos >= 0 && pos < CAP_C) cand[pos] = (int32_t)j;
@@ -483,6 +474,26 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// fl32(v * 2^-18) for v = D0 + 64 D1 + 64^2 D2 + 64^3 D3 + 64^4 D4 (the exact
+// dot of the limbs, |v| < 2^46), correctly rounded with full-rate int32 and
+// fp32 instructions only:
+//   t = A + 4096 (B mod 2048), A = D0 + 64 D1, B = D2 + 64 D3   (|t| < 2^28)
+//   v = Q 2^23 + R,  R = t mod 2^23 in [0, 2^23),  Q = floor(t / 2^23)
+//       + floor(B / 2048) + 2 D4  (|Q| < 2^22)
+// Q 2^5 and R 2^-18 are exact floats (the 1.5 * 2^23 and 2^23 magic-number
+// conversions, scaled by exact fused multiply-adds), so their one rounded sum
+// is the rounded v * 2^-18.
+__device__ __forceinline__ float exact_dot_f32(int d0, int d1, int d2, int d3, int d4) {
+    const int A = d0 + 64 * d1;                       // |A| < 2^27
+    const int B = d2 + 64 * d3;                       // |B| < 2^27
+    const int t = A + ((B & 2047) << 12);
+    const int R = t & ((1 << 23) - 1);
+    const int Q = (t >> 23) + (B >> 11) + 2 * d4;
+    const float X = __fmaf_rn(__int_as_float(0x4B400000 + Q), 32.0f, -402653184.0f);   // Q 2^5
+    const float Y = __fmaf_rn(__int_as_float(0x4B000000 | R), 0x1p-18f, -32.0f);       // R 2^-18
+    return __fadd_rn(X, Y);
 }
 
 __device__ __forceinline__ bool r_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
@@ -769,12 +780,9 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                         const float* wh = wq + h2 * HW + h0;
 #pragma unroll
                         for (int h = 0; h < 16; ++h) {
-                            // v = D0 + 64 D1 + 64^2 D2 + 64^3 D3 + 64^4 D4, exactly
-                            const int A = (int)d[0][h] + 64 * (int)d[1][h];   // |A| < 2^27
-                            const int B = (int)d[2][h] + 64 * (int)d[3][h];   // |B| < 2^27
-                            const long long v = (long long)A + ((long long)B << 12) +
-                                                ((long long)(int)d[4][h] << 24);
-                            const float x = fmaxf(__ll2float_rn(v) * (1.0f / 262144.0f), 0.0f);
+                            const float x = fmaxf(exact_dot_f32((int)d[0][h], (int)d[1][h],
+                                                                (int)d[2][h], (int)d[3][h],
+                                                                (int)d[4][h]), 0.0f);
                             total = __fadd_rn(total, __fmul_rn(wh[h], x));
                         }
                     }
@@ -915,14 +923,13 @@ size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 // Workspace of the exact selection: status words and flagged tokens, key
 // limbs and norms, candidate lists and their exact scores.
 struct DsaExactLayout {
-    size_t status, knorm, cand, cand_cnt, exact, total;
+    size_t status, cand, cand_cnt, exact, total;
 };
 
 static DsaExactLayout dsa_exact_layout(int64_t T, int64_t L) {
     DsaExactLayout d;
     size_t o = 0;
     d.status = o; o += up256(sizeof(int) * (size_t)(ST_FLAGS + T));
-    d.knorm = o; o += up256(sizeof(float) * (size_t)L);
     d.cand = o; o += up256(sizeof(int32_t) * (size_t)T * CAP_C);
     d.cand_cnt = o; o += up256(sizeof(int) * (size_t)T);
     d.exact = o; o += up256(sizeof(float) * (size_t)T * CAP_C);
@@ -943,8 +950,7 @@ hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* 
     HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int) * ST_FLAGS, st));
     if (L > 0) {
         const int64_t blocks = std::min<int64_t>((L + 7) / 8, 8 * (int64_t)device_sm_count());
-        dsa_key_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(
-            keys, L, reinterpret_cast<float*>(w + d.knorm), status);
+        dsa_key_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(keys, L, status);
         return check_launch("dsa_key_prep_kernel");
     }
     return HMM_OK;
@@ -966,7 +972,6 @@ hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float
 
     BandArgs ba;
     ba.scores = scores; ba.q = q; ba.w = w;
-    ba.knorm = reinterpret_cast<const float*>(wb + d.knorm);
     ba.cand = cand; ba.cand_cnt = cand_cnt; ba.status = status;
     ba.T = T; ba.L = L; ba.pos0 = pos0; ba.H = (int)H; ba.k = (int)topk;
     HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_band_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
