@@ -76,6 +76,31 @@ __device__ __forceinline__ uint32_t limb_byte(int v, int i) {
     return (uint32_t)(l & 0xff);
 }
 
+// Limb bytes of one e4m3 byte packed as (l0 | l1 << 8 | l2 << 16).
+__device__ __forceinline__ uint32_t limb_entry(uint32_t b) {
+    const int v = e4m3_scaled(b);
+    return limb_byte(v, 0) | (limb_byte(v, 1) << 8) | (limb_byte(v, 2) << 16);
+}
+
+// Limbs of 16 e4m3 bytes through the table: out[i] = 16 bytes of limb i.
+__device__ __forceinline__ void limbs16_lut(const uint4 raw, const uint32_t* lut, uint4 out[3]) {
+    const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[3][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t x = wv[q];
+        const uint32_t e0 = lut[x & 255u], e1 = lut[(x >> 8) & 255u];
+        const uint32_t e2 = lut[(x >> 16) & 255u], e3 = lut[x >> 24];
+#pragma unroll
+        for (int i = 0; i < NLIMB; ++i) {
+            const uint32_t sel = 0x0040u + (uint32_t)i * 0x0011u;   // bytes i of (e_a, e_b)
+            o[i][q] = __byte_perm(__byte_perm(e0, e1, sel), __byte_perm(e2, e3, sel), 0x5410u);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NLIMB; ++i) out[i] = make_uint4(o[i][0], o[i][1], o[i][2], o[i][3]);
+}
+
 // ---------------------------------------------------------------------------
 // K0: max_j ||k_j||_2 rounded up; flags NaN encodings.  One warp per key (4
 // bytes per lane), warps striding over keys.
@@ -103,6 +128,27 @@ __global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
     if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(&status[ST_NAN], 1);
     if (lane == 0 && kmax > 0.0f)
         atomicMax(&status[ST_KMAX], __float_as_int(kmax));   // >= 0: int order = float order
+}
+
+// K0b: the keys' limb rows [L][3][128] (int8), written just before the
+// rescoring so that they are still in L2 when its gather reads them.  One
+// thread per 16 key bytes.
+__global__ void dsa_key_limbs_kernel(const uint8_t* __restrict__ keys, int64_t L,
+                                     uint8_t* __restrict__ limbs) {
+    __shared__ uint32_t lut[256];
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) lut[b] = limb_entry((uint32_t)b);
+    __syncthreads();
+    const int64_t n16 = L * (DK / 16);
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n16;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = e >> 3;
+        const int c = (int)(e & 7);
+        uint4 l[3];
+        limbs16_lut(__ldg(reinterpret_cast<const uint4*>(keys) + e), lut, l);
+#pragma unroll
+        for (int i = 0; i < NLIMB; ++i)
+            *reinterpret_cast<uint4*>(limbs + j * (NLIMB * DK) + i * DK + c * 16) = l[i];
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -451,7 +497,7 @@ struct RescoreCtrl {
 struct RescoreArgs {
     const uint8_t* q;          // [T][H][128] e4m3
     const float* w;            // [T][H]
-    const uint8_t* keys;       // [L][128] e4m3
+    const uint8_t* klimbs;     // [L][3][128] key limbs
     const int32_t* cand;       // [T][CAP_C]
     const int* cand_cnt;       // [T]
     float* exact;              // [T][CAP_C] exact scores of the candidates
@@ -507,29 +553,17 @@ __device__ __forceinline__ void r_abort(RescoreCtrl* c, int* status) {
     atomicExch(&status[ST_TIMEOUT], 1);
 }
 
-// Limb bytes of one e4m3 byte packed as (l0 | l1 << 8 | l2 << 16).
-__device__ __forceinline__ uint32_t limb_entry(uint32_t b) {
-    const int v = e4m3_scaled(b);
-    return limb_byte(v, 0) | (limb_byte(v, 1) << 8) | (limb_byte(v, 2) << 16);
+// 16-byte asynchronous copy global -> shared (L2 only), and its groups.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
 }
-
-// Limbs of 16 e4m3 bytes through the table: out[i] = 16 bytes of limb i.
-__device__ __forceinline__ void limbs16_lut(const uint4 raw, const uint32_t* lut, uint4 out[3]) {
-    const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
-    uint32_t o[3][4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const uint32_t x = wv[q];
-        const uint32_t e0 = lut[x & 255u], e1 = lut[(x >> 8) & 255u];
-        const uint32_t e2 = lut[(x >> 16) & 255u], e3 = lut[x >> 24];
-#pragma unroll
-        for (int i = 0; i < NLIMB; ++i) {
-            const uint32_t sel = 0x0040u + (uint32_t)i * 0x0011u;   // bytes i of (e_a, e_b)
-            o[i][q] = __byte_perm(__byte_perm(e0, e1, sel), __byte_perm(e2, e3, sel), 0x5410u);
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < NLIMB; ++i) out[i] = make_uint4(o[i][0], o[i][1], o[i][2], o[i][3]);
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Byte offset of 16-byte chunk c of row r in a K-major tile of 128-byte rows
@@ -599,28 +633,30 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
 
     if (warp < R_PROD_WARPS) {
         // ---------------------------------------------------------- producers
-        // Each thread copies one candidate row per tile: the key's 128 e4m3
-        // bytes (loaded one tile ahead, its index two tiles ahead) become three
-        // limb rows through a 256-entry table.
+        // Each thread copies one candidate row per tile: its three limb rows
+        // (384 B) by cp.async; one tile's copies stay in flight while the
+        // previous tile's complete, and the next tile's candidate index is
+        // read a tile early.
         const int p = threadIdx.x;   // 0..127
         uint32_t* lut = reinterpret_cast<uint32_t*>(smem + S::LUT_OFF);
         for (int b = p; b < 256; b += 32 * R_PROD_WARPS) lut[b] = limb_entry((uint32_t)b);
         asm volatile("bar.sync 1, %0;" ::"n"(32 * R_PROD_WARPS));   // producers only
         int tile_seq = 0, tok_seq = 0;
+        int pending = -1;            // stage whose copies are still in flight
         bool ok = true;
-        auto load_key = [&](int j, uint4 raw[8]) {
-            const uint4* src = reinterpret_cast<const uint4*>(a.keys + (int64_t)j * DK);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) raw[c] = __ldg(src + c);
+        auto complete = [&](int keep) {
+            if (pending < 0) return;
+            if (keep) cp_async_wait<1>(); else cp_async_wait<0>();
+            fence_proxy_async_smem();
+            mbar_arrive(&ctl->a_full[pending]);
+            pending = -1;
         };
         for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
             const int n = a.cand_cnt[t];
             if (n <= 0) continue;
             const int qb = tok_seq & 1;
             const int32_t* cl = a.cand + t * CAP_C;
-            int j1 = p + R_M < n ? cl[p + R_M] : -1;       // row p of tile 1
-            uint4 raw[8];
-            if (p < n) load_key(cl[p], raw);                // row p of tile 0
+            int j_next = p < n ? cl[p] : 0;   // candidate of this thread's row in tile 0
             if (!r_wait(&ctl->q_empty[qb], ((tok_seq >> 1) & 1) ^ 1, abort, a.wait_ns)) {
                 ok = false;
                 break;
@@ -644,32 +680,29 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
                 const int s = tile_seq % R_STAGES;
+                const int j = j_next;
                 const int row = ti * R_M + p;
-                const int j2 = row + 2 * R_M < n ? cl[row + 2 * R_M] : -1;
-                uint4 nxt[8];
-                if (j1 >= 0) load_key(j1, nxt);
                 if (!r_wait(&ctl->a_empty[s], ((tile_seq / R_STAGES) & 1) ^ 1, abort, a.wait_ns)) {
                     ok = false;
                     break;
                 }
                 if (row < n) {
                     unsigned char* Ab = As + s * R_A_STAGE;
+                    const unsigned char* src = a.klimbs + (int64_t)j * (NLIMB * DK);
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        uint4 l[3];
-                        limbs16_lut(raw[c], lut, l);
+                    for (int i = 0; i < NLIMB; ++i)
 #pragma unroll
-                        for (int i = 0; i < NLIMB; ++i)
-                            *reinterpret_cast<uint4*>(Ab + i * R_A_LIMB + sw128(p, c)) = l[i];
-                    }
+                        for (int c = 0; c < 8; ++c)
+                            cp_async16(Ab + i * R_A_LIMB + sw128(p, c), src + i * DK + c * 16);
                 }
-                fence_proxy_async_smem();
-                mbar_arrive(&ctl->a_full[s]);
-#pragma unroll
-                for (int c = 0; c < 8; ++c) raw[c] = nxt[c];
-                j1 = j2;
+                cp_async_commit();
+                if (row + R_M < n) j_next = cl[row + R_M];   // next tile's candidate, early
+                complete(1);                                   // the previous tile
+                pending = s;
             }
+            complete(0);
         }
+        complete(0);
         if (!ok && lane == 0) r_abort(ctl, a.status);
     } else if (warp == 4) {
         // --------------------------------------------------------- MMA issuer
@@ -703,24 +736,27 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                     }
                     tc_fence_after();
                     if (lane == 0) {
+                        // descriptors from two bases: the start-address field
+                        // (bits 0-13, address / 16) takes the byte offsets as
+                        // plain adds (every offset stays below 256 KB)
+                        const uint64_t ad0 = desc_k_sw128(abase);
+                        const uint64_t bd0 = desc_k_sw128(qbase + h2 * HW * DK);
+                        const uint32_t d0 = tmem + (uint32_t)(slot * SLOT_COLS);
+#pragma unroll
                         for (int g = 0; g < R_GROUPS; ++g) {
-                            const uint32_t d = tmem + (uint32_t)(slot * SLOT_COLS + g * HW);
-                            bool first = true;
-                            // key limb i times query limb g - i, scale 64^g
+#pragma unroll
                             for (int i = 0; i < NLIMB; ++i) {
-                                const int iq = g - i;
+                                const int iq = g - i;   // key limb i times query limb g - i: scale 64^g
                                 if (iq < 0 || iq >= NLIMB) continue;
 #pragma unroll
-                                for (int kc = 0; kc < DK / 32; ++kc) {
-                                    mma_i8(d, desc_k_sw128(abase + i * R_A_LIMB + kc * 32),
-                                           desc_k_sw128(qbase + iq * S::Q_LIMB + h2 * HW * DK +
-                                                        kc * 32),
-                                           idesc_h, first ? 0u : 1u);
-                                    first = false;
-                                    issued = true;
-                                }
+                                for (int kc = 0; kc < DK / 32; ++kc)
+                                    mma_i8(d0 + (uint32_t)(g * HW),
+                                           ad0 + (uint64_t)((i * R_A_LIMB + kc * 32) >> 4),
+                                           bd0 + (uint64_t)((iq * S::Q_LIMB + kc * 32) >> 4),
+                                           idesc_h, (i == (g > 2 ? g - 2 : 0) && kc == 0) ? 0u : 1u);
                             }
                         }
+                        issued = true;
                         mma_commit(&ctl->acc_full[slot]);
                     }
                     __syncwarp();
@@ -923,13 +959,14 @@ size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 // Workspace of the exact selection: status words and flagged tokens, key
 // limbs and norms, candidate lists and their exact scores.
 struct DsaExactLayout {
-    size_t status, cand, cand_cnt, exact, total;
+    size_t status, limbs, cand, cand_cnt, exact, total;
 };
 
 static DsaExactLayout dsa_exact_layout(int64_t T, int64_t L) {
     DsaExactLayout d;
     size_t o = 0;
     d.status = o; o += up256(sizeof(int) * (size_t)(ST_FLAGS + T));
+    d.limbs = o; o += up256((size_t)L * NLIMB * DK);
     d.cand = o; o += up256(sizeof(int32_t) * (size_t)T * CAP_C);
     d.cand_cnt = o; o += up256(sizeof(int) * (size_t)T);
     d.exact = o; o += up256(sizeof(float) * (size_t)T * CAP_C);
@@ -980,8 +1017,16 @@ hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float
     s = check_launch("dsa_band_kernel");
     if (s != HMM_OK) return s;
 
+    // the key limbs, right before the gather that reads them
+    {
+        const int64_t n16 = L * (DK / 16);
+        const int64_t blocks = std::min<int64_t>((n16 + 255) / 256, 8 * (int64_t)device_sm_count());
+        dsa_key_limbs_kernel<<<(unsigned)blocks, 256, 0, st>>>(keys, L, wb + d.limbs);
+        s = check_launch("dsa_key_limbs_kernel");
+        if (s != HMM_OK) return s;
+    }
     RescoreArgs ra;
-    ra.q = q; ra.w = w; ra.keys = keys; ra.cand = cand; ra.cand_cnt = cand_cnt;
+    ra.q = q; ra.w = w; ra.klimbs = wb + d.limbs; ra.cand = cand; ra.cand_cnt = cand_cnt;
     ra.exact = exact; ra.status = status; ra.T = T; ra.wait_ns = wait_limit_ns();
     const int grid = std::max(1, (int)std::min<int64_t>(device_sm_count(), T));
     const ProfileMark pm = profile_begin(st);
