@@ -468,9 +468,9 @@ constexpr int R_STAGES = 3;
 constexpr int R_A_LIMB = R_M * DK;               // 16 KB: one limb of a tile
 constexpr int R_A_STAGE = NLIMB * R_A_LIMB;      // 48 KB
 constexpr int R_PROD_WARPS = 4;
-constexpr int R_THREADS = 32 * 16;               // producers 0-3, MMA 4, TMEM 5, epilogue 8-15
+constexpr int R_THREADS = 32 * 10;               // producers 0-3, MMA 4, TMEM 5, epilogue 6-9
 constexpr int R_GROUPS = 5;                      // limb scales 64^0 .. 64^4
-constexpr int R_HMAX = 32;                       // heads per MMA pass (N) at most
+constexpr int R_SLOTS = 8;                       // TMEM group slots of H columns (a ring)
 
 template <int H>
 struct RescoreSmem {
@@ -487,8 +487,8 @@ struct RescoreSmem {
 struct RescoreCtrl {
     uint64_t a_full[R_STAGES], a_empty[R_STAGES];
     uint64_t q_full[2], q_empty[2];
-    uint64_t acc_full[8];            // per half-tile slot of TMEM (MMA commit)
-    uint64_t slot_empty[8];          // per slot: drained by its epilogue warpgroup
+    uint64_t slot_full[R_SLOTS];     // group accumulator written (MMA commit per group)
+    uint64_t slot_empty[R_SLOTS];    // group accumulator read by the epilogue
     uint64_t drain;                  // MMA warp: every MMA issued has completed (abort path)
     uint32_t tmem_base;
     int abort;
@@ -522,18 +522,16 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
-// fl32(v * 2^-18) for v = D0 + 64 D1 + 64^2 D2 + 64^3 D3 + 64^4 D4 (the exact
-// dot of the limbs, |v| < 2^46), correctly rounded with full-rate int32 and
-// fp32 instructions only:
-//   t = A + 4096 (B mod 2048), A = D0 + 64 D1, B = D2 + 64 D3   (|t| < 2^28)
+// fl32(v * 2^-18) for v = A + 4096 B + 2^24 D4, A = D0 + 64 D1, B = D2 + 64
+// D3 (the exact dot of the limbs, |v| < 2^46), correctly rounded with
+// full-rate int32 and fp32 instructions only:
+//   t = A + 4096 (B mod 2048)   (|t| < 2^28)
 //   v = Q 2^23 + R,  R = t mod 2^23 in [0, 2^23),  Q = floor(t / 2^23)
 //       + floor(B / 2048) + 2 D4  (|Q| < 2^22)
 // Q 2^5 and R 2^-18 are exact floats (the 1.5 * 2^23 and 2^23 magic-number
 // conversions, scaled by exact fused multiply-adds), so their one rounded sum
 // is the rounded v * 2^-18.
-__device__ __forceinline__ float exact_dot_f32(int d0, int d1, int d2, int d3, int d4) {
-    const int A = d0 + 64 * d1;                       // |A| < 2^27
-    const int B = d2 + 64 * d3;                       // |B| < 2^27
+__device__ __forceinline__ float exact_dot_f32(int A, int B, int d4) {
     const int t = A + ((B & 2047) << 12);
     const int R = t & ((1 << 23) - 1);
     const int Q = (t >> 23) + (B >> 11) + 2 * d4;
@@ -578,15 +576,17 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 //               limbs gathered by cp.async (A operand, 3 x 16 KB, 128-byte
 //               swizzle), one tile's copies in flight while the previous
 //               tile's complete
-//   warp 4      MMA issuer: per tile and half of the heads (N = 32 heads,
-//               or all H if fewer), 9 limb pairs x 4 K-steps of tcgen05.mma
-//               kind::i8 (M = 128 candidates, K = 32) into 5 accumulators of
-//               N columns (one per scale 64^g): one TMEM slot of 5N columns,
-//               from a ring of slots, so MMAs run while both epilogue
-//               warpgroups drain earlier halves
+//   warp 4      MMA issuer: per tile, 9 limb pairs x 4 K-steps of
+//               tcgen05.mma kind::i8 (M = 128 candidates, N = H heads, K = 32),
+//               summed by the scale 64^g they carry into 5 group accumulators
+//               of H columns, each taken from a ring of 8 TMEM slots and
+//               committed on its own (the issue of one MMA costs about as much
+//               as an N = 32 MMA computes, so MMAs are kept at N = H)
 //   warp 5      TMEM allocator
-//   warps 8-15  epilogue, two warpgroups (tile parity): thread = candidate;
-//               joins the 5 groups exactly and sums the heads in order
+//   warps 6-9   epilogue: thread = candidate; reads groups 0-1 and 2-3 into
+//               registers and frees their slots at once, so that the next
+//               tile's MMAs overlap the rest; joins the groups exactly and sums
+//               the heads in order
 template <int H>
 __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const RescoreArgs a) {
     using S = RescoreSmem<H>;
@@ -598,11 +598,7 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
     RescoreCtrl* ctl = reinterpret_cast<RescoreCtrl*>(smem + S::CTRL_OFF);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     volatile int* abort = &ctl->abort;
-    constexpr int HW = H < R_HMAX ? H : R_HMAX;        // heads per half (MMA N)
-    constexpr int NH = H / HW;                         // halves per tile
-    constexpr int SLOT_COLS = R_GROUPS * HW;
-    constexpr int NSLOT = 512 / SLOT_COLS < 8 ? 512 / SLOT_COLS : 8;   // 3 (HW 32), 6 (HW 16)
-    constexpr uint32_t TMEM_COLS = 512;
+    constexpr uint32_t TMEM_COLS = R_SLOTS * H < 32 ? 32 : R_SLOTS * H;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < R_STAGES; ++s) {
@@ -611,10 +607,10 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->q_full[b], 32 * R_PROD_WARPS);
-            mbar_init(&ctl->q_empty[b], 1 + 8);   // the MMAs' commit + the 8 epilogue warps
+            mbar_init(&ctl->q_empty[b], 1 + 4);   // the MMAs' commit + the 4 epilogue warps
         }
-        for (int s = 0; s < NSLOT; ++s) {
-            mbar_init(&ctl->acc_full[s], 1);
+        for (int s = 0; s < R_SLOTS; ++s) {
+            mbar_init(&ctl->slot_full[s], 1);
             mbar_init(&ctl->slot_empty[s], 4);
         }
         mbar_init(&ctl->drain, 1);
@@ -726,38 +722,36 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                     break;
                 }
                 const uint32_t abase = smem_u32(As + s * R_A_STAGE);
-                constexpr uint32_t idesc_h = idesc_i8(R_M, HW);
-                for (int h2 = 0; h2 < NH; ++h2) {
-                    const int u = tile_seq * NH + h2;   // half-tile sequence number
-                    const int slot = u % NSLOT;
-                    if (!r_wait(&ctl->slot_empty[slot], ((u / NSLOT) & 1) ^ 1, abort, a.wait_ns)) {
+                constexpr uint32_t idesc = idesc_i8(R_M, H);
+                // descriptors from two bases: the start-address field (bits 0-13,
+                // address / 16) takes the byte offsets as plain adds (every
+                // offset stays below 256 KB)
+                const uint64_t ad0 = desc_k_sw128(abase);
+                const uint64_t bd0 = desc_k_sw128(qbase);
+#pragma unroll
+                for (int g = 0; g < R_GROUPS; ++g) {
+                    const int n_slot = R_GROUPS * tile_seq + g;
+                    const int slot = n_slot % R_SLOTS;
+                    if (!r_wait(&ctl->slot_empty[slot], ((n_slot / R_SLOTS) & 1) ^ 1, abort,
+                                a.wait_ns)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     if (lane == 0) {
-                        // descriptors from two bases: the start-address field
-                        // (bits 0-13, address / 16) takes the byte offsets as
-                        // plain adds (every offset stays below 256 KB)
-                        const uint64_t ad0 = desc_k_sw128(abase);
-                        const uint64_t bd0 = desc_k_sw128(qbase + h2 * HW * DK);
-                        const uint32_t d0 = tmem + (uint32_t)(slot * SLOT_COLS);
+                        const uint32_t d = tmem + (uint32_t)(slot * H);
 #pragma unroll
-                        for (int g = 0; g < R_GROUPS; ++g) {
+                        for (int i = 0; i < NLIMB; ++i) {
+                            const int iq = g - i;   // key limb i times query limb g - i: scale 64^g
+                            if (iq < 0 || iq >= NLIMB) continue;
 #pragma unroll
-                            for (int i = 0; i < NLIMB; ++i) {
-                                const int iq = g - i;   // key limb i times query limb g - i: scale 64^g
-                                if (iq < 0 || iq >= NLIMB) continue;
-#pragma unroll
-                                for (int kc = 0; kc < DK / 32; ++kc)
-                                    mma_i8(d0 + (uint32_t)(g * HW),
-                                           ad0 + (uint64_t)((i * R_A_LIMB + kc * 32) >> 4),
-                                           bd0 + (uint64_t)((iq * S::Q_LIMB + kc * 32) >> 4),
-                                           idesc_h, (i == (g > 2 ? g - 2 : 0) && kc == 0) ? 0u : 1u);
-                            }
+                            for (int kc = 0; kc < DK / 32; ++kc)
+                                mma_i8(d, ad0 + (uint64_t)((i * R_A_LIMB + kc * 32) >> 4),
+                                       bd0 + (uint64_t)((iq * S::Q_LIMB + kc * 32) >> 4), idesc,
+                                       (i == (g > 2 ? g - 2 : 0) && kc == 0) ? 0u : 1u);
                         }
                         issued = true;
-                        mma_commit(&ctl->acc_full[slot]);
+                        mma_commit(&ctl->slot_full[slot]);
                     }
                     __syncwarp();
                 }
@@ -779,13 +773,27 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                 mbar_wait_drain(&ctl->drain, 0);
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 6) {
         // ----------------------------------------------------------- epilogue
-        const int wg = (warp - 8) >> 2;  // tiles with tile_seq % 2 == wg
         const int sub = warp & 3;
         const int r = sub * 32 + lane;   // candidate row of the tile (TMEM lane)
+        const uint32_t lane_base = tmem + ((uint32_t)(sub * 32) << 16);
         int tile_seq = 0, tok_seq = 0;
         bool ok = true;
+        // waits for group g of this tile; returns its TMEM address
+        auto group = [&](int g, uint32_t* col) {
+            const int n_slot = R_GROUPS * tile_seq + g;
+            const bool got = r_wait(&ctl->slot_full[n_slot % R_SLOTS], (n_slot / R_SLOTS) & 1,
+                                    abort, a.wait_ns);
+            tc_fence_after();
+            *col = lane_base + (uint32_t)((n_slot % R_SLOTS) * H);
+            return got;
+        };
+        auto release = [&](int g) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->slot_empty[(R_GROUPS * tile_seq + g) % R_SLOTS]);
+        };
         for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
             const int n = a.cand_cnt[t];
             if (n <= 0) continue;
@@ -794,39 +802,48 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const float* wq = Ws + qb * H;
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
-                if ((tile_seq & 1) != wg) continue;
-                float total = 0.0f;
-                for (int h2 = 0; h2 < NH && ok; ++h2) {
-                    const int u = tile_seq * NH + h2;
-                    const int slot = u % NSLOT;
-                    if (!r_wait(&ctl->acc_full[slot], (u / NSLOT) & 1, abort, a.wait_ns)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t cbase = tmem + ((uint32_t)(sub * 32) << 16) +
-                                           (uint32_t)(slot * SLOT_COLS);
-#pragma unroll 1
-                    for (int h0 = 0; h0 < HW; h0 += 16) {
-                        uint32_t d[R_GROUPS][16];
+                // A_h = D0 + 64 D1 and B_h = D2 + 64 D3 (|A|, |B| < 2^27), then
+                // the slots of groups 0-3 go back to the MMAs
+                int A[H], B[H];
+                uint32_t c0, c1;
+                if (!group(0, &c0) || !group(1, &c1)) { ok = false; break; }
 #pragma unroll
-                        for (int g = 0; g < R_GROUPS; ++g)
-                            tmem_ld_x16(cbase + (uint32_t)(g * HW + h0), d[g]);
-                        tmem_wait_ld();
-                        const float* wh = wq + h2 * HW + h0;
+                for (int h0 = 0; h0 < H; h0 += 16) {
+                    uint32_t d0[16], d1[16];
+                    tmem_ld_x16(c0 + (uint32_t)h0, d0);
+                    tmem_ld_x16(c1 + (uint32_t)h0, d1);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int h = 0; h < 16; ++h) {
-                            const float x = fmaxf(exact_dot_f32((int)d[0][h], (int)d[1][h],
-                                                                (int)d[2][h], (int)d[3][h],
-                                                                (int)d[4][h]), 0.0f);
-                            total = __fadd_rn(total, __fmul_rn(wh[h], x));
-                        }
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&ctl->slot_empty[slot]);
+                    for (int h = 0; h < 16; ++h) A[h0 + h] = (int)d0[h] + 64 * (int)d1[h];
                 }
-                if (!ok) break;
+                release(0);
+                release(1);
+                if (!group(2, &c0) || !group(3, &c1)) { ok = false; break; }
+#pragma unroll
+                for (int h0 = 0; h0 < H; h0 += 16) {
+                    uint32_t d2[16], d3[16];
+                    tmem_ld_x16(c0 + (uint32_t)h0, d2);
+                    tmem_ld_x16(c1 + (uint32_t)h0, d3);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < 16; ++h) B[h0 + h] = (int)d2[h] + 64 * (int)d3[h];
+                }
+                release(2);
+                release(3);
+                if (!group(4, &c0)) { ok = false; break; }
+                float total = 0.0f;
+#pragma unroll
+                for (int h0 = 0; h0 < H; h0 += 16) {
+                    uint32_t d4[16];
+                    tmem_ld_x16(c0 + (uint32_t)h0, d4);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < 16; ++h) {
+                        const float x = fmaxf(exact_dot_f32(A[h0 + h], B[h0 + h], (int)d4[h]), 0.0f);
+                        total = __fadd_rn(total, __fmul_rn(wq[h0 + h], x));
+                    }
+                }
+                release(4);
                 const int row = ti * R_M + r;
                 if (row < n) a.exact[t * CAP_C + row] = total;
             }
