@@ -728,30 +728,42 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                 // offset stays below 256 KB)
                 const uint64_t ad0 = desc_k_sw128(abase);
                 const uint64_t bd0 = desc_k_sw128(qbase);
-#pragma unroll
-                for (int g = 0; g < R_GROUPS; ++g) {
+                // Issue order: key limb i, then K-step, then the three groups
+                // g = i .. i + 2 it feeds (query limb g - i), so that
+                // consecutive MMAs accumulate into different groups and never
+                // wait on each other.  Group g's slot is claimed before its first
+                // MMA (g0-g2 at i = 0, g3 at i = 1, g4 at i = 2) and committed
+                // after its last (g0 after i = 0, g1 after i = 1, the rest after
+                // i = 2).
+                auto claim = [&](int g) {
                     const int n_slot = R_GROUPS * tile_seq + g;
-                    const int slot = n_slot % R_SLOTS;
-                    if (!r_wait(&ctl->slot_empty[slot], ((n_slot / R_SLOTS) & 1) ^ 1, abort,
-                                a.wait_ns)) {
-                        ok = false;
-                        break;
-                    }
+                    return r_wait(&ctl->slot_empty[n_slot % R_SLOTS], ((n_slot / R_SLOTS) & 1) ^ 1,
+                                  abort, a.wait_ns);
+                };
+                auto slot_of = [&](int g) { return (R_GROUPS * tile_seq + g) % R_SLOTS; };
+#pragma unroll
+                for (int i = 0; i < NLIMB; ++i) {
+                    if (i == 0) ok = claim(0) && claim(1) && claim(2);
+                    else ok = claim(i + 2);
+                    if (!ok) break;
                     tc_fence_after();
                     if (lane == 0) {
-                        const uint32_t d = tmem + (uint32_t)(slot * H);
 #pragma unroll
-                        for (int i = 0; i < NLIMB; ++i) {
-                            const int iq = g - i;   // key limb i times query limb g - i: scale 64^g
-                            if (iq < 0 || iq >= NLIMB) continue;
+                        for (int kc = 0; kc < DK / 32; ++kc)
 #pragma unroll
-                            for (int kc = 0; kc < DK / 32; ++kc)
-                                mma_i8(d, ad0 + (uint64_t)((i * R_A_LIMB + kc * 32) >> 4),
-                                       bd0 + (uint64_t)((iq * S::Q_LIMB + kc * 32) >> 4), idesc,
-                                       (i == (g > 2 ? g - 2 : 0) && kc == 0) ? 0u : 1u);
-                        }
+                            for (int g = i; g < i + NLIMB; ++g)
+                                mma_i8(tmem + (uint32_t)(slot_of(g) * H),
+                                       ad0 + (uint64_t)((i * R_A_LIMB + kc * 32) >> 4),
+                                       bd0 + (uint64_t)(((g - i) * S::Q_LIMB + kc * 32) >> 4),
+                                       idesc, (i == (g > 2 ? g - 2 : 0) && kc == 0) ? 0u : 1u);
                         issued = true;
-                        mma_commit(&ctl->slot_full[slot]);
+                        if (i < NLIMB - 1) {
+                            mma_commit(&ctl->slot_full[slot_of(i)]);
+                        } else {
+#pragma unroll
+                            for (int g = NLIMB - 1; g < R_GROUPS; ++g)
+                                mma_commit(&ctl->slot_full[slot_of(g)]);
+                        }
                     }
                     __syncwarp();
                 }
