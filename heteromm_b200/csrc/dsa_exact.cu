@@ -468,7 +468,7 @@ constexpr int R_STAGES = 3;
 constexpr int R_A_LIMB = R_M * DK;               // 16 KB: one limb of a tile
 constexpr int R_A_STAGE = NLIMB * R_A_LIMB;      // 48 KB
 constexpr int R_PROD_WARPS = 4;
-constexpr int R_THREADS = 32 * 10;               // producers 0-3, MMA 4, TMEM 5, epilogue 6-9
+constexpr int R_THREADS = 32 * 14;               // producers 0-3, MMA 4, TMEM 5, epilogue 6-13
 constexpr int R_GROUPS = 5;                      // limb scales 64^0 .. 64^4
 constexpr int R_SLOTS = 8;                       // TMEM group slots of H columns (a ring)
 
@@ -481,14 +481,16 @@ struct RescoreSmem {
     static constexpr size_t W_OFF = Q_OFF + 2 * (size_t)Q_BUF;
     static constexpr size_t LUT_OFF = W_OFF + 2 * H * sizeof(float);   // 256 limb entries
     static constexpr size_t CTRL_OFF = LUT_OFF + 256 * sizeof(uint32_t);
-    static constexpr size_t BYTES = CTRL_OFF + 256 + 1024;   // + barriers, + alignment slack
+    static constexpr size_t BYTES = CTRL_OFF + 1536 + 1024;   // + barriers, + alignment slack
 };
 
 struct RescoreCtrl {
     uint64_t a_full[R_STAGES], a_empty[R_STAGES];
     uint64_t q_full[2], q_empty[2];
     uint64_t slot_full[R_SLOTS];     // group accumulator written (MMA commit per group)
-    uint64_t slot_empty[R_SLOTS];    // group accumulator read by the epilogue
+    uint64_t slot_empty[R_SLOTS];    // group accumulator read by both epilogue warpgroups
+    uint64_t hand_full[2], hand_empty[2];   // partial head sums, first -> second warpgroup
+    float hand[2][R_M];
     uint64_t drain;                  // MMA warp: every MMA issued has completed (abort path)
     uint32_t tmem_base;
     int abort;
@@ -583,10 +585,10 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 //               committed on its own (the issue of one MMA costs about as much
 //               as an N = 32 MMA computes, so MMAs are kept at N = H)
 //   warp 5      TMEM allocator
-//   warps 6-9   epilogue: thread = candidate; reads groups 0-1 and 2-3 into
-//               registers and frees their slots at once, so that the next
-//               tile's MMAs overlap the rest; joins the groups exactly and sums
-//               the heads in order
+//   warps 6-13  epilogue, two warpgroups over the heads of the same tile:
+//               thread = candidate; each joins the 5 groups of its heads exactly;
+//               the first sums heads 0 .. H/2-1 in order and hands the partial
+//               sum (shared memory) to the second, which adds its heads in order
 template <int H>
 __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const RescoreArgs a) {
     using S = RescoreSmem<H>;
@@ -607,11 +609,13 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->q_full[b], 32 * R_PROD_WARPS);
-            mbar_init(&ctl->q_empty[b], 1 + 4);   // the MMAs' commit + the 4 epilogue warps
+            mbar_init(&ctl->q_empty[b], 1 + 8);   // the MMAs' commit + the 8 epilogue warps
+            mbar_init(&ctl->hand_full[b], 4);
+            mbar_init(&ctl->hand_empty[b], 4);
         }
         for (int s = 0; s < R_SLOTS; ++s) {
             mbar_init(&ctl->slot_full[s], 1);
-            mbar_init(&ctl->slot_empty[s], 4);
+            mbar_init(&ctl->slot_empty[s], 8);
         }
         mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
@@ -787,25 +791,15 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
         }
     } else if (warp >= 6) {
         // ----------------------------------------------------------- epilogue
+        constexpr int HA = H >= 32 ? H / 2 : H;   // heads of the first warpgroup
+        constexpr int HC = HA;                    // heads of either warpgroup, at most
+        const int wg = (warp - 6) >> 2;           // 0: heads [0, HA), 1: heads [HA, H)
+        const int h_lo = wg == 0 ? 0 : HA, h_hi = wg == 0 ? HA : H;
         const int sub = warp & 3;
         const int r = sub * 32 + lane;   // candidate row of the tile (TMEM lane)
         const uint32_t lane_base = tmem + ((uint32_t)(sub * 32) << 16);
         int tile_seq = 0, tok_seq = 0;
         bool ok = true;
-        // waits for group g of this tile; returns its TMEM address
-        auto group = [&](int g, uint32_t* col) {
-            const int n_slot = R_GROUPS * tile_seq + g;
-            const bool got = r_wait(&ctl->slot_full[n_slot % R_SLOTS], (n_slot / R_SLOTS) & 1,
-                                    abort, a.wait_ns);
-            tc_fence_after();
-            *col = lane_base + (uint32_t)((n_slot % R_SLOTS) * H);
-            return got;
-        };
-        auto release = [&](int g) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->slot_empty[(R_GROUPS * tile_seq + g) % R_SLOTS]);
-        };
         for (int64_t t = blockIdx.x; ok && t < a.T; t += G) {
             const int n = a.cand_cnt[t];
             if (n <= 0) continue;
@@ -814,50 +808,71 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const float* wq = Ws + qb * H;
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
-                // A_h = D0 + 64 D1 and B_h = D2 + 64 D3 (|A|, |B| < 2^27), then
-                // the slots of groups 0-3 go back to the MMAs
-                int A[H], B[H];
-                uint32_t c0, c1;
-                if (!group(0, &c0) || !group(1, &c1)) { ok = false; break; }
+                uint32_t col[R_GROUPS];
 #pragma unroll
-                for (int h0 = 0; h0 < H; h0 += 16) {
-                    uint32_t d0[16], d1[16];
-                    tmem_ld_x16(c0 + (uint32_t)h0, d0);
-                    tmem_ld_x16(c1 + (uint32_t)h0, d1);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int h = 0; h < 16; ++h) A[h0 + h] = (int)d0[h] + 64 * (int)d1[h];
+                for (int g = 0; g < R_GROUPS; ++g) {
+                    const int n_slot = R_GROUPS * tile_seq + g;
+                    if (!r_wait(&ctl->slot_full[n_slot % R_SLOTS], (n_slot / R_SLOTS) & 1, abort,
+                                a.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    col[g] = lane_base + (uint32_t)((n_slot % R_SLOTS) * H);
                 }
-                release(0);
-                release(1);
-                if (!group(2, &c0) || !group(3, &c1)) { ok = false; break; }
+                if (!ok) break;
+                tc_fence_after();
+                // p_h = fl(w_h * x_h) for this warpgroup's heads, x_h from the 5 groups
+                float p[HC];
 #pragma unroll
-                for (int h0 = 0; h0 < H; h0 += 16) {
-                    uint32_t d2[16], d3[16];
-                    tmem_ld_x16(c0 + (uint32_t)h0, d2);
-                    tmem_ld_x16(c1 + (uint32_t)h0, d3);
-                    tmem_wait_ld();
+                for (int c0 = 0; c0 < HC; c0 += 16) {
+                    if (c0 >= h_hi - h_lo) break;   // (H = 16: the second warpgroup has no heads)
+                    const int h0 = h_lo + c0;
+                    uint32_t d[R_GROUPS][16];
 #pragma unroll
-                    for (int h = 0; h < 16; ++h) B[h0 + h] = (int)d2[h] + 64 * (int)d3[h];
-                }
-                release(2);
-                release(3);
-                if (!group(4, &c0)) { ok = false; break; }
-                float total = 0.0f;
-#pragma unroll
-                for (int h0 = 0; h0 < H; h0 += 16) {
-                    uint32_t d4[16];
-                    tmem_ld_x16(c0 + (uint32_t)h0, d4);
+                    for (int g = 0; g < R_GROUPS; ++g) tmem_ld_x16(col[g] + (uint32_t)h0, d[g]);
                     tmem_wait_ld();
 #pragma unroll
                     for (int h = 0; h < 16; ++h) {
-                        const float x = fmaxf(exact_dot_f32(A[h0 + h], B[h0 + h], (int)d4[h]), 0.0f);
-                        total = __fadd_rn(total, __fmul_rn(wq[h0 + h], x));
+                        const int A = (int)d[0][h] + 64 * (int)d[1][h];   // |A| < 2^27
+                        const int B = (int)d[2][h] + 64 * (int)d[3][h];   // |B| < 2^27
+                        const float x = fmaxf(exact_dot_f32(A, B, (int)d[4][h]), 0.0f);
+                        p[c0 + h] = __fmul_rn(wq[h0 + h], x);
                     }
                 }
-                release(4);
-                const int row = ti * R_M + r;
-                if (row < n) a.exact[t * CAP_C + row] = total;
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+#pragma unroll
+                    for (int g = 0; g < R_GROUPS; ++g)
+                        mbar_arrive(&ctl->slot_empty[(R_GROUPS * tile_seq + g) % R_SLOTS]);
+                // the head sum, in head order across the two warpgroups
+                const int hb = tile_seq & 1;
+                float total = 0.0f;
+                if (wg == 1) {
+                    if (!r_wait(&ctl->hand_full[hb], (tile_seq >> 1) & 1, abort, a.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    total = ctl->hand[hb][r];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ctl->hand_empty[hb]);
+                }
+#pragma unroll
+                for (int h = 0; h < HC; ++h)
+                    if (h < h_hi - h_lo) total = __fadd_rn(total, p[h]);
+                if (wg == 0) {
+                    if (!r_wait(&ctl->hand_empty[hb], ((tile_seq >> 1) & 1) ^ 1, abort,
+                                a.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    ctl->hand[hb][r] = total;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ctl->hand_full[hb]);
+                } else {
+                    const int row = ti * R_M + r;
+                    if (row < n) a.exact[t * CAP_C + row] = total;
+                }
             }
             if (!ok) break;
             __syncwarp();
