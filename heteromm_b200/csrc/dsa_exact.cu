@@ -805,7 +805,10 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             if (n <= 0) continue;
             const int qb = tok_seq & 1;
             ++tok_seq;
-            const float* wq = Ws + qb * H;
+            // this warpgroup's head weights, in registers for the whole token
+            float wr[HC];
+#pragma unroll
+            for (int h = 0; h < HC; ++h) wr[h] = h < h_hi - h_lo ? Ws[qb * H + h_lo + h] : 0.0f;
             const int tiles = (n + R_M - 1) / R_M;
             for (int ti = 0; ti < tiles; ++ti, ++tile_seq) {
                 uint32_t col[R_GROUPS];
@@ -822,21 +825,25 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                 if (!ok) break;
                 tc_fence_after();
                 // p_h = fl(w_h * x_h) for this warpgroup's heads, x_h from the 5 groups
+                // p_h = fl(w_h * x_h) for this warpgroup's heads, 8 heads per TMEM read;
+                // the first warpgroup adds them to its in-order sum at once
                 float p[HC];
+                float total = 0.0f;
 #pragma unroll
-                for (int c0 = 0; c0 < HC; c0 += 16) {
+                for (int c0 = 0; c0 < HC; c0 += 8) {
                     if (c0 >= h_hi - h_lo) break;   // (H = 16: the second warpgroup has no heads)
                     const int h0 = h_lo + c0;
-                    uint32_t d[R_GROUPS][16];
+                    uint32_t d[R_GROUPS][8];
 #pragma unroll
-                    for (int g = 0; g < R_GROUPS; ++g) tmem_ld_x16(col[g] + (uint32_t)h0, d[g]);
+                    for (int g = 0; g < R_GROUPS; ++g) tmem_ld_x8(col[g] + (uint32_t)h0, d[g]);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int h = 0; h < 16; ++h) {
+                    for (int h = 0; h < 8; ++h) {
                         const int A = (int)d[0][h] + 64 * (int)d[1][h];   // |A| < 2^27
                         const int B = (int)d[2][h] + 64 * (int)d[3][h];   // |B| < 2^27
                         const float x = fmaxf(exact_dot_f32(A, B, (int)d[4][h]), 0.0f);
-                        p[c0 + h] = __fmul_rn(wq[h0 + h], x);
+                        p[c0 + h] = __fmul_rn(wr[c0 + h], x);
+                        if (wg == 0) total = __fadd_rn(total, p[c0 + h]);
                     }
                 }
                 tc_fence_before();
@@ -847,7 +854,6 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                         mbar_arrive(&ctl->slot_empty[(R_GROUPS * tile_seq + g) % R_SLOTS]);
                 // the head sum, in head order across the two warpgroups
                 const int hb = tile_seq & 1;
-                float total = 0.0f;
                 if (wg == 1) {
                     if (!r_wait(&ctl->hand_full[hb], (tile_seq >> 1) & 1, abort, a.wait_ns)) {
                         ok = false;
@@ -857,9 +863,10 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&ctl->hand_empty[hb]);
                 }
+                if (wg == 1)
 #pragma unroll
-                for (int h = 0; h < HC; ++h)
-                    if (h < h_hi - h_lo) total = __fadd_rn(total, p[h]);
+                    for (int h = 0; h < HC; ++h)
+                        if (h < h_hi - h_lo) total = __fadd_rn(total, p[h]);
                 if (wg == 0) {
                     if (!r_wait(&ctl->hand_empty[hb], ((tile_seq >> 1) & 1) ^ 1, abort,
                                 a.wait_ns)) {
