@@ -804,8 +804,13 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
             const int n = a.cand_cnt[t];
             if (n <= 0) continue;
             const int qb = tok_seq & 1;
+            // this warpgroup's head weights, in registers for the whole token,
+            // once the producers have written them
+            if (!r_wait(&ctl->q_full[qb], (tok_seq >> 1) & 1, abort, a.wait_ns)) {
+                ok = false;
+                break;
+            }
             ++tok_seq;
-            // this warpgroup's head weights, in registers for the whole token
             float wr[HC];
 #pragma unroll
             for (int h = 0; h < HC; ++h) wr[h] = h < h_hi - h_lo ? Ws[qb * H + h_lo + h] : 0.0f;
