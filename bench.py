@@ -344,6 +344,7 @@ def flat_parity(out_i, out_s, world, rank, dev, n_check: int = 16):
     import numpy as np
 
     from oracle import oracle as O
+    O.set_threads(os.cpu_count() or 1)   # rank 0 alone runs it while the others wait
     pick = np.arange(0, N_QUERIES, N_QUERIES // n_check)
     qh = gen_queries(dev).view(torch.int16).cpu().numpy().view(np.uint16)[pick]
     piece = 8 * CHUNK
@@ -749,34 +750,37 @@ def run_paged(args, rank, world, local):
                      "kernel_launches_per_step": k_n / args.steps, "peak_kind": f"{pk_kind} copy bandwidth"},
         "clocks": clk.summary(),
     }
+    # parity and CPU baseline: the reference's own decode of 8 of this rank's
+    # sequences (blocks exact, outputs within the attention tolerance); timed
+    # as the CPU baseline on one GPU
+    from oracle import oracle as O
+    import numpy as np
+    n_s = 8
+    tb = table.long()
+    t_total = 0.0
+    blocks_equal, out_close = True, True
+    for s_i in range(n_s):
+        keys = kp[tb[s_i]].float().reshape(P_LEN, P_DIM).cpu().numpy()
+        vals = vp[tb[s_i]].float().reshape(P_LEN, P_DIM).cpu().numpy()
+        qq = q[s_i].float().cpu().numpy()
+        t = time.perf_counter()
+        rb, ro = O.ref_paged_decode_f32(keys, vals, qq, P_BLOCK, P_TOP)
+        t_total += time.perf_counter() - t
+        # the last end-to-end step's results for this sequence
+        blocks_equal &= bool(np.array_equal(ob[s_i].numpy(), rb))
+        out_close &= bool(np.allclose(oo[s_i].numpy(), ro, rtol=2e-5, atol=2e-6))
+    res["parity"] = {"checked_sequences": n_s, "blocks_equal": blocks_equal,
+                     "outputs_within_tolerance": out_close, "equal": blocks_equal and out_close,
+                     "against": "the reference's own PagedKVIndexBuilder + "
+                                "InnerProductCompute + TopKRetrieval + BlockSparseAttention "
+                                "(blocks exact, outputs rtol 2e-5 atol 2e-6)"}
     if world == 1 and not args.no_cpu_baseline:
-        from oracle import oracle as O
-        import numpy as np
-        n_s = 8
-        tb = table.long()
-        t_total = 0.0
-        blocks_equal, out_close = True, True
-        for s_i in range(n_s):
-            keys = kp[tb[s_i]].float().reshape(P_LEN, P_DIM).cpu().numpy()
-            vals = vp[tb[s_i]].float().reshape(P_LEN, P_DIM).cpu().numpy()
-            qq = q[s_i].float().cpu().numpy()
-            t = time.perf_counter()
-            rb, ro = O.ref_paged_decode_f32(keys, vals, qq, P_BLOCK, P_TOP)
-            t_total += time.perf_counter() - t
-            # the last end-to-end step's results for this sequence
-            blocks_equal &= bool(np.array_equal(ob[s_i].numpy(), rb))
-            out_close &= bool(np.allclose(oo[s_i].numpy(), ro, rtol=2e-5, atol=2e-6))
-        res["parity"] = {"checked_sequences": n_s, "blocks_equal": blocks_equal,
-                         "outputs_within_tolerance": out_close, "equal": blocks_equal and out_close,
-                         "against": "the reference's own PagedKVIndexBuilder + "
-                                    "InnerProductCompute + TopKRetrieval + BlockSparseAttention "
-                                    "(blocks exact, outputs rtol 2e-5 atol 2e-6)"}
         res["cpu_baseline"] = {"value": n_s / t_total, "unit": "queries/s", "cores": 1,
                                "kind": "reference",
-                               "sample": f"{n_s} sequences: the reference's PagedKVIndexBuilder "
-                                         f"+ InnerProductCompute + TopKRetrieval + "
-                                         f"BlockSparseAttention per sequence (summary build "
-                                         f"included), {t_total:.2f} s"}
+                               "sample": f"{n_s} sequences: the reference's "
+                                         f"PagedKVIndexBuilder + InnerProductCompute + "
+                                         f"TopKRetrieval + BlockSparseAttention per sequence "
+                                         f"(summary build included), {t_total:.2f} s"}
     return res
 
 
@@ -1123,6 +1127,11 @@ def traffic_per_launch(kernel: str, units: int):
 
 def main():
     global N_ROWS, WORKLOAD
+    # stdout carries the JSON line alone: anything the libraries print (NCCL's
+    # version banner, for one) goes to stderr
+    json_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -1193,7 +1202,7 @@ def main():
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()
     if rank == 0 and res is not None:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=json_out, flush=True)
 
 
 if __name__ == "__main__":

@@ -10,8 +10,15 @@
 #include "hmm_oracle.h"
 
 #include <math.h>
+#include <omp.h>
 #include <stdlib.h>
 #include <string.h>
+
+/* Threads of the oracle's OpenMP loops (a launcher may have pinned the
+ * process to one thread through OMP_NUM_THREADS). */
+void orc_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
 
 /* ------------------------------------------------------------------ keys */
 

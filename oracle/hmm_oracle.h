@@ -30,6 +30,8 @@
 extern "C" {
 #endif
 
+void orc_set_threads(int n);
+
 /* Orderable 32-bit key of a float: larger key = better score.  NaN -> 0,
  * -0.0 -> key of +0.0. */
 uint32_t orc_f32_key(float f);

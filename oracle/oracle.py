@@ -160,6 +160,11 @@ def ip_topk_f32(mem, qry, k, thr=None, want_scores=False):
     return idx, bm, sc
 
 
+def set_threads(n: int) -> None:
+    """OpenMP threads of the oracle's parallel loops."""
+    lib().orc_set_threads(int(n))
+
+
 def ip_topk_bf16(mem, qry, k, row_offset=0):
     mem = _c(mem, np.uint16); qry = _c(np.atleast_2d(qry), np.uint16)
     n, d = mem.shape
