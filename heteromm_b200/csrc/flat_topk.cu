@@ -61,11 +61,13 @@ struct Plan {
     int n_qgroups;
 };
 
+// One CTA per SM (the kernel's shared memory allows no more): the CTAs of
+// all query groups together form one wave.
 Plan plan_fused(int64_t n, int64_t nq) {
     Plan p;
     p.n_qgroups = (int)((nq + QG - 1) / QG);
     const int64_t tiles = std::max<int64_t>(1, (n + RT - 1) / RT);
-    const int64_t target = std::max<int64_t>(1, (int64_t)device_sm_count() * 2 / p.n_qgroups);
+    const int64_t target = std::max<int64_t>(1, (int64_t)device_sm_count() / p.n_qgroups);
     const int64_t tiles_per_part = (tiles + target - 1) / target;
     p.rows_per_part = tiles_per_part * RT;
     p.n_parts = (int)((tiles + tiles_per_part - 1) / tiles_per_part);
@@ -82,26 +84,35 @@ __device__ __forceinline__ void load_rows(float* srow, const typename In::T* __r
     const int wp = (w + 3) & ~3;
     if (vec_ok && (w % In::VEC) == 0) {
         const int per_row = w / In::VEC;
-        for (int idx = threadIdx.x; idx < RT * per_row; idx += NT) {
+        // every load of this thread issued before any store: one memory round
+        // trip per chunk instead of one per vector
+        constexpr int MAXV = RT * (KC / In::VEC) / NT;
+        uint4 v[MAXV];
+#pragma unroll
+        for (int u = 0; u < MAXV; ++u) {
+            const int idx = threadIdx.x + u * NT;
             const int r = idx / per_row, j = (idx % per_row) * In::VEC;
             const int64_t row = t0 + r;
+            v[u] = (idx < RT * per_row && row < r_end)
+                       ? __ldg(reinterpret_cast<const uint4*>(mem + row * dim + c0 + j))
+                       : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < MAXV; ++u) {
+            const int idx = threadIdx.x + u * NT;
+            if (idx >= RT * per_row) break;
+            const int r = idx / per_row, j = (idx % per_row) * In::VEC;
             float* dst = srow + r * SROW + j;
-            if (row < r_end) {
-                const typename In::T* src = mem + row * dim + c0 + j;
-                if constexpr (In::VEC == 4) {
-                    *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
-                } else {
-                    const uint4 v = *reinterpret_cast<const uint4*>(src);
-                    float4 lo, hi;
-                    lo.x = __uint_as_float(v.x << 16); lo.y = __uint_as_float(v.x & 0xffff0000u);
-                    lo.z = __uint_as_float(v.y << 16); lo.w = __uint_as_float(v.y & 0xffff0000u);
-                    hi.x = __uint_as_float(v.z << 16); hi.y = __uint_as_float(v.z & 0xffff0000u);
-                    hi.z = __uint_as_float(v.w << 16); hi.w = __uint_as_float(v.w & 0xffff0000u);
-                    *reinterpret_cast<float4*>(dst) = lo;
-                    *reinterpret_cast<float4*>(dst + 4) = hi;
-                }
+            if constexpr (In::VEC == 4) {
+                *reinterpret_cast<uint4*>(dst) = v[u];
             } else {
-                for (int e = 0; e < In::VEC; ++e) dst[e] = 0.0f;
+                float4 lo, hi;
+                lo.x = __uint_as_float(v[u].x << 16); lo.y = __uint_as_float(v[u].x & 0xffff0000u);
+                lo.z = __uint_as_float(v[u].y << 16); lo.w = __uint_as_float(v[u].y & 0xffff0000u);
+                hi.x = __uint_as_float(v[u].z << 16); hi.y = __uint_as_float(v[u].z & 0xffff0000u);
+                hi.z = __uint_as_float(v[u].w << 16); hi.w = __uint_as_float(v[u].w & 0xffff0000u);
+                *reinterpret_cast<float4*>(dst) = lo;
+                *reinterpret_cast<float4*>(dst + 4) = hi;
             }
         }
     } else {
@@ -265,6 +276,36 @@ scores_topk_partition_kernel(const float* __restrict__ scores, int64_t n, int k,
         if (keys[i] >= T) dst[atomicAdd(&cnt, 1)] = keys[i];
     }
     for (int i = kk + threadIdx.x; i < k; i += 256) dst[i] = 0ull;
+}
+
+// First level of the candidate merge when the partitions left too many for
+// one CTA per query: CTA (g, q) keeps the best k of cand[q][g*span ..
+// g*span + span) (unsorted; empty slots 0) in out[q][g][0..k).
+constexpr int MERGE_GROUP = 16;        // partitions per first-level CTA
+constexpr int MERGE_ONE_CTA = 4096;    // candidates per query one merge CTA takes directly
+
+__global__ void __launch_bounds__(256)
+merge_groups_kernel(const uint64_t* __restrict__ cand, int64_t M, int64_t span, int k,
+                    uint64_t* __restrict__ out) {
+    __shared__ unsigned sm[300];
+    __shared__ int cnt;
+    const int g = blockIdx.x, q = blockIdx.y;
+    const int64_t b0 = (int64_t)g * span;
+    const int64_t m = min(span, M - b0);
+    const uint64_t* src = cand + (int64_t)q * M + b0;
+    uint64_t* dst = out + ((int64_t)q * gridDim.x + g) * k;
+    const uint64_t T = block_select_threshold(src, m, k, sm);
+    if (threadIdx.x == 0) cnt = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < m; i += 256) {
+        const uint64_t c = src[i];
+        if (c > T) dst[atomicAdd(&cnt, 1)] = c;
+    }
+    __syncthreads();
+    // keys equal to T: one real key (T > 0) or any number of empty slots (T == 0)
+    if (threadIdx.x == 0 && T != 0ull && cnt < k) dst[cnt++] = T;
+    __syncthreads();
+    for (int i = cnt + threadIdx.x; i < k; i += 256) dst[i] = 0ull;
 }
 
 // One CTA per query: best k of cand[q][0..M) -> sorted outputs.
@@ -572,14 +613,31 @@ hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const 
     const size_t msmem = sizeof(uint64_t) * next_pow2((int)k);
     hmm_status_t ms = prepare_merge_kernel<IdxT>();
     if (ms != HMM_OK) return ms;
+    int64_t M = (int64_t)p.n_parts * k;
+    const uint64_t* src = cand;
+    if (M > MERGE_ONE_CTA) {   // a first level of CTAs, so that no CTA merges them all
+        const int groups = (p.n_parts + MERGE_GROUP - 1) / MERGE_GROUP;
+        uint64_t* lvl = cand + (int64_t)nq * M;
+        merge_groups_kernel<<<dim3(groups, (unsigned)nq), 256, 0, st>>>(cand, M,
+                                                                        (int64_t)MERGE_GROUP * k,
+                                                                        (int)k, lvl);
+        ms = check_launch("merge_groups_kernel");
+        if (ms != HMM_OK) return ms;
+        src = lvl;
+        M = (int64_t)groups * k;
+    }
     merge_candidates_kernel<IdxT><<<(unsigned)nq, 256, msmem, st>>>(
-        cand, (int64_t)p.n_parts * k, (int)k, row_offset, out_idx, out_scores, nullptr);
+        src, M, (int)k, row_offset, out_idx, out_scores, nullptr);
     return check_launch("merge_candidates_kernel");
 }
 
 size_t fused_ws_bytes(int64_t n, int64_t nq, int64_t k) {
     const Plan p = plan_fused(n, nq);
-    return sizeof(uint64_t) * (size_t)nq * (size_t)p.n_parts * (size_t)k + 256;
+    size_t b = sizeof(uint64_t) * (size_t)nq * (size_t)p.n_parts * (size_t)k;
+    if ((int64_t)p.n_parts * k > MERGE_ONE_CTA)   // the first merge level's output
+        b += sizeof(uint64_t) * (size_t)nq * (size_t)((p.n_parts + MERGE_GROUP - 1) / MERGE_GROUP) *
+             (size_t)k;
+    return b + 256;
 }
 
 }  // namespace

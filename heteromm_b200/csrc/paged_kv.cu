@@ -40,6 +40,7 @@ constexpr int BSA_MIN_SPLIT_TOKENS = BSA_WARPS * 4;
 constexpr int BSA_MIN_SPLIT_PAGES = BSA_WARPS;
 constexpr int BSA_PAGES_PER_SPLIT = 8 * BSA_WARPS;   // pages a split takes when sequences are many
 constexpr int SEL_MAX_BLOCKS = 8192;    // summaries per sequence for the fused selection
+constexpr int SEL_THREADS_MAX = 1024;   // block selection: threads per sequence
 
 struct PagedCache {
     const uint16_t* pages;   // [n_pages][page_tokens][D]
@@ -740,10 +741,9 @@ __global__ void __launch_bounds__(CMB_THREADS) bsa_combine_kernel(const float* _
 // upper bound of q.k over its keys, sum_j max(q_j * min_j, q_j * max_j) in j
 // order; otherwise rows are [block][D] and the score is q . summary.
 template <bool MINMAX>
-__global__ void __launch_bounds__(256) block_select_kernel(const float* __restrict__ summ,
-                                                           int n_blocks, int D,
-                                                           const uint16_t* __restrict__ q,
-                                                           int top, int32_t* __restrict__ sel) {
+__global__ void __launch_bounds__(SEL_THREADS_MAX) block_select_kernel(
+    const float* __restrict__ summ, int n_blocks, int D, const uint16_t* __restrict__ q, int top,
+    int32_t* __restrict__ sel) {
     extern __shared__ unsigned char ssm[];
     const int s = blockIdx.x;
     const int n2 = next_pow2(n_blocks);
@@ -753,32 +753,41 @@ __global__ void __launch_bounds__(256) block_select_kernel(const float* __restri
         qf[d] = bf16_bits_to_f32(q[(int64_t)s * D + d]);
     __syncthreads();
     const float* S = summ + (int64_t)s * n_blocks * D * (MINMAX ? 2 : 1);
+    // one thread per summary row (blockDim >= n2 up to SEL_THREADS_MAX); each
+    // thread keeps 8 16-byte loads of its row (4 of each bound row) in flight
+    // ahead of the in-order sum (the reference's separate multiply and add)
+    constexpr int U = MINMAX ? 4 : 8;
     for (int b = threadIdx.x; b < n2; b += blockDim.x) {
         uint64_t key = 0ull;
-        if (MINMAX && b < n_blocks) {
-            const float4* lo = reinterpret_cast<const float4*>(S + (int64_t)b * 2 * D);
+        if (b < n_blocks) {
+            const float4* lo = reinterpret_cast<const float4*>(S + (int64_t)b * (MINMAX ? 2 : 1) * D);
             const float4* hi = lo + (D >> 2);
             float acc = 0.0f;
-            for (int d4 = 0; d4 < (D >> 2); ++d4) {
-                const float4 a = __ldg(lo + d4), z = __ldg(hi + d4);
-                const float av[4] = {a.x, a.y, a.z, a.w}, zv[4] = {z.x, z.y, z.z, z.w};
+            for (int d0 = 0; d0 < (D >> 2); d0 += U) {
+                float4 a[U], z[U];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float l = __fmul_rn(qf[4 * d4 + i], av[i]);
-                    const float h = __fmul_rn(qf[4 * d4 + i], zv[i]);
-                    acc = __fadd_rn(acc, l > h ? l : h);
+                for (int u = 0; u < U; ++u) {
+                    const bool in = d0 + u < (D >> 2);
+                    a[u] = in ? __ldg(lo + d0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (MINMAX) z[u] = in ? __ldg(hi + d0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-            }
-            key = make_cand(f32_key(acc), (uint32_t)b);
-        } else if (b < n_blocks) {
-            const float4* r = reinterpret_cast<const float4*>(S + (int64_t)b * D);
-            float acc = 0.0f;
-            for (int d4 = 0; d4 < (D >> 2); ++d4) {
-                const float4 x = __ldg(r + d4);
-                acc = __fadd_rn(acc, __fmul_rn(x.x, qf[4 * d4 + 0]));
-                acc = __fadd_rn(acc, __fmul_rn(x.y, qf[4 * d4 + 1]));
-                acc = __fadd_rn(acc, __fmul_rn(x.z, qf[4 * d4 + 2]));
-                acc = __fadd_rn(acc, __fmul_rn(x.w, qf[4 * d4 + 3]));
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (d0 + u >= (D >> 2)) break;
+                    const float av[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float qv = qf[4 * (d0 + u) + i];
+                        if (MINMAX) {
+                            const float zv[4] = {z[u].x, z[u].y, z[u].z, z[u].w};
+                            const float l = __fmul_rn(qv, av[i]);
+                            const float h = __fmul_rn(qv, zv[i]);
+                            acc = __fadd_rn(acc, l > h ? l : h);
+                        } else {
+                            acc = __fadd_rn(acc, __fmul_rn(av[i], qv));
+                        }
+                    }
+                }
             }
             key = make_cand(f32_key(acc), (uint32_t)b);
         }
@@ -791,6 +800,9 @@ __global__ void __launch_bounds__(256) block_select_kernel(const float* __restri
 }
 
 // ---------------------------------------------------------------- host
+// Threads of the block selection: one per summary row, 128 .. SEL_THREADS_MAX.
+int select_threads(int n2) { return std::max(128, std::min(SEL_THREADS_MAX, n2)); }
+
 struct BsaPlan {
     int splits, split_tokens;
     size_t smem, part_bytes;
@@ -1086,8 +1098,8 @@ extern "C" hmm_status_t hmm_block_select_minmax(const uint16_t* q, const float* 
     const size_t ssm = sizeof(uint64_t) * n2 + sizeof(float) * D;
     HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel<true>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm));
-    block_select_kernel<true><<<(unsigned)n_seq, 256, ssm, st>>>(minmax, (int)n_blocks, (int)D, q,
-                                                                 (int)top_blocks, out_blocks);
+    block_select_kernel<true><<<(unsigned)n_seq, select_threads(n2), ssm, st>>>(
+        minmax, (int)n_blocks, (int)D, q, (int)top_blocks, out_blocks);
     return check_launch("block_select_kernel");
 }
 
@@ -1200,8 +1212,8 @@ extern "C" hmm_status_t hmm_block_sparse_decode_bf16_async(
     const size_t ssm = sizeof(uint64_t) * n2 + sizeof(float) * D;
     HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel<false>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm));
-    block_select_kernel<false><<<(unsigned)n_seq, 256, ssm, st>>>(summaries, (int)n_blocks, (int)D,
-                                                                  q, (int)top_blocks, sel);
+    block_select_kernel<false><<<(unsigned)n_seq, select_threads(n2), ssm, st>>>(
+        summaries, (int)n_blocks, (int)D, q, (int)top_blocks, sel);
     s = check_launch("block_select_kernel");
     if (s != HMM_OK) return s;
     // slots past the number of blocks hold -1: treat them as absent by
