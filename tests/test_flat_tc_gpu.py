@@ -81,8 +81,10 @@ def test_tc_sharded_merge(cuda):
 def test_tc_pool_overflow_falls_back_to_exact(cuda):
     """Rows ordered so that query 0's score is the row index: every row beats
     the running top-k, so query 0's candidate pool fills up.  The call must
-    notice the dropped candidates and recompute the pass exactly (two extra
-    kernel launches on top of the tensor-core path's five)."""
+    notice the dropped candidates and recompute the pass exactly (three extra
+    kernel launches on top of the tensor-core path's five: the exact kernel
+    and the two levels of its candidate merge, 127 partitions of 65,000 rows
+    being too many for one merge CTA)."""
     from heteromm_b200 import _abi
     n, nq, k = 65000, 4, 100
     x = gen.normal_f32(81, (n, 128))
@@ -101,7 +103,7 @@ def test_tc_pool_overflow_falls_back_to_exact(cuda):
     assert np.array_equal(idx[0], np.arange(n - 1, n - 1 - k, -1))
     assert np.array_equal(idx, oidx)
     assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
-    assert launches == 7, launches
+    assert launches == 8, launches
 
 
 def test_tc_normal_call_launch_count(cuda):
