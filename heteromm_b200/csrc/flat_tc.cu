@@ -8,8 +8,8 @@
 // The kernel uses them only to decide which (row, query) pairs can matter:
 //   s~ = tensor-core score of row r for query q (fp32 accumulate in TMEM)
 //   |s~ - s| <= EPS * max_j|a_rj| * sum_j|b_qj|   (s = the reference's score)
-// A pair is rescored exactly - fp32 multiply-add in ascending j from the row
-// tile still resident in shared memory, which rounds exactly as the
+// A pair is rescored exactly - fp32 multiply-add in ascending j over the row
+// (read back from L2, where it was just streamed), which rounds exactly as the
 // reference's separate multiply and add because bf16 products are exact in
 // fp32 - only when its upper bound s~ + margin reaches the query's current
 // threshold.  Exact (score, row) composites that beat the threshold enter a
@@ -22,12 +22,12 @@
 // The threshold is seeded with the exact top-k of the first SEED_ROWS rows
 // (CUDA-core kernel of flat_topk.cu), so the first tiles already filter.
 //
-// The thresholds themselves are folded into the tensor-core accumulator: a
-// ninth K = 16 MMA per tile adds -t'_q (t'_q = the query's threshold score
-// rounded down to bf16), so the epilogue only needs a 3-input max tree over
-// each row's folded scores against one per-row margin.  The kernel's thread
-// roles are listed at the kernel.  Every mbarrier wait is bounded; a wait that
-// gives up sets a status word and the CTA drains and exits.
+// The queries are the MMA's M side and the rows its N side, so each epilogue
+// thread owns one query and compares its scores against one threshold held in
+// a register; a pair of SMs (a cluster of two CTAs) shares each tile, so each
+// SM's tensor core reads half of the row operand.  The kernel's thread roles
+// are listed at the kernel.  Every mbarrier wait is bounded; a wait that gives
+// up sets a status word and both CTAs of the pair drain and exit.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -53,22 +53,23 @@ namespace {
 
 using namespace sm100;
 
-constexpr int TC_M = 128;                      // rows per tile (MMA M)
-constexpr int TC_NMAX = 256;                   // queries per pass (MMA N)
 constexpr int TC_DIM = 128;                    // row width handled (MMA K total)
-constexpr int STAGES = 4;
-constexpr int A_BOX = TC_M * 128;              // 64 bf16 columns x 128 rows = 16 KiB
-constexpr int A_STAGE = 2 * A_BOX;             // 32 KiB per tile
-constexpr int Q_BOX = TC_NMAX * 128;           // 256 queries x 64 columns = 32 KiB
-constexpr int Q_BYTES = 2 * Q_BOX;             // 64 KiB
-constexpr int FA_BYTES = TC_M * 32;            // threshold-fold A operand: 128 rows x 16 bf16
-constexpr int FB_BYTES = TC_NMAX * 32;         // threshold-fold B operand: 256 rows x 16 bf16
-constexpr int N_EPI_WARPS = 8;                 // two epilogue warpgroups (query halves)
-constexpr int NTHREADS = 32 * (10 + N_EPI_WARPS);   // + TMA, MMA, 4 rescorers, 4 row-bound warps
+constexpr int TC_NMAX = 256;                   // queries per pass: 128 per CTA of the pair
+constexpr int PQ = 128;                        // queries per CTA (the pair's MMA M is 256)
+constexpr int PR = 128;                        // rows per CTA and tile (the pair's MMA N is 256)
+constexpr int STAGES = 5;
+constexpr int ROW_BOX = PR * 128;              // 128 rows x 64 bf16 columns = 16 KiB
+constexpr int ROW_STAGE = 2 * ROW_BOX;         // 32 KiB per CTA and tile
+constexpr int Q_BOX = PQ * 128;                // 128 queries x 64 columns = 16 KiB
+constexpr int Q_BYTES = 2 * Q_BOX;             // 32 KiB
+constexpr int N_EPI_WARPS = 8;                 // two epilogue warpgroups (row halves)
+constexpr int N_RB_WARPS = 2;                  // row-bound warps (two rows per lane)
+constexpr int NTHREADS = 32 * (8 + N_EPI_WARPS);    // + TMA, MMA, 4 rescorers, 2 row-bound warps
 constexpr int RING = 128;                       // pairs per epilogue warp awaiting rescoring
-constexpr int N_RESCORERS = 4;                  // warps 2, 3, 16 and 17
-constexpr int RPR = N_EPI_WARPS / N_RESCORERS;  // rings per rescorer
-constexpr int TMEM_COLS = 512;
+constexpr int N_RESCORERS = 4;                  // warps 2, 3, 6 and 7 (warp 3 of the first
+                                                // CTA issues MMAs instead)
+constexpr int RPR_MAX = 3;                      // rings per rescorer: 8 over 3 or 4 of them
+constexpr int TMEM_COLS = 512;                  // two accumulators of 256 fp32 columns
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
 #ifndef HMM_SEED_ROWS
 #define HMM_SEED_ROWS 8192
@@ -84,36 +85,40 @@ constexpr int KMAX_TC = 128;
 #endif
 constexpr int RAISE_STEP = HMM_RAISE_STEP;      // appends between threshold raises
 constexpr int RAISE_WINDOW = HMM_RAISE_WINDOW;  // newest pool entries a raise selects over
-constexpr int MR_RING = 8;                     // tiles of row bounds in flight (>= STAGES + 2)
+constexpr int MR_RING = 8;                      // tiles of row bounds in flight
+static_assert(MR_RING >= STAGES + 2, "a row-bound slot is rewritten only after both epilogues read it");
+static_assert(N_RB_WARPS == 2, "the epilogue reads two row-bound slots per half");
 constexpr uint64_t REFRESH_NS = 2000;          // cadence of the rescorers' shared-threshold refresh
 
 struct __align__(8) Ctrl {
-    uint64_t a_full[STAGES];        // tile landed (TMA tx)
-    uint64_t a_empty[STAGES];       // tile consumed: row-bound threads + MMA commit
-    uint64_t acc_full[2];           // accumulator written (MMA commit)
-    uint64_t acc_empty[2];          // accumulator drained by its epilogue warpgroup
-    uint64_t b_full;                // queries landed
-    uint64_t mr_full[MR_RING];      // row bounds of tile i published
+    uint64_t full[STAGES];          // this CTA's rows of tile i landed (TMA tx); in the first
+                                    // CTA also the peer's (its forwarder arrives)
+    uint64_t empty[STAGES];         // ... consumed: row-bound threads + one epilogue thread
+                                    // that has seen the tile's accumulator
+    uint64_t acc_full[2];           // accumulator written (pair MMA commit)
+    uint64_t acc_empty[2];          // first CTA only: drained by the epilogue warps of both CTAs
+    uint64_t q_full;                // this CTA's queries landed (first CTA: and the peer's)
     uint32_t tmem_base;
     int abort;
-    float l1max;                    // max over queries of sum_j |b_qj|
-    float tmax;                     // max |folded threshold| ever written to the fold operand
-    uint64_t tau[TC_NMAX];          // CTA copy of each query's threshold composite
+    int issued;                     // first CTA: tiles whose MMAs are all issued (turn counter)
+    // max|a| over the rows of (tile, half, row-bound warp) as (tile + 1) << 32 |
+    // float bits: one 8-byte store carries the value and the tile it is for
+    uint64_t mr[MR_RING][2][N_RB_WARPS];
+    uint64_t tau[TC_NMAX];          // CTA copy of each of its queries' threshold composites
     uint64_t ring[N_EPI_WARPS][RING];    // (shard row << 8) | query, epilogue -> rescorer
     int ring_head[N_EPI_WARPS];          // consumed (rescorer)
     int ring_tail[N_EPI_WARPS];          // published (epilogue warp)
     int epi_done[N_EPI_WARPS];           // the epilogue warp has published its last pair
     unsigned hist[N_RESCORERS][256];
-    float mrow[MR_RING][TC_M];      // EPS * max|a_r| per row of tile i
 };
 
-constexpr size_t TC_SMEM =
-    1024 /* alignment slack */ + Q_BYTES + STAGES * A_STAGE + FA_BYTES + FB_BYTES + sizeof(Ctrl);
+constexpr size_t TC_SMEM = 1024 /* alignment slack */ + Q_BYTES + STAGES * ROW_STAGE + sizeof(Ctrl);
+static_assert(TC_SMEM <= 227 * 1024, "shared memory per CTA");
 
 struct TcArgs {
     int64_t n_rows;
     int64_t row_begin;
-    int n_tiles;             // 128-row tiles over [row_begin, n_rows)
+    int n_tiles;             // 256-row pair tiles over [row_begin, n_rows)
     int nq;
     int k;
     int pool_cap;
@@ -142,42 +147,6 @@ __device__ __forceinline__ float max3_nan(float a, float b, float c) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// Largest bf16 value <= x (round toward -inf), as fp32.
-__device__ __forceinline__ float bf16_floor(float x) {
-    const uint32_t u = __float_as_uint(x);
-    uint32_t hi = u & 0xffff0000u;                         // truncation: toward 0
-    if ((u & 0xffffu) != 0u && (u & 0x80000000u)) hi += 0x10000u;   // negative: away from 0
-    return __uint_as_float(hi);
-}
-
-// The folded threshold t' = t_hi + t_lo <= t (the score part of threshold
-// composite T) as two bf16: t_hi = bf16_floor(t), t_lo = bf16_floor(t - t_hi)
-// (t - t_hi is exact in fp32), so t - t' < 2^-16 |t|.  Returns the packed
-// bf16x2 (-t_hi, -t_lo) for K columns 0 and 1 of the fold B operand, and
-// |t_hi| + |t_lo| in *mag (an empty threshold folds to +inf: nothing is filtered).
-__device__ __forceinline__ uint32_t neg_fold_pair(uint64_t T, float* mag) {
-    const float t = tau_score(T);
-    if (!(t > -INFINITY)) { *mag = 0.0f; return 0x7f80u; }   // (+inf, +0)
-    const float th = bf16_floor(t);
-    const float tl = bf16_floor(t - th);
-    *mag = fabsf(th) + fabsf(tl);
-    return ((__float_as_uint(th) ^ 0x80000000u) >> 16) | ((__float_as_uint(tl) ^ 0x80000000u) & 0xffff0000u);
-}
-
-// Writes query q's folded threshold into the fold B operand (row q, K
-// columns 0-1 as one 4-byte store, so a concurrent MMA sees the old or the
-// new pair, both <= the current threshold; 32-byte swizzle: 16-byte chunk c
-// of row q sits at c ^ ((q >> 2) & 1)).  The fold bound tmax is raised
-// first, so no MMA can read a fold that the epilogue's margin does not cover.
-__device__ __forceinline__ void write_fold(unsigned char* FB, Ctrl* ctl, int q, uint64_t T) {
-    float mag;
-    const uint32_t bits = neg_fold_pair(T, &mag);
-    atomicMax(reinterpret_cast<int*>(&ctl->tmax), __float_as_int(__fmul_ru(mag, 1.0f + 1.0f / 1024.0f)));
-    __threadfence_block();
-    *reinterpret_cast<uint32_t*>(FB + q * 32 + ((((q >> 2) & 1)) << 4)) = bits;
-    fence_proxy_async_smem();
-}
-
 // The reference's fp32 dot product of a memory row and a query, j
 // ascending, both read from global memory (the row was just streamed and is
 // in L2; the queries are small and stay cached).
@@ -198,23 +167,49 @@ __device__ __forceinline__ float exact_dot_rows(const uint16_t* __restrict__ row
     return s;
 }
 
-// max_j |a_rj| over row r of a tile (chunk order is irrelevant).
-__device__ __forceinline__ float row_absmax(const unsigned char* As, int r) {
-    __nv_bfloat162 m = __floats2bfloat162_rn(0.0f, 0.0f);
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t min_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// Per half: the operand of larger magnitude, with the xor of both signs; a NaN
+// operand gives NaN.  Its magnitude is max(|a|, |b|) whatever the signs.
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// max_j |a_rj| over rows r and r + 32 of a staged 128-row tile, as fp32 bits.
+// Magnitude bit patterns order as unsigned integers; NaN counts as +inf (so a
+// NaN makes the bound infinite instead of hiding the other values).
+__device__ __forceinline__ uint32_t rows_absmax_bits(const unsigned char* Rs, int r) {
+    uint32_t m[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint4* p = reinterpret_cast<const uint4*>(As + h * A_BOX + r * 128);
+    for (int rr = 0; rr < 2; ++rr) {
+        const int row = r + 32 * rr;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            uint4 a = p[c ^ (r & 7)];   // lanes of a quarter-warp hit distinct banks
-            a.x &= 0x7fff7fffu; a.y &= 0x7fff7fffu; a.z &= 0x7fff7fffu; a.w &= 0x7fff7fffu;
-            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.x));
-            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.y));
-            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.z));
-            m = __hmax2(m, *reinterpret_cast<__nv_bfloat162*>(&a.w));
+        for (int h = 0; h < 2; ++h) {
+            const uint4* p = reinterpret_cast<const uint4*>(Rs + h * ROW_BOX + row * 128);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const uint4 a = p[c ^ (row & 7)];   // a quarter-warp's lanes hit distinct banks
+                m[0] = absmax_bf16x2(m[0], a.x);
+                m[1] = absmax_bf16x2(m[1], a.y);
+                m[2] = absmax_bf16x2(m[2], a.z);
+                m[3] = absmax_bf16x2(m[3], a.w);
+            }
         }
     }
-    return fmaxf(__low2float(m), __high2float(m));
+    const uint32_t v = min_u16x2(max_u16x2(max_u16x2(m[0] & 0x7fff7fffu, m[1] & 0x7fff7fffu),
+                                           max_u16x2(m[2] & 0x7fff7fffu, m[3] & 0x7fff7fffu)),
+                                 0x7f807f80u);
+    return max(v & 0xffffu, v >> 16) << 16;
 }
 
 // Every lane polls (so each observes the phase itself); the warp proceeds
@@ -225,28 +220,26 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, ok);
 }
 
-__device__ __forceinline__ void set_abort(Ctrl* ctl, int* status) {
+// Gives up in both CTAs of the pair: the peer's waits see its flag at once.
+__device__ __forceinline__ void set_abort(Ctrl* ctl, int* status, uint32_t peer) {
     atomicExch(&ctl->abort, 1);
+    st_cluster_u32(mapa_shared(smem_u32(&ctl->abort), peer), 1u);
     atomicExch(&status[0], 1);
 }
 
-// Raises query q's CTA threshold to T (if higher) and refolds it.
-__device__ __forceinline__ void raise_tau(Ctrl* ctl, unsigned char* FB, int q, uint64_t T) {
-    const unsigned long long old =
-        atomicMax(reinterpret_cast<unsigned long long*>(&ctl->tau[q]), (unsigned long long)T);
-    if (T > old) write_fold(FB, ctl, q, T);
-}
+__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+__device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
 
 // Rescores one batch of up to 32 queued pairs exactly (lane = pair) and
 // appends the ones that beat their query's threshold to the pools; raises
 // thresholds at fill marks from the newest RAISE_WINDOW pool entries.
-__device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned char* FB, unsigned* hist,
-                                           uint64_t e, bool valid, int m, const TcArgs& a) {
+__device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned* hist, uint64_t e, bool valid,
+                                           int m, const TcArgs& a) {
     const int lane = threadIdx.x & 31;
     if (lane == 0) atomicAdd(&a.status[2], m);
     int q = 0, raise = 0;
-    if (valid) {
-        const int64_t row = (int64_t)(e >> 8);
+    const int64_t row = (int64_t)(e >> 8);
+    if (valid && row < a.n_rows && (int)(e & 255u) < a.nq) {
         q = (int)(e & 255u);
         const float s = exact_dot_rows(a.mem + row * TC_DIM, a.qry + (int64_t)q * TC_DIM);
         const uint64_t E = make_cand(f32_key(s), (uint32_t)row);
@@ -274,249 +267,355 @@ __device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned char* FB, unsigne
         if (lane == 0 && T != 0ull) {
             atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
                       (unsigned long long)T);
-            raise_tau(ctl, FB, qq, T);
+            atomicMax(reinterpret_cast<unsigned long long*>(&ctl->tau[qq]), (unsigned long long)T);
         }
         __syncwarp();
     }
     __syncwarp();
 }
 
-__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
-__device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
-
-// One persistent CTA per SM.  Roles (18 warps):
-//   warp 0      TMA producer: the 256 queries once, then 128-row x 128-col bf16
-//               tiles (two 64-column boxes, 128-byte swizzle) into a 4-stage ring
-//   warp 1      MMA issuer: per tile, 8 x tcgen05.mma (M = 128 rows, N = 256
-//               queries, K = 16) plus one K = 16 MMA that adds -t'_q (each
-//               query's threshold, folded as a bf16 rounded down) into the same
-//               TMEM accumulator (two accumulators of 256 fp32 columns)
-//   warp 2      TMEM allocator, then (with warps 3, 16, 17) exact rescoring of
-//               the pairs the epilogue publishes to per-warp rings, and the
-//               refolding of thresholds that other CTAs raised
-//   warps 4-7   row bounds: EPS * max|a_r| for each row of a landed tile; with
-//               the MMA commit they free the tile's stage
-//   warps 8-15  epilogue, two warpgroups on every tile, each over half of the
-//               256 query columns (measured faster than one warpgroup per
-//               tile): thread = row (TMEM lane); a 3-input max tree over the
-//               row's 128 folded scores s~ - t'_q against the row's margin;
-//               pairs that reach it are published to the warp's ring for the
-//               rescorer warps, so rescoring never delays the accumulator release
-__global__ void __launch_bounds__(NTHREADS, 1)
-tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
-                       const __grid_constant__ CUtensorMap tmB, const TcArgs a) {
+// One cluster of two CTAs per pair of SMs; the pair scores 256-row tiles
+// against all 256 queries with one tcgen05.mma.cta_group::2 of M = 256
+// queries (128 resident in each CTA) x N = 256 rows (128 staged in each CTA)
+// per K = 16 slice, so each SM's tensor core reads half of the row operand
+// it would read alone.  D lands in TMEM as query (lane) x row (column).
+// Roles in each CTA (16 warps, so that each SM sub-partition holds four
+// warps of up to 128 registers):
+//   warp 0      TMA producer: the CTA's 128 queries once, then its 128 rows of
+//               each tile (two 64-column boxes, 128-byte swizzle), 5 stages
+//   warps 1, 3  first CTA: MMA issuers (one lane each; even and odd tiles),
+//               8 pair MMAs per tile into one of two accumulators of 256 fp32
+//               columns, committed to both CTAs' accumulator barriers;
+//   warp 1      second CTA: forwards each landing of its queries and rows
+//               onto the first CTA's barriers
+//   warp 2      TMEM allocator (both CTAs), then a rescorer
+//   warps 4-5   row bounds: max|a| over the CTA's 128 rows of a landed tile,
+//               stored with the tile number into both CTAs (one 8-byte store
+//               each, polled by the epilogue)
+//   warps 8-15  epilogue, two warpgroups: warpgroup h reads the columns of
+//               the rows staged by CTA h; thread = query (TMEM lane), with its
+//               own threshold less its error bound in a register; a 3-input
+//               max tree per 32 columns; pairs that reach it are published to
+//               the warp's ring
+//   warps 2, 3, 6, 7  rescorers (first CTA: 2, 6, 7): exact rescoring of the rings' pairs, pools,
+//               threshold raises, and the refresh of thresholds that other
+//               clusters raised
+// A pair (row r, query q) can beat q's threshold t only if its exact score
+// s >= score(t); |s~ - s| <= EPS * max_j|a_rj| * sum_j|b_qj| <= EPS * M_h * L1_q
+// (M_h = max over the tile half's rows), so the epilogue passes every pair
+// with s~ >= score(t) - EPS * M_h * L1_q (rounded down); NaN passes.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
+tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
+                       const __grid_constant__ CUtensorMap tmQ, const TcArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned base, derived by pointer arithmetic so that the
-    // compiler keeps every access below in the shared address space
+    // compiler keeps every access below in the shared address space; both
+    // CTAs get the same offsets, which the pair MMAs rely on
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* Qs = smem;
-    unsigned char* As = Qs + Q_BYTES;
-    unsigned char* FA = As + STAGES * A_STAGE;     // 1024-aligned
-    unsigned char* FB = FA + FA_BYTES;
-    Ctrl* ctl = reinterpret_cast<Ctrl*>(FB + FB_BYTES);
+    unsigned char* Rs = Qs + Q_BYTES;
+    Ctrl* ctl = reinterpret_cast<Ctrl*>(Rs + STAGES * ROW_STAGE);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = gridDim.x;
-    const int my_tiles = (int)blockIdx.x < a.n_tiles ? (a.n_tiles - 1 - (int)blockIdx.x) / G + 1 : 0;
+    const uint32_t crank = cluster_ctarank();   // 0: issues the pair's MMAs
+    const uint32_t peer = crank ^ 1u;
+    const int cl = (int)blockIdx.x >> 1, ncl = (int)gridDim.x >> 1;
+    const int my_tiles = cl < a.n_tiles ? (a.n_tiles - 1 - cl) / ncl + 1 : 0;
+    const int q0 = (int)crank * PQ;             // this CTA's first query
     volatile int* abort = &ctl->abort;
 
     if (threadIdx.x == 0) {
+        const uint32_t landings = crank == 0 ? 2 : 1;   // own copy (+ the peer's, forwarded)
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&ctl->a_full[s], 1);
-            mbar_init(&ctl->a_empty[s], TC_M + 1);   // row-bound threads + the MMA commit
+            mbar_init(&ctl->full[s], landings);
+            mbar_init(&ctl->empty[s], 32 * N_RB_WARPS + 1);   // row-bound threads + an epilogue thread
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->acc_full[b], 1);
-            mbar_init(&ctl->acc_empty[b], N_EPI_WARPS);   // every epilogue warp
+            mbar_init(&ctl->acc_empty[b], 2 * N_EPI_WARPS);   // every epilogue warp of the pair
         }
-        mbar_init(&ctl->b_full, 1);
-        for (int e = 0; e < MR_RING; ++e) mbar_init(&ctl->mr_full[e], 4);
+        mbar_init(&ctl->q_full, landings);
         ctl->abort = 0;
+        ctl->issued = 0;
         for (int e = 0; e < N_EPI_WARPS; ++e) {
             ctl->ring_head[e] = 0;
             ctl->ring_tail[e] = 0;
             ctl->epi_done[e] = 0;
         }
-        ctl->l1max = 0.0f;
-        ctl->tmax = 0.0f;
         fence_barrier_init();
     }
-    // fold operands: A' = 1 in K column 0, B' = -t'_q in K column 0, zero elsewhere
-    for (int i = threadIdx.x; i < (FA_BYTES + FB_BYTES) / 4; i += NTHREADS)
-        reinterpret_cast<uint32_t*>(FA)[i] = 0u;
-    __syncthreads();
-    for (int r = threadIdx.x; r < TC_M; r += NTHREADS)   // (1.0, 1.0) in K columns 0-1
-        *reinterpret_cast<uint32_t*>(FA + r * 32 + (((r >> 2) & 1) << 4)) = 0x3f803f80u;
-    for (int q = threadIdx.x; q < TC_NMAX; q += NTHREADS) {
-        float l1 = 0.0f;
-        uint64_t t = ~0ull;   // padded queries: never selected (fold = -inf below)
-        if (q < a.nq) {
-            const uint16_t* p = a.qry + (int64_t)q * TC_DIM;
-            for (int j = 0; j < TC_DIM; ++j) l1 += fabsf(bf16_bits_to_f32(p[j]));
-            l1 *= 1.0f + 1.0f / 256.0f;   // covers the rounding of this sum
-            t = a.tau_global[q];
-            atomicMax(reinterpret_cast<int*>(&ctl->l1max), __float_as_int(l1));   // l1 >= 0
-        }
-        ctl->tau[q] = t;
-        float mag = 0.0f;
-        const uint32_t bits = q < a.nq ? neg_fold_pair(t, &mag) : 0xff80u;   // (-inf, +0)
-        *reinterpret_cast<uint32_t*>(FB + q * 32 + (((q >> 2) & 1) << 4)) = bits;
-        atomicMax(reinterpret_cast<int*>(&ctl->tmax), __float_as_int(__fmul_ru(mag, 1.0f + 1.0f / 1024.0f)));
-    }
-    fence_proxy_async_smem();
+    for (int q = threadIdx.x; q < TC_NMAX; q += NTHREADS)
+        ctl->tau[q] = q < a.nq ? a.tau_global[q] : ~0ull;
+    for (int e = threadIdx.x; e < MR_RING * 2 * N_RB_WARPS; e += NTHREADS)
+        (&ctl->mr[0][0][0])[e] = 0ull;   // tag 0: no tile
     if (warp == 2) {
-        tmem_alloc(&ctl->tmem_base, TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc_pair(&ctl->tmem_base, TMEM_COLS);
+        tmem_relinquish_pair();
     }
+    // both CTAs' barriers and slots initialised and TMEM allocated before any
+    // remote arrive, remote store or pair MMA
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
 
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
-            prefetch_tmap(&tmA);
-            prefetch_tmap(&tmB);
-            mbar_expect_tx(&ctl->b_full, Q_BYTES);
-            tma_load_2d(Qs, &tmB, &ctl->b_full, 0, 0);
-            tma_load_2d(Qs + Q_BOX, &tmB, &ctl->b_full, 64, 0);
+            prefetch_tmap(&tmR);
+            prefetch_tmap(&tmQ);
+            mbar_expect_tx(&ctl->q_full, Q_BYTES);
+            tma_load_2d(Qs, &tmQ, &ctl->q_full, 0, q0);
+            tma_load_2d(Qs + Q_BOX, &tmQ, &ctl->q_full, 64, q0);
         }
         int issued = 0;
         for (int i = 0; i < my_tiles; ++i) {
             const int s = i % STAGES;
-            if (!warp_wait(&ctl->a_empty[s], ((i / STAGES) & 1) ^ 1, abort, a.wait_ns)) {
-                if (lane == 0) set_abort(ctl, a.status);
+            if (!warp_wait(&ctl->empty[s], ((i / STAGES) & 1) ^ 1, abort, a.wait_ns)) {
+                if (lane == 0) set_abort(ctl, a.status, peer);
                 break;
             }
             if (lane == 0) {
-                const int y = (int)(a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M);
-                mbar_expect_tx(&ctl->a_full[s], A_STAGE);
-                tma_load_2d(As + s * A_STAGE, &tmA, &ctl->a_full[s], 0, y);
-                tma_load_2d(As + s * A_STAGE + A_BOX, &tmA, &ctl->a_full[s], 64, y);
+                const int y = (int)(a.row_begin + ((int64_t)(cl + i * ncl) * 2 + crank) * PR);
+                mbar_expect_tx(&ctl->full[s], ROW_STAGE);
+                tma_load_2d(Rs + s * ROW_STAGE, &tmR, &ctl->full[s], 0, y);
+                tma_load_2d(Rs + s * ROW_STAGE + ROW_BOX, &tmR, &ctl->full[s], 64, y);
             }
             __syncwarp();
             issued = i + 1;
         }
+        if (!*abort) {
+            // tail: the MMA commits that release the last stages arrive before
+            // the CTA exits (nothing may arrive on a CTA that has exited)
+            for (int i = max(0, issued - STAGES); i < issued; ++i)
+                if (!warp_wait(&ctl->empty[i % STAGES], (i / STAGES) & 1, abort, a.wait_ns)) {
+                    if (lane == 0) set_abort(ctl, a.status, peer);
+                    break;
+                }
+        }
         if (*abort) {
             // drain: the latest arming of each stage must land before exit
             for (int i = max(0, issued - STAGES); i < issued; ++i)
-                mbar_wait_drain(&ctl->a_full[i % STAGES], (i / STAGES) & 1);
-            mbar_wait_drain(&ctl->b_full, 0);
+                mbar_wait_drain(&ctl->full[i % STAGES], (i / STAGES) & 1);
+            mbar_wait_drain(&ctl->q_full, 0);
+            // the pair MMAs already issued commit to this CTA's barriers after
+            // they complete; their arrivals land well within this pause, before
+            // the CTA can exit
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 50000ull) __nanosleep(1000);
         }
-    } else if (warp == 1) {
-        // -------------------------------------------------------- MMA issuer
-        const uint32_t idesc = idesc_f16(TC_M, TC_NMAX, 1);
-        int last = -1;
-        bool ok = warp_wait(&ctl->b_full, 0, abort, a.wait_ns);
-        if (!ok && lane == 0) set_abort(ctl, a.status);
-        for (int i = 0; ok && i < my_tiles; ++i) {
-            const int s = i % STAGES, b = i & 1;
-            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort, a.wait_ns) ||
-                !warp_wait(&ctl->acc_empty[b], ((i >> 1) & 1) ^ 1, abort, a.wait_ns)) {
-                if (lane == 0) set_abort(ctl, a.status);
-                break;
-            }
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t a0 = smem_u32(As + s * A_STAGE), q0 = smem_u32(Qs);
-                const uint32_t d = tmem + (uint32_t)(b * TC_NMAX);
+    } else if (warp == 1 || (warp == 3 && crank == 0)) {
+        // ------------------------------------------ MMA issuers (first CTA)
+        // Two threads, lane 0 of warps 1 and 3: warp 1 issues the even tiles
+        // (accumulator 0), warp 3 the odd ones (accumulator 1).  A pair MMA
+        // holds its issuing thread for about its own execution time, so while
+        // one thread waits for its next tile's barriers and commits, the
+        // other keeps the tensor core busy.  They take turns (ctl->issued):
+        // a tile's MMAs enter the tensor core's queue whole and in tile
+        // order, so no tile waits behind half of the next one.  A commit
+        // tracks only its own thread's MMAs; the two threads share no
+        // accumulator and no stage phase.
+        if (crank == 0 && lane == 0) {
+            const int par = warp == 1 ? 0 : 1;
+            const uint32_t idesc = idesc_f16(2 * PQ, 2 * PR, 1);
+            const uint32_t qa = smem_u32(Qs);
+            const uint32_t d = tmem + (uint32_t)(par * 2 * PR);
+            const uint32_t f_loc = smem_u32(&ctl->acc_full[par]);
+            const uint32_t f_peer = mapa_shared(f_loc, 1);
+            int last = -1;
+            bool ok = mbar_wait_bounded(&ctl->q_full, 0, abort, a.wait_ns);   // both CTAs' queries
+            for (int i = par; ok && i < my_tiles; i += 2) {
+                const int s = i % STAGES;
+                // both CTAs' rows of tile i landed; both epilogues released the accumulator
+                if (!mbar_wait_bounded(&ctl->full[s], (i / STAGES) & 1, abort, a.wait_ns) ||
+                    !mbar_wait_bounded(&ctl->acc_empty[par], ((i >> 1) & 1) ^ 1, abort, a.wait_ns)) {
+                    ok = false;
+                    break;
+                }
+                // this thread's turn: the other has issued every MMA of tile i - 1
+                if (ld_volatile(&ctl->issued) != i) {
+                    const uint64_t t0 = globaltimer_ns();
+                    while (ld_volatile(&ctl->issued) != i) {
+                        if (*abort || globaltimer_ns() - t0 >= a.wait_ns) { ok = false; break; }
+                    }
+                    if (!ok) break;
+                }
+                tc_fence_after();
+                const uint32_t ra = smem_u32(Rs + s * ROW_STAGE);
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks)
-                        mma_f16(d, desc_k_sw128(a0 + h * A_BOX + ks * 32),
-                                desc_k_sw128(q0 + h * Q_BOX + ks * 32), idesc, (h | ks) != 0);
-                // fold: D[r][q] += 1 * (-t'_q)
-                mma_f16(d, desc_k_sw32(smem_u32(FA)), desc_k_sw32(smem_u32(FB)), idesc, 1u);
-                mma_commit(&ctl->acc_full[b]);
-                mma_commit(&ctl->a_empty[s]);
+                        mma_f16_pair(d, desc_k_sw128(qa + h * Q_BOX + ks * 32),
+                                     desc_k_sw128(ra + h * ROW_BOX + ks * 32), idesc,
+                                     (h | ks) != 0);
+                st_volatile(&ctl->issued, i + 1);   // the other thread's turn
+                // the accumulator of both CTAs (each epilogue then releases its
+                // CTA's stage: the MMAs that read it have completed)
+                mma_commit_pair(f_loc);
+                mma_commit_pair(f_peer);
+                last = i;
             }
-            __syncwarp();
-            last = i;
+            // tail: both CTAs' epilogues have released this thread's last
+            // accumulator (their arrivals on this CTA's barrier have landed)
+            if (ok && last >= 0)
+                ok = mbar_wait_bounded(&ctl->acc_empty[par], (last >> 1) & 1, abort, a.wait_ns);
+            if (!ok) set_abort(ctl, a.status, peer);
+            if (*abort && last >= 0)   // the MMAs issued must finish before TMEM is freed
+                mbar_wait_drain(&ctl->acc_full[par], (last >> 1) & 1);
+        } else if (crank != 0) {
+            // ------------------------- forwarder (second CTA): each landing of
+            // this CTA's queries and rows, onto the first CTA's barriers
+            bool ok = warp_wait(&ctl->q_full, 0, abort, a.wait_ns);
+            if (ok && lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl->q_full), 0));
+            for (int i = 0; ok && i < my_tiles; ++i) {
+                const int s = i % STAGES;
+                ok = warp_wait(&ctl->full[s], (i / STAGES) & 1, abort, a.wait_ns);
+                if (ok && lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl->full[s]), 0));
+            }
+            if (!ok && lane == 0) set_abort(ctl, a.status, peer);
         }
-        if (*abort && last >= 0)   // the MMAs issued must finish before TMEM is freed
-            mbar_wait_drain(&ctl->acc_full[last & 1], (last >> 1) & 1);
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < 4 + N_RB_WARPS) {
         // ---------------------------------------------------- row-bound warps
-        const int r = (warp - 4) * 32 + lane;
-        for (int i = 0; i < my_tiles; ++i) {
+        const int w4 = warp - 4;
+        const int r = w4 * 64 + lane;   // and r + 32
+        bool ok = true;
+        for (int i = 0; ok && i < my_tiles; ++i) {
             const int s = i % STAGES;
-            if (!warp_wait(&ctl->a_full[s], (i / STAGES) & 1, abort, a.wait_ns)) {
-                if (lane == 0) set_abort(ctl, a.status);
+            if (!warp_wait(&ctl->full[s], (i / STAGES) & 1, abort, a.wait_ns)) {
+                ok = false;
                 break;
             }
-            const int64_t row = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M + r;
-            const float e = row < a.n_rows ? __fmul_ru(EPS, row_absmax(As + s * A_STAGE, r)) : 0.0f;
-            mbar_arrive(&ctl->a_empty[s]);       // smem reads of this tile are done
-            ctl->mrow[i % MR_RING][r] = e;
+            const uint32_t m = rows_absmax_bits(Rs + s * ROW_STAGE, r);   // rows past the end are 0
+            mbar_arrive(&ctl->empty[s]);                                 // smem reads of this tile done
+            const uint32_t wm = __reduce_max_sync(0xffffffffu, m);      // >= 0: int order = float order
+            if (lane == 0) {
+                const uint64_t v = ((uint64_t)(uint32_t)(i + 1) << 32) | wm;
+                uint64_t* slot = &ctl->mr[i % MR_RING][crank][w4];
+                *reinterpret_cast<volatile uint64_t*>(slot) = v;
+                st_cluster_u64(mapa_shared(smem_u32(slot), peer), v);
+            }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->mr_full[i % MR_RING]);
         }
+        if (!ok && lane == 0) set_abort(ctl, a.status, peer);
     } else if (warp >= 8 && warp < 16) {
         // --------------------------------------------------------- epilogue
         const int ew = warp - 8;            // 0..7
-        const int g = ew >> 2;              // warpgroup: query columns 128g .. 128g + 127
+        const int hh = ew >> 2;             // row half: the columns of CTA hh's rows
         const int sub = warp & 3;           // TMEM lanes 32*sub .. +31
-        const int r = sub * 32 + lane;      // tile row of this thread
-        const int nchunks = min((a.nq + 31) / 32, 4 * g + 4);
+        const int q = q0 + sub * 32 + lane; // query of this thread
+        const bool qvalid = q < a.nq;
+        float l1 = 0.0f;                    // sum_j |b_qj|, rounded up
+        if (qvalid) {
+            const uint4* qp = reinterpret_cast<const uint4*>(a.qry + (int64_t)q * TC_DIM);
+#pragma unroll 4
+            for (int c = 0; c < 16; ++c) {
+                const uint4 v = __ldg(qp + c);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    l1 = __fadd_ru(__fadd_ru(l1, fabsf(bf_lo(w[t]))), fabsf(bf_hi(w[t])));
+            }
+        }
         int tail = 0;        // pairs this warp has queued in its ring (warp-uniform)
         int published = 0;   // of those, pairs whose tail the rescorers can see
         bool ring_ok = true;
         for (int i = 0; i < my_tiles; ++i) {
-            const int b = i & 1;
-            // ---- off the critical path: the tile's row bounds are published
-            if (!warp_wait(&ctl->mr_full[i % MR_RING], (i / MR_RING) & 1, abort, a.wait_ns)) {
-                if (lane == 0) set_abort(ctl, a.status);
-                break;
-            }
-            const int64_t tile_row0 = a.row_begin + (int64_t)((int)blockIdx.x + i * G) * TC_M;
-            const bool valid = tile_row0 + r < a.n_rows;
-            const float er = ctl->mrow[i % MR_RING][r];
-
-            // ---- critical path: accumulator ready -> filter -> release
+            const int b = i & 1, e = i % MR_RING;
+            // ---- accumulator ready -> the maxima of the four 32-column chunks
             if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort, a.wait_ns)) {
-                if (lane == 0) set_abort(ctl, a.status);
+                if (lane == 0) set_abort(ctl, a.status, peer);
                 break;
             }
             tc_fence_after();
-            // |s~ - t' - (s - t')| <= EPS * (max|a_r| * sum|b_q| + |t'|) for every
-            // query; a pair can beat its threshold only if s~ - t' >= -margin
-            const float margin = __fmaf_ru(er, ctl->l1max, __fmul_ru(EPS, ctl->tmax));
-            const float neg = valid ? -margin : INFINITY;   // rows past the end never pass
-            const uint32_t tbase = tmem + (uint32_t)(b * TC_NMAX) + ((uint32_t)(sub * 32) << 16);
-            // filter: one 32-column chunk per tcgen05.wait::ld (measured faster than
-            // two), kept free of the rare hit path, which would slow every chunk
-            unsigned hitmask = 0;   // warp-uniform: chunks where some pair reaches -margin
+            // the MMAs that read this CTA's rows of tile i have completed
+            if (ew == 0 && lane == 0) mbar_arrive(&ctl->empty[i % STAGES]);
+            const uint32_t tbase =
+                tmem + (uint32_t)(b * 2 * PR + hh * PR) + ((uint32_t)(sub * 32) << 16);
+            static_assert(PR / 32 == 4, "four 32-column chunks per row half");
+            float cm0 = 0.0f, cm1 = 0.0f, cm2 = 0.0f, cm3 = 0.0f;   // chunk maxima
 #pragma unroll 1
-            for (int c = 4 * g; c < nchunks; ++c) {
-                uint32_t v[32];
+            for (int c = 0; c < PR / 32; c += 2) {
+                uint32_t v[64];   // two chunks per tcgen05.wait::ld
                 tmem_ld_x32(tbase + (uint32_t)(c * 32), v);
+                tmem_ld_x32(tbase + (uint32_t)(c * 32 + 32), v + 32);
                 tmem_wait_ld();
-                float m[11];
+                float mx2[2];
 #pragma unroll
-                for (int j = 0; j < 10; ++j)
-                    m[j] = max3_nan(__uint_as_float(v[3 * j]), __uint_as_float(v[3 * j + 1]),
-                                    __uint_as_float(v[3 * j + 2]));
-                m[10] = max3_nan(__uint_as_float(v[30]), __uint_as_float(v[31]), __uint_as_float(v[31]));
-                const float m0 = max3_nan(m[0], m[1], m[2]), m1 = max3_nan(m[3], m[4], m[5]);
-                const float m2 = max3_nan(m[6], m[7], m[8]), m3 = max3_nan(m[9], m[10], m[10]);
-                const float mx = max3_nan(max3_nan(m0, m1, m2), m3, m3);
-                if (__any_sync(0xffffffffu, !(mx < neg))) hitmask |= 1u << c;   // NaN passes
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t* w = v + 32 * h;
+                    float m[11];
+#pragma unroll
+                    for (int j = 0; j < 10; ++j)
+                        m[j] = max3_nan(__uint_as_float(w[3 * j]), __uint_as_float(w[3 * j + 1]),
+                                        __uint_as_float(w[3 * j + 2]));
+                    m[10] = max3_nan(__uint_as_float(w[30]), __uint_as_float(w[31]), __uint_as_float(w[31]));
+                    const float m0 = max3_nan(m[0], m[1], m[2]), m1 = max3_nan(m[3], m[4], m[5]);
+                    const float m2 = max3_nan(m[6], m[7], m[8]), m3 = max3_nan(m[9], m[10], m[10]);
+                    mx2[h] = max3_nan(max3_nan(m0, m1, m2), m3, m3);
+                }
+                if (c == 0) { cm0 = mx2[0]; cm1 = mx2[1]; } else { cm2 = mx2[0]; cm3 = mx2[1]; }
             }
-            // rare: re-read the hit chunks and queue their (row, query) pairs
-            while (hitmask != 0u && ring_ok) {
-                const int c = __ffs(hitmask) - 1;
-                hitmask &= hitmask - 1u;
-                uint32_t v[32];
-                tmem_ld_x32(tbase + (uint32_t)(c * 32), v);
-                tmem_wait_ld();
+            // ---- then the tile half's row bounds (both row-bound warps of CTA
+            // hh; tagged with the tile, polled, bounded): by now they are
+            // normally there, so their latency hides behind the filter
+            uint64_t v0 = 0, v1 = 0;
+            {
+                const uint32_t tag = (uint32_t)(i + 1);
+                const volatile uint64_t* sl = &ctl->mr[e][hh][0];
+                bool ready = false;
+                uint64_t t0 = 0;
+                for (int it = 0;; ++it) {
+                    if (lane == 0) { v0 = sl[0]; v1 = sl[1]; }
+                    v0 = __shfl_sync(0xffffffffu, v0, 0);
+                    v1 = __shfl_sync(0xffffffffu, v1, 0);
+                    if ((uint32_t)(v0 >> 32) == tag && (uint32_t)(v1 >> 32) == tag) { ready = true; break; }
+                    if (it == 0) t0 = globaltimer_ns();
+                    if (*abort || globaltimer_ns() - t0 >= a.wait_ns) break;
+                    __nanosleep(32);
+                }
+                if (!ready) {
+                    if (lane == 0) set_abort(ctl, a.status, peer);
+                    break;
+                }
+            }
+            const float mh = fmaxf(__uint_as_float((uint32_t)v0), __uint_as_float((uint32_t)v1));
+            const float ts = tau_score(*reinterpret_cast<volatile uint64_t*>(&ctl->tau[q]));
+            const float theta =
+                qvalid ? __fsub_rd(ts, __fmul_ru(EPS, __fmul_ru(mh, l1))) : INFINITY;
+            // warp-uniform: chunks where some pair reaches theta (NaN passes)
+            unsigned hitmask = (__any_sync(0xffffffffu, !(cm0 < theta)) ? 1u : 0u) |
+                               (__any_sync(0xffffffffu, !(cm1 < theta)) ? 2u : 0u) |
+                               (__any_sync(0xffffffffu, !(cm2 < theta)) ? 4u : 0u) |
+                               (__any_sync(0xffffffffu, !(cm3 < theta)) ? 8u : 0u);
+            // rare: re-read the hit chunks into per-chunk bit masks, release the
+            // accumulator, and only then queue the (row, query) pairs, so that
+            // queueing never holds up the next MMAs
+            const int64_t half_row0 = a.row_begin + ((int64_t)(cl + i * ncl) * 2 + hh) * PR;
+            uint32_t hb0 = 0, hb1 = 0, hb2 = 0, hb3 = 0;
+            for (unsigned hm = hitmask; hm != 0u; hm &= hm - 1u) {
+                const int c = __ffs(hm) - 1;
                 uint32_t bits = 0;
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    bits |= (uint32_t)(!(__uint_as_float(v[j]) < neg)) << j;
-                const int rem = a.nq - c * 32;
-                bits &= rem >= 32 ? 0xffffffffu : (1u << rem) - 1u;
+                for (int hf = 0; hf < 2; ++hf) {   // 16 columns at a time: fewer live registers
+                    uint32_t v[16];
+                    tmem_ld_x16(tbase + (uint32_t)(c * 32 + hf * 16), v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        bits |= (uint32_t)(!(__uint_as_float(v[j]) < theta)) << (hf * 16 + j);
+                }
+                const int64_t rem = a.n_rows - (half_row0 + c * 32);   // rows past the end never pass
+                bits &= rem >= 32 ? 0xffffffffu : (rem <= 0 ? 0u : (1u << rem) - 1u);
+                if (!qvalid) bits = 0u;   // padded queries (a NaN row passes the compare)
+                if (c == 0) hb0 = bits; else if (c == 1) hb1 = bits; else if (c == 2) hb2 = bits; else hb3 = bits;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl->acc_empty[b]), 0));
+            for (int c = 0; hitmask != 0u && ring_ok && c < PR / 32; ++c) {
+                if (!((hitmask >> c) & 1u)) continue;
+                uint32_t bits = c == 0 ? hb0 : c == 1 ? hb1 : c == 2 ? hb2 : hb3;
                 while (ring_ok && __any_sync(0xffffffffu, bits != 0)) {
                     const bool has = bits != 0;
                     const int j = has ? __ffs(bits) - 1 : 0;
@@ -546,13 +645,10 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                     }
                     if (has)
                         ctl->ring[ew][(tail + __popc(mk & ((1u << lane) - 1u))) % RING] =
-                            ((uint64_t)(tile_row0 + r) << 8) | (uint64_t)(c * 32 + j);
+                            ((uint64_t)(half_row0 + c * 32 + j) << 8) | (uint64_t)q;
                     tail += n;   // published once per tile, below
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->acc_empty[b]);
             if (tail != published) {   // this tile's pairs
                 if (lane == 0) {
                     __threadfence_block();
@@ -561,7 +657,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                 published = tail;
             }
             if (!ring_ok) {
-                if (lane == 0) set_abort(ctl, a.status);
+                if (lane == 0) set_abort(ctl, a.status, peer);
                 break;
             }
         }
@@ -570,40 +666,47 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             __threadfence_block();
             st_volatile(&ctl->epi_done[ew], 1);   // after its last published pair
         }
-    } else if (warp == 2 || warp == 3 || warp >= 16) {
+    } else if (warp == 2 || warp == 3 || warp == 6 || warp == 7) {
         // ------------------------------------------------------- rescorers
         // Exact rescoring of the epilogue warps' pairs, off the accumulator
-        // path: rescorer c drains the rings of epilogue warps RPR*c .. RPR*c + RPR-1,
-        // gathering up to 32 pairs across them into one batch (lane = pair), so
-        // that sparse hits do not pay a batch's memory latency each.
-        const int c = warp < 16 ? warp - 2 : warp - 14;
-        int head[RPR];   // warp-uniform
+        // path.  The first CTA has three rescorers (warp 3 issues MMAs there),
+        // the second four; rescorer c drains rings c, c + nres, ... gathering up
+        // to 32 pairs across them into one batch (lane = pair), so that sparse
+        // hits do not pay a batch's memory latency each.
+        const int nres = crank == 0 ? 3 : 4;
+        const int c = warp == 2 ? 0 : warp == 3 ? 3 : warp - 5;   // warps 6, 7 -> 1, 2
+        const int nr = (N_EPI_WARPS - c + nres - 1) / nres;       // rings of this rescorer
+        int head[RPR_MAX];   // warp-uniform
 #pragma unroll
-        for (int e4 = 0; e4 < RPR; ++e4) head[e4] = 0;
+        for (int e4 = 0; e4 < RPR_MAX; ++e4) head[e4] = 0;
         uint64_t last = globaltimer_ns();
         uint64_t refreshed = 0;
         for (;;) {
-            // thresholds raised by other CTAs (shared through tau_global), refolded
-            // here every REFRESH_NS so that the epilogue never waits on them
+            // thresholds raised by other clusters (shared through tau_global),
+            // copied here every REFRESH_NS: rescorer c refreshes the CTA's query
+            // blocks of 32 numbered c, c + nres, ...
             const uint64_t now = globaltimer_ns();
             if (now - refreshed > REFRESH_NS) {
                 refreshed = now;
-#pragma unroll
-                for (int j = 0; j < TC_NMAX / (32 * N_RESCORERS); ++j) {
-                    const int q = c * (TC_NMAX / N_RESCORERS) + j * 32 + lane;
+                for (int j = c; j < PQ / 32; j += nres) {
+                    const int q = q0 + j * 32 + lane;
                     if (q < a.nq) {
                         const uint64_t t = *reinterpret_cast<volatile uint64_t*>(&a.tau_global[q]);
-                        if (t > ctl->tau[q]) raise_tau(ctl, FB, q, t);
+                        if (t > ctl->tau[q])
+                            atomicMax(reinterpret_cast<unsigned long long*>(&ctl->tau[q]),
+                                      (unsigned long long)t);
                     }
                 }
             }
-            int avail[RPR];
+            int avail[RPR_MAX];
             int total = 0;
 #pragma unroll
-            for (int e4 = 0; e4 < RPR; ++e4) {
+            for (int e4 = 0; e4 < RPR_MAX; ++e4) {
                 // one lane's read, shared: every lane sees the same count
-                avail[e4] = __shfl_sync(0xffffffffu, ld_volatile(&ctl->ring_tail[c * RPR + e4]), 0) -
-                            head[e4];
+                avail[e4] = e4 < nr ? __shfl_sync(0xffffffffu,
+                                                  ld_volatile(&ctl->ring_tail[c + e4 * nres]), 0) -
+                                          head[e4]
+                                    : 0;
                 total += avail[e4];
             }
             __threadfence_block();   // the entries published before those tails
@@ -613,7 +716,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                 // lane l takes the l-th pending pair in ring order
                 int off = lane, er = 0;
 #pragma unroll
-                for (int e4 = 0; e4 < RPR - 1; ++e4)
+                for (int e4 = 0; e4 < RPR_MAX - 1; ++e4)
                     if (er == e4 && off >= avail[e4]) {
                         off -= avail[e4];
                         er = e4 + 1;
@@ -621,23 +724,23 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
                 const bool valid = lane < m;
                 uint64_t entry = 0ull;
 #pragma unroll
-                for (int e4 = 0; e4 < RPR; ++e4)
-                    if (valid && er == e4) entry = ctl->ring[c * RPR + e4][(head[e4] + off) % RING];
+                for (int e4 = 0; e4 < RPR_MAX; ++e4)
+                    if (valid && er == e4) entry = ctl->ring[c + e4 * nres][(head[e4] + off) % RING];
                 __syncwarp();
                 int rem = m;
 #pragma unroll
-                for (int e4 = 0; e4 < RPR; ++e4) {
+                for (int e4 = 0; e4 < RPR_MAX; ++e4) {
                     const int take = min(avail[e4], rem);
                     rem -= take;
                     if (take > 0) {
                         head[e4] += take;
                         if (lane == 0) {
                             __threadfence_block();
-                            st_volatile(&ctl->ring_head[c * RPR + e4], head[e4]);   // slots read: free them
+                            st_volatile(&ctl->ring_head[c + e4 * nres], head[e4]);   // slots read: free them
                         }
                     }
                 }
-                rescore_batch(ctl, FB, ctl->hist[c], entry, valid, m, a);
+                rescore_batch(ctl, ctl->hist[c], entry, valid, m, a);
                 progress = true;
             }
             if (progress) {
@@ -647,8 +750,9 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             // idle: done once every producer has finished and its ring is empty
             bool done = true;
 #pragma unroll
-            for (int e4 = 0; e4 < RPR; ++e4) {
-                const int e = c * RPR + e4;
+            for (int e4 = 0; e4 < RPR_MAX; ++e4) {
+                if (e4 >= nr) continue;
+                const int e = c + e4 * nres;
                 const bool fin = ld_volatile(&ctl->epi_done[e]) != 0;
                 __threadfence_block();
                 done = done && fin && ld_volatile(&ctl->ring_tail[e]) == head[e4];
@@ -656,18 +760,22 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmA,
             if (__all_sync(0xffffffffu, done)) break;
             if (*abort) break;
             if (globaltimer_ns() - last >= a.wait_ns) {
-                if (lane == 0) set_abort(ctl, a.status);
+                if (lane == 0) set_abort(ctl, a.status, peer);
                 break;
             }
             __nanosleep(256);
         }
     }
 
+    // every role of both CTAs has finished (each loop above is bounded) before
+    // either CTA frees the TMEM or exits: the pair's MMAs, commits, remote
+    // arrivals and stores all target both CTAs
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();
     tc_fence_after();
-    if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
+    if (warp == 2) tmem_dealloc_pair(tmem, TMEM_COLS);
 }
+
 
 // Seeds each query's pool with the exact top-k of the sample rows and sets
 // its starting threshold to the k-th of them.
@@ -780,12 +888,13 @@ size_t tc_ws_bytes(int64_t n, int64_t nq, int64_t k) {
 hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, int64_t nq,
                           int64_t k, int64_t row_offset, int64_t* out_idx, float* out_scores,
                           void* ws, size_t ws_bytes, cudaStream_t st, int32_t* dev_status) {
-    HMM_REQUIRE(n < (int64_t(1) << 31), "n_rows must be < 2^31");
+    // tile coordinates (up to n + 255) stay int32
+    HMM_REQUIRE(n < (int64_t(1) << 31) - 512, "n_rows must be < 2^31 - 512");
     HMM_CUDA_TRY(cudaFuncSetAttribute(tc_score_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     const int64_t seed = std::min<int64_t>(n, SEED_ROWS);
-    CUtensorMap tmA;
-    hmm_status_t s = make_tmap_bf16(&tmA, mem, n, TC_M);
+    CUtensorMap tmR;
+    hmm_status_t s = make_tmap_bf16(&tmR, mem, n, PR);
     if (s != HMM_OK) return s;
     const int sms = device_sm_count();
     for (int64_t q0 = 0; q0 < nq; q0 += TC_NMAX) {
@@ -812,8 +921,8 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         s = check_launch("seed_pool_kernel");
         if (s != HMM_OK) return s;
 
-        CUtensorMap tmB;
-        s = make_tmap_bf16(&tmB, qp, nqp_pass, TC_NMAX);
+        CUtensorMap tmQ;
+        s = make_tmap_bf16(&tmQ, qp, nqp_pass, PQ);
         if (s != HMM_OK) return s;
         // One tensor-core pass over rows [seed, n), appending to the pools.  The
         // pools start from the seed's exact top-k, and the rescorers refresh the
@@ -824,7 +933,7 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
             TcArgs a;
             a.n_rows = n;
             a.row_begin = seed;
-            a.n_tiles = (int)((n - seed + TC_M - 1) / TC_M);
+            a.n_tiles = (int)((n - seed + 2 * PR - 1) / (2 * PR));
             a.nq = nqp_pass;
             a.k = (int)k;
             a.pool_cap = POOL_CAP;
@@ -836,9 +945,10 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
             a.pool_cnt = cnt;
             a.status = status;
             a.wait_ns = wait_limit_ns();
-            const int grid = std::max(1, std::min(sms, a.n_tiles));
+            // clusters of two CTAs, one per pair of SMs
+            const int grid = 2 * std::max(1, std::min(sms / 2, a.n_tiles));
             const ProfileMark pm = profile_begin(st);
-            tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmA, tmB, a);
+            tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmR, tmQ, a);
             s = check_launch("tc_score_select_kernel");
             profile_end(pm, st);
             if (s != HMM_OK) return s;

@@ -40,7 +40,7 @@ constexpr int BSA_MIN_SPLIT_TOKENS = BSA_WARPS * 4;
 constexpr int BSA_MIN_SPLIT_PAGES = BSA_WARPS;
 constexpr int BSA_PAGES_PER_SPLIT = 8 * BSA_WARPS;   // pages a split takes when sequences are many
 constexpr int SEL_MAX_BLOCKS = 8192;    // summaries per sequence for the fused selection
-constexpr int SEL_THREADS_MAX = 512;    // block selection: threads per sequence
+constexpr int SEL_THREADS_MAX = 1024;   // block selection: threads per sequence
 
 struct PagedCache {
     const uint16_t* pages;   // [n_pages][page_tokens][D]
@@ -741,61 +741,57 @@ __global__ void __launch_bounds__(CMB_THREADS) bsa_combine_kernel(const float* _
 // upper bound of q.k over its keys, sum_j max(q_j * min_j, q_j * max_j) in j
 // order; otherwise rows are [block][D] and the score is q . summary.
 template <bool MINMAX>
-__global__ void __launch_bounds__(SEL_THREADS_MAX, 2) block_select_kernel(
+__global__ void __launch_bounds__(SEL_THREADS_MAX) block_select_kernel(
     const float* __restrict__ summ, int n_blocks, int D, const uint16_t* __restrict__ q, int top,
     int32_t* __restrict__ sel) {
-    extern __shared__ __align__(16) unsigned char ssm[];
+    extern __shared__ unsigned char ssm[];
     const int s = blockIdx.x;
     const int n2 = next_pow2(n_blocks);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int NR = MINMAX ? 2 : 1;            // summary rows per block (mean; min and max)
-    constexpr int CW = 32;                        // columns per staged chunk
     uint64_t* keys = reinterpret_cast<uint64_t*>(ssm);
     float* qf = reinterpret_cast<float*>(keys + n2);
-    // per warp: 32 rows x CW columns (x NR), row stride CW + 1 floats (lane l
-    // reads row l column j from bank (l + j) mod 32: no conflicts)
-    float* stage = qf + ((D + 3) & ~3) + warp * NR * 32 * (CW + 1);
     for (int d = threadIdx.x; d < D; d += blockDim.x)
         qf[d] = bf16_bits_to_f32(q[(int64_t)s * D + d]);
     __syncthreads();
-    const float* S = summ + (int64_t)s * n_blocks * D * NR;
-    // a warp takes 32 summary rows at a time; its loads are coalesced (8 lanes
-    // read one row's 128-byte chunk), and each lane then extends its own row's
-    // sum in column order from shared memory (the reference's separate
-    // multiply and add)
-    for (int b0 = warp * 32; b0 < n2; b0 += (int)(blockDim.x >> 5) * 32) {
-        const int b = b0 + lane;
-        float acc = 0.0f;
-        for (int c0 = 0; c0 < D; c0 += CW) {
-            __syncwarp();
+    const float* S = summ + (int64_t)s * n_blocks * D * (MINMAX ? 2 : 1);
+    // one thread per summary row (blockDim >= n2 up to SEL_THREADS_MAX); each
+    // thread keeps 8 16-byte loads of its row (4 of each bound row) in flight
+    // ahead of the in-order sum (the reference's separate multiply and add)
+    constexpr int U = MINMAX ? 4 : 8;
+    for (int b = threadIdx.x; b < n2; b += blockDim.x) {
+        uint64_t key = 0ull;
+        if (b < n_blocks) {
+            const float4* lo = reinterpret_cast<const float4*>(S + (int64_t)b * (MINMAX ? 2 : 1) * D);
+            const float4* hi = lo + (D >> 2);
+            float acc = 0.0f;
+            for (int d0 = 0; d0 < (D >> 2); d0 += U) {
+                float4 a[U], z[U];
 #pragma unroll
-            for (int rr = 0; rr < 32; rr += 4) {           // 4 rows per load instruction
-                const int r = rr + (lane >> 3), c = c0 + (lane & 7) * 4;
-                const int row = b0 + r;
+                for (int u = 0; u < U; ++u) {
+                    const bool in = d0 + u < (D >> 2);
+                    a[u] = in ? __ldg(lo + d0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (MINMAX) z[u] = in ? __ldg(hi + d0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
 #pragma unroll
-                for (int h = 0; h < NR; ++h) {
-                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (row < n_blocks && c < D)
-                        v = __ldg(reinterpret_cast<const float4*>(S + ((int64_t)row * NR + h) * D + c));
-                    float* dst = stage + (h * 32 + r) * (CW + 1) + (lane & 7) * 4;
-                    dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+                for (int u = 0; u < U; ++u) {
+                    if (d0 + u >= (D >> 2)) break;
+                    const float av[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float qv = qf[4 * (d0 + u) + i];
+                        if (MINMAX) {
+                            const float zv[4] = {z[u].x, z[u].y, z[u].z, z[u].w};
+                            const float l = __fmul_rn(qv, av[i]);
+                            const float h = __fmul_rn(qv, zv[i]);
+                            acc = __fadd_rn(acc, l > h ? l : h);
+                        } else {
+                            acc = __fadd_rn(acc, __fmul_rn(av[i], qv));
+                        }
+                    }
                 }
             }
-            __syncwarp();
-            const int w = min(CW, D - c0);
-            const float* mine = stage + lane * (CW + 1);
-            for (int j = 0; j < w; ++j) {
-                const float qv = qf[c0 + j];
-                if (MINMAX) {
-                    const float l = __fmul_rn(qv, mine[j]);
-                    const float h = __fmul_rn(qv, mine[32 * (CW + 1) + j]);
-                    acc = __fadd_rn(acc, l > h ? l : h);
-                } else {
-                    acc = __fadd_rn(acc, __fmul_rn(mine[j], qv));
-                }
-            }
+            key = make_cand(f32_key(acc), (uint32_t)b);
         }
-        if (b < n2) keys[b] = b < n_blocks ? make_cand(f32_key(acc), (uint32_t)b) : 0ull;
+        keys[b] = key;
     }
     block_bitonic_sort_desc(keys, n2);
     const int m = min(top, n_blocks);
@@ -806,13 +802,6 @@ __global__ void __launch_bounds__(SEL_THREADS_MAX, 2) block_select_kernel(
 // ---------------------------------------------------------------- host
 // Threads of the block selection: one per summary row, 128 .. SEL_THREADS_MAX.
 int select_threads(int n2) { return std::max(128, std::min(SEL_THREADS_MAX, n2)); }
-
-// Its dynamic shared memory: keys, the query, and each warp's staged rows.
-size_t select_smem_bytes(int n2, int64_t D, bool minmax) {
-    const int warps = select_threads(n2) / 32;
-    return sizeof(uint64_t) * n2 + sizeof(float) * ((D + 3) & ~3) +
-           sizeof(float) * (size_t)warps * (minmax ? 2 : 1) * 32 * 33;
-}
 
 struct BsaPlan {
     int splits, split_tokens;
@@ -1106,7 +1095,7 @@ extern "C" hmm_status_t hmm_block_select_minmax(const uint16_t* q, const float* 
     HMM_REQUIRE((reinterpret_cast<uintptr_t>(minmax) % 16) == 0, "minmax must be 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int n2 = next_pow2((int)std::max<int64_t>(n_blocks, 1));
-    const size_t ssm = select_smem_bytes(n2, D, true);
+    const size_t ssm = sizeof(uint64_t) * n2 + sizeof(float) * D;
     HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel<true>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm));
     block_select_kernel<true><<<(unsigned)n_seq, select_threads(n2), ssm, st>>>(
@@ -1220,7 +1209,7 @@ extern "C" hmm_status_t hmm_block_sparse_decode_bf16_async(
     int* status = device_status;
     int32_t* sel = out_blocks ? out_blocks : reinterpret_cast<int32_t*>(ws + sel_off);
     const int n2 = next_pow2((int)n_blocks);
-    const size_t ssm = select_smem_bytes(n2, D, false);
+    const size_t ssm = sizeof(uint64_t) * n2 + sizeof(float) * D;
     HMM_CUDA_TRY(cudaFuncSetAttribute(block_select_kernel<false>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssm));
     block_select_kernel<false><<<(unsigned)n_seq, select_threads(n2), ssm, st>>>(

@@ -88,11 +88,12 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 // wall time or when *abort becomes nonzero.  Returns false when it gave up.
 // The limit and the abort flag are checked before the first suspended
 // try_wait and then every eighth.  A limit of 0 (a test setting) never
-// blocks: the wait gives up whenever the phase is not already complete
-// (try_wait itself may suspend for a while before it reports that).
+// blocks: the wait gives up whenever the phase is not already complete.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort, uint64_t limit_ns) {
-    if (limit_ns == 0) return mbar_test_wait(bar, parity);
+    // a phase that already completed costs one non-blocking test
+    if (mbar_test_wait(bar, parity)) return true;
+    if (limit_ns == 0) return false;
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 0;; ++i) {
@@ -102,6 +103,42 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
         }
         if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     }
+}
+
+// ------------------------------------------------- clusters (CTA pairs)
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// The shared::cluster address of `local` (a shared::cta address of this CTA)
+// in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
+// Arrives on an mbarrier of any CTA of the cluster (default .release.cta
+// semantics, as CUTLASS's pair pipelines release a peer's stage).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+// One 8-byte store (single-copy atomic) into a cluster CTA's shared memory.
+__device__ __forceinline__ void st_cluster_u64(uint32_t cluster_addr, uint64_t v) {
+    asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(cluster_addr), "l"(v) : "memory");
+}
+
+// Every thread of every CTA of the cluster: arrive (release) and wait (acquire).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
 }
 
 // Waits for the phase with `parity` whatever any abort flag says, for at
@@ -184,6 +221,42 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
             smem_u32(bar))
+        : "memory");
+}
+
+// --- CTA-pair forms (cta_group::2).  A kernel that uses them uses no
+// cta_group::1 tcgen05 instruction.  Both CTAs of the pair allocate and free
+// (the same warp index, the same shared-memory slot); the pair's first CTA
+// issues the MMAs, which read the A and B halves at the same shared-memory
+// offsets in both CTAs and write each CTA's half of D into its own TMEM.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives once on the mbarrier at `cluster_addr` (this CTA's or the peer's)
+// when every pair MMA this thread issued so far completes.
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            cluster_addr)
         : "memory");
 }
 
