@@ -24,7 +24,7 @@ def run(cuda, mem, qry, k, off=0):
 
 @pytest.mark.parametrize("n,nq,k,seed", [
     (20000, 16, 100, 1),      # a few tiles per SM
-    (12345, 1, 64, 2),        # one query (MMA N = 16), ragged last tile
+    (12345, 1, 64, 2),        # one query (255 padded query rows), ragged last tile
     (9000, 300, 32, 3),       # two query passes (256 + 44)
     (300000, 256, 100, 4),    # every SM busy for many tiles
 ])
