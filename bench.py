@@ -1068,7 +1068,8 @@ def run_dsa(args, rank, world, local):
         "config": {"workload": f"DSA indexer: {n_tok} tokens x {D_HEADS} heads x {D_DIM} e4m3, "
                                f"{D_KEYS} keys, causal, top-{D_TOPK}",
                    "parallelism": f"token split x{world}",
-                   "l2": "score rows (T x 131,072 fp32, 2 GB) larger than L2"},
+                   "l2": "keys (16 MiB) re-read per token group, hit bitmap (T x 16 KiB) "
+                         "and candidate lists larger than L2"},
         "e2e": {"value": n_tok / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": T * D_HEADS * D_DIM + T * D_HEADS * 4,
                 "d2h_bytes_per_step": T * D_TOPK * (4 + 4), "token_slices": args.dsa_chunks or "waves"},

@@ -18,12 +18,14 @@
 //   warps 4-19  epilogue, four warpgroups (tile parity x token half):
 //               thread = key; per token, sum_h w * max(x, 0) over the
 //               token's head columns (weights staged in shared memory per
-//               warp and group), causal mask, coalesced fp32 score rows
+//               warp and group), causal mask; then (COLLECT) one ballot per
+//               warp marks the keys whose upper bound reaches the token's
+//               threshold in a bitmap word; (WRITE) coalesced fp32 score rows
 // Scores are fp32 tensor-core sums of exact e4m3 products; they differ from
 // the exact dot products by the accumulation's rounding.  The selection is
-// exact: dsa_exact.cu takes each token's band of keys whose score could reach
-// the k-th, rescores them exactly (integer limbs on the tensor cores) and
-// selects the top-k from the exact scores.
+// exact: dsa_exact.cu takes each token's keys whose score could reach the
+// k-th (the bitmap), rescores them exactly (integer limbs on the tensor
+// cores) and selects the top-k from the exact scores.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -31,6 +33,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "dsa_exact.cuh"
 #include "heteromm_cuda.h"
 #include "hmm_common.cuh"
 #include "sm100_ptx.cuh"
@@ -51,6 +54,8 @@ constexpr int D_THREADS = 128 + 128 * D_EPI_WG;
 
 struct DsaCtrl {
     float wsm[4 * D_EPI_WG][NQ / 2];        // each epilogue warp's token weights for its group
+    float esm[4 * D_EPI_WG][8];             // ... its tokens' E_t (COLLECT)
+    float tsm[4 * D_EPI_WG][8];             // ... its tokens' thresholds (COLLECT)
     uint64_t a_full[D_STAGES], a_empty[D_STAGES];
     uint64_t q_full[2], q_empty[2];
     uint64_t acc_full[2], acc_empty[2];
@@ -61,7 +66,12 @@ constexpr size_t D_SMEM = 1024 + 2 * Q_TILE_BYTES + D_STAGES * K_TILE_BYTES + si
 
 struct DsaArgs {
     const float* w;       // [T][H]
-    float* scores;        // [T][L]
+    float* scores;        // [T][L] (WRITE)
+    const float* norms;   // [L] ||k_j|| rounded up (COLLECT)
+    const float* tok_e;   // [T] E_t (COLLECT)
+    const float* tok_tau; // [T] thresholds (COLLECT)
+    uint32_t* bitmap;     // [T][W] keys with s~ + E_t ||k_j|| >= tau (COLLECT)
+    int W;                // bitmap words per token
     int* status;          // [0] timeout, [1] a row the sampled top-k could not select
     int64_t T, L, pos0;
     int H, tg;            // heads, tokens per group (NQ / H)
@@ -102,11 +112,12 @@ __device__ __forceinline__ void dsa_abort(DsaCtrl* c, int* status) {
     atomicExch(&status[0], 1);
 }
 
-template <int H>   // heads: 16, 32 or 64; the epilogue loops unroll fully
+template <int H, bool WRITE, bool COLLECT>   // heads: 16, 32 or 64; the epilogue loops unroll fully
 __global__ void __launch_bounds__(D_THREADS, 1)
 dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
                   const DsaArgs a) {
     constexpr int TG2 = NQ / H / 2;   // tokens per epilogue warp and tile
+    static_assert(TG2 <= 8, "per-warp token slots");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     unsigned char* Qs = smem;                                  // 2 x 32 KB
@@ -225,6 +236,8 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         const int sub = warp & 3;              // TMEM lanes 32*sub .. +31
         const int r = sub * 32 + lane;         // key within the tile
         float* wsm = ctl->wsm[ew];   // per warp: no cross-warp barrier on any path
+        float* esm = ctl->esm[ew];
+        float* tsm = ctl->tsm[ew];
         int i = 0, g_loaded = -1;
         bool ok = true;
         for (int g = blockIdx.x; ok && g < a.n_groups; g += G) {
@@ -238,6 +251,11 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     const int64_t base = ((int64_t)g * (2 * TG2) + half * TG2) * H;
                     for (int e = lane; e < n; e += 32)
                         wsm[e] = base + e < a.T * H ? a.w[base + e] : 0.0f;
+                    if (COLLECT && lane < TG2) {
+                        const int64_t tok = (int64_t)g * (2 * TG2) + half * TG2 + lane;
+                        esm[lane] = tok < a.T ? a.tok_e[tok] : 0.0f;
+                        tsm[lane] = tok < a.T ? a.tok_tau[tok] : INFINITY;
+                    }
                     __syncwarp();
                     g_loaded = g;
                 }
@@ -246,6 +264,7 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 tc_fence_after();
                 const int64_t j = (int64_t)t * KT + r;
                 const uint32_t tb = tmem + (uint32_t)(b * NQ) + ((uint32_t)(sub * 32) << 16);
+                const float nj = COLLECT && j < a.L ? __ldg(a.norms + j) : 0.0f;
 #pragma unroll
                 for (int tl = 0; tl < TG2; ++tl) {
                     const int tcol = (half * TG2 + tl) * H;
@@ -278,8 +297,16 @@ dsa_scores_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     float s_lo, s_hi;
                     unpack_f32x2(s2, s_lo, s_hi);
                     const float s = s_lo + s_hi;
-                    if (tok < a.T && j < a.L)
-                        a.scores[tok * a.L + j] = j <= a.pos0 + tok ? s : -INFINITY;
+                    const bool vis = tok < a.T && j < a.L && j <= a.pos0 + tok;
+                    if (WRITE && tok < a.T && j < a.L) a.scores[tok * a.L + j] = vis ? s : -INFINITY;
+                    if (COLLECT) {
+                        // the key's upper bound s~ + E_t ||k_j|| (rounded up) against
+                        // the token's threshold; one bitmap word per warp and token
+                        const unsigned bh = __ballot_sync(
+                            0xffffffffu, vis && __fadd_ru(s, __fmul_ru(esm[tl], nj)) >= tsm[tl]);
+                        const int64_t w0 = ((int64_t)t * KT + sub * 32) >> 5;   // this warp's 32 keys
+                        if (lane == 0 && tok < a.T && w0 < a.W) a.bitmap[tok * a.W + w0] = bh;
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -358,20 +385,46 @@ size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 
 using namespace hmm;
 
-namespace hmm {
-size_t dsa_exact_ws_bytes(int64_t T, int64_t L);
-hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* ws,
-                               cudaStream_t st, int** status_out);
-hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float* w, int64_t T,
-                              int64_t H, int64_t L, int64_t pos0, int64_t topk, float* scores,
-                              int32_t* out_idx, float* out_sc, void* ws, cudaStream_t st);
-}  // namespace hmm
+namespace {
+
+// One scoring pass over keys[0, L) (the call's keys or the sample): TMA maps,
+// then the kernel for the head count and the pass's outputs.
+template <bool WRITE, bool COLLECT>
+hmm_status_t launch_scores(const uint8_t* q, const uint8_t* keys, int64_t T, int64_t H, int64_t L,
+                           DsaArgs a, bool profiled, cudaStream_t st) {
+    CUtensorMap tmK, tmQ;
+    hmm_status_t s = make_tmap_u8(&tmK, keys, L, KT);
+    if (s != HMM_OK) return s;
+    s = make_tmap_u8(&tmQ, q, T * H, NQ);
+    if (s != HMM_OK) return s;
+    a.T = T;
+    a.L = L;
+    a.H = (int)H;
+    a.tg = NQ / (int)H;
+    a.n_groups = (int)((T + a.tg - 1) / a.tg);
+    a.key_tiles = (int)((L + KT - 1) / KT);
+    a.wait_ns = wait_limit_ns();
+    auto kern = H == 64 ? dsa_scores_kernel<64, WRITE, COLLECT>
+              : H == 32 ? dsa_scores_kernel<32, WRITE, COLLECT>
+                        : dsa_scores_kernel<16, WRITE, COLLECT>;
+    HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)D_SMEM));
+    const int grid = std::max(1, std::min(device_sm_count(), a.n_groups));
+    // the profile marks time the pass over every key, not the sample's
+    ProfileMark pm{};
+    if (profiled) pm = profile_begin(st);
+    kern<<<grid, D_THREADS, D_SMEM, st>>>(tmK, tmQ, a);
+    s = check_launch("dsa_scores_kernel");
+    if (profiled) profile_end(pm, st);
+    return s;
+}
+
+}  // namespace
 
 extern "C" size_t hmm_dsa_indexer_fp8_workspace_size(int64_t T, int64_t H, int64_t L,
                                                      int64_t topk) {
     if (T < 0 || H < 1 || L < 0 || topk < 1) return 0;
-    return up256(sizeof(float) * (size_t)T * (size_t)L) + up256(dsa_exact_ws_bytes(T, L)) +
-           up256(sizeof(float) * (size_t)T * (size_t)topk);
+    return up256(dsa_exact_ws_bytes(T, L)) + up256(sizeof(float) * (size_t)T * (size_t)topk);
 }
 
 extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* keys,
@@ -395,15 +448,13 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
                 "q, keys and w must be 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    const size_t sc_bytes = all_scores ? 0 : up256(sizeof(float) * (size_t)T * (size_t)L);
     const size_t ex_bytes = up256(dsa_exact_ws_bytes(T, L));
     const size_t sel_bytes = up256(sizeof(float) * (size_t)T * (size_t)topk);
-    const size_t need = sc_bytes + ex_bytes + sel_bytes;
+    const size_t need = ex_bytes + sel_bytes;
     if (!ws || workspace_bytes < need)
         return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", workspace_bytes, need);
-    float* scores = all_scores ? all_scores : reinterpret_cast<float*>(ws);
-    void* ex_ws = ws + sc_bytes;
-    float* sel_sc = out_scores ? out_scores : reinterpret_cast<float*>(ws + sc_bytes + ex_bytes);
+    void* ex_ws = ws;
+    float* sel_sc = out_scores ? out_scores : reinterpret_cast<float*>(ws + ex_bytes);
     const int64_t n_sel = T * topk;
 
     if (L == 0) {   // no key is visible to any token
@@ -411,43 +462,51 @@ extern "C" hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* key
         dsa_fill_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(sel_sc, n_sel);
         return check_launch("dsa_fill_kernel");
     }
-    int* status = nullptr;
-    hmm_status_t s = dsa_exact_prepare(keys, T, L, ex_ws, st, &status);
+    DsaExactBufs b;
+    hmm_status_t s = dsa_exact_prepare(keys, T, L, topk, ex_ws, st, &b);
     if (s != HMM_OK) return s;
-    CUtensorMap tmK, tmQ;
-    s = make_tmap_u8(&tmK, keys, L, KT);
-    if (s != HMM_OK) return s;
-    s = make_tmap_u8(&tmQ, q, T * H, NQ);
-    if (s != HMM_OK) return s;
-    DsaArgs a;
+    DsaArgs a{};
     a.w = w;
-    a.scores = scores;
-    a.status = status;   // [0]: a bounded wait gave up
-    a.T = T;
-    a.L = L;
+    a.status = b.status;   // [0]: a bounded wait gave up
+    a.norms = b.norms;
+    a.tok_e = b.tok_e;
+    a.tok_tau = b.tok_tau;
+    a.bitmap = b.bitmap;
+    a.W = b.W;
+    if (b.S > 0) {
+        // 1. the sampled keys' scores (every sampled key visible to every token)
+        DsaArgs sa = a;
+        sa.scores = b.sscores;
+        sa.pos0 = b.S;
+        s = launch_scores<true, false>(q, b.skeys, T, H, b.S, sa, false, st);
+        if (s != HMM_OK) return s;
+    }
+    // 2. E_t and the thresholds
+    s = dsa_exact_thresholds(q, w, T, H, L, pos0, topk, b, st);
+    if (s != HMM_OK) return s;
+    // 3. the scoring pass over every key: the bitmap of each token's keys that
+    //    can reach its k-th (and the scores themselves when asked for); when no
+    //    token sees more than the candidate capacity, every visible key is a
+    //    candidate and only the asked-for scores need the pass
     a.pos0 = pos0;
-    a.H = (int)H;
-    a.tg = NQ / (int)H;
-    a.n_groups = (int)((T + a.tg - 1) / a.tg);
-    a.key_tiles = (int)((L + KT - 1) / KT);
-    a.wait_ns = wait_limit_ns();
-    auto kern = H == 64 ? dsa_scores_kernel<64> : H == 32 ? dsa_scores_kernel<32>
-                                                          : dsa_scores_kernel<16>;
-    HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)D_SMEM));
-    const int grid = std::max(1, std::min(device_sm_count(), a.n_groups));
-    const ProfileMark pm = profile_begin(st);
-    kern<<<grid, D_THREADS, D_SMEM, st>>>(tmK, tmQ, a);
-    s = check_launch("dsa_scores_kernel");
-    profile_end(pm, st);
-    if (s != HMM_OK) return s;
-    dsa_tail_kernel<<<dim3(16, (unsigned)T), 256, 0, st>>>(scores, T, L, pos0, a.tg,
-                                                           a.key_tiles);
-    s = check_launch("dsa_tail_kernel");
-    if (s != HMM_OK) return s;
-    // exact selection over the approximate scores (reads the status words, so
-    // this waits for the stream), then -1 for the slots of keys nobody sees
-    s = dsa_exact_select(q, keys, w, T, H, L, pos0, topk, scores, out_idx, sel_sc, ex_ws, st);
+    if (all_scores) {
+        a.scores = all_scores;
+        s = b.S > 0 ? launch_scores<true, true>(q, keys, T, H, L, a, true, st)
+                    : launch_scores<true, false>(q, keys, T, H, L, a, true, st);
+        if (s != HMM_OK) return s;
+        const int tg = NQ / (int)H;
+        const int key_tiles = (int)((L + KT - 1) / KT);
+        dsa_tail_kernel<<<dim3(16, (unsigned)T), 256, 0, st>>>(all_scores, T, L, pos0, tg,
+                                                               key_tiles);
+        s = check_launch("dsa_tail_kernel");
+        if (s != HMM_OK) return s;
+    } else if (b.S > 0) {
+        s = launch_scores<false, true>(q, keys, T, H, L, a, true, st);
+        if (s != HMM_OK) return s;
+    }
+    // 4. exact selection (reads the status words, so this waits for the
+    //    stream), then -1 for the slots of keys nobody sees
+    s = dsa_exact_select(q, keys, w, T, H, L, pos0, topk, b, out_idx, sel_sc, ex_ws, st);
     if (s != HMM_OK) return s;
     dsa_pad_kernel<<<(unsigned)((n_sel + 255) / 256), 256, 0, st>>>(out_idx, sel_sc, n_sel);
     return check_launch("dsa_pad_kernel");

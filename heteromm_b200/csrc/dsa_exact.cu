@@ -8,32 +8,43 @@
 //
 // The tensor-core pass (dsa.cu) gives approximate scores s~ with
 //   |s~ - s| <= C_TOL * sum_h |w_h| sum_d |q_hd| |k_jd|
-//            <= C_TOL * ||u_t||_2 * ||k_j||_2,  u_t[d] = sum_h |w_h| |q_hd|
+//            <= C_TOL * ||u_t||_2 * ||k_j||_2 = E_t ||k_j||,  u_t[d] = sum_h |w_h| |q_hd|
 // where C_TOL covers the tensor core's fp32 accumulation (assumed to lose at
 // most 2^-10 of sum_d |q_hd||k_jd|, 128x the worst case of sequential fp32;
 // measured below 2e-5 of that) and the fp32 roundings of both head sums.
-// Then, per query token:
-//   1. dsa_band_kernel: lo_j = s~_j - tol_j, hi_j = s~_j + tol_j; L_k = the
-//      k-th largest lo.  Every key of the exact top-k has hi >= L_k (k keys
-//      have s >= lo >= L_k, so the exact k-th score is >= L_k), so the keys
-//      with hi_j >= L_k are the candidates.
-//   2. dsa_rescore_kernel: the candidates' exact scores on the tensor cores
+// With hi_j = s~_j + E_t ||k_j|| (rounded up) >= s_j and any threshold tau:
+// the keys with hi < tau have exact scores s < tau, so if the m-th best exact
+// score (m = min(k, visible)) among the keys with hi >= tau is >= tau, the
+// exact top-k (ties included) lies among them.  Per call:
+//   1. dsa_key_prep_kernel: ||k_j|| per key (rounded up) and a NaN check;
+//      dsa_sample_gather_kernel: S keys at j_i = floor(i L / S);
+//      the scoring pass (dsa.cu) scores the sample: [T][S] approximate scores
+//   2. dsa_threshold_kernel: E_t and tau, a floor of the r1-th largest
+//      lo = s~ - E_t ||k_j|| of the token's visible sample keys, r1 chosen so
+//      that at least m keys of the row have s >= lo >= tau except with
+//      negligible probability
+//   3. the scoring pass over every key (dsa.cu) marks the keys with hi >= tau
+//      in a bitmap; no score is stored
+//   4. dsa_cand_kernel: the marked keys become the token's candidates
+//   5. dsa_rescore_kernel: the candidates' exact scores on the tensor cores
 //      (tcgen05.mma kind::i8, exact int32 accumulation): every e4m3 value
 //      times 2^9 is an integer v, |v| <= 229,376, split into three signed
 //      6-bit limbs v = l0 + 64 l1 + 4096 l2; the nine limb products are summed
 //      in five TMEM accumulators by the scale 64^(i+i') they carry and joined
-//      exactly in 64-bit integers; the head sum is then the reference's.
-//   3. dsa_select_kernel: the exact top-k of the candidates, best first,
-//      ties to the lowest key.
-// A token whose band does not fit (possible only for near-identical keys,
-// whose scores crowd the k-th) is flagged; the host recomputes its whole row
-// exactly on CUDA cores (dsa_exact_row_kernel) and selects from that.
+//      exactly; the head sum is then the reference's.
+//   6. dsa_select_kernel: the exact top-k of the candidates, best first,
+//      ties to the lowest key, after checking that the m-th of them is >= tau.
+// A token whose candidates do not fit or whose check fails (possible only
+// for near-identical keys, whose scores crowd the k-th) is flagged; the host
+// recomputes its whole row exactly on CUDA cores (dsa_exact_rows_kernel) and
+// selects from that.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 
 #include "heteromm_cuda.h"
+#include "dsa_exact.cuh"
 #include "hmm_common.cuh"
 #include "sm100_ptx.cuh"
 
@@ -45,18 +56,18 @@ namespace {
 constexpr int DK = 128;                    // head dim: bytes per fp8 row and per limb row
 constexpr int NLIMB = 3;
 constexpr int CAP_C = 8192;                // candidates per token
-constexpr int BAND_THREADS = 512;
-constexpr int BAND_SAMPLE = 4096;
-constexpr int BAND_COLLECT = 8192;         // keys with hi >= the sampled threshold
+constexpr int BAND_THREADS = 512;          // threshold and candidate kernels
+constexpr int BAND_SAMPLE = 4096;          // sampled keys per call
+constexpr int FB_ROWS = 32;                // flagged tokens per exact-row fallback pass
 constexpr int SEL_THREADS = 512;
 constexpr int KMAX = 4096;
 // C_TOL: 2^-10 for the tensor-core accumulation plus 2^-16, which covers the
 // fp32 roundings of x_h and of both head sums (about 100 * 2^-24).
 constexpr double C_TOL = 1.0 / 1024.0 + 1.0 / 65536.0;
 
-// Status words (int) at the start of the selection workspace.
-// ST_KMAX: max_j ||k_j|| as float bits; ST_FLAGS: up to T flagged token ids.
-enum { ST_TIMEOUT = 0, ST_NAN = 1, ST_NFLAG = 2, ST_KMAX = 3, ST_FLAGS = 4 };
+// Status words (int) at the start of the selection workspace, then up to T
+// flagged token ids.
+enum { ST_TIMEOUT = 0, ST_NAN = 1, ST_NFLAG = 2, ST_FLAGS = 4 };
 
 // e4m3 (OCP FP8: bias 7, no infinities, S.1111.111 = NaN) times 2^9 as an
 // integer; the NaN encodings give 0 and are reported by the callers.
@@ -102,14 +113,13 @@ __device__ __forceinline__ void limbs16_lut(const uint4 raw, const uint32_t* lut
 }
 
 // ---------------------------------------------------------------------------
-// K0: max_j ||k_j||_2 rounded up; flags NaN encodings.  One warp per key (4
-// bytes per lane), warps striding over keys.
+// K0: ||k_j||_2 of every key rounded up; flags NaN encodings.  One warp per
+// key (4 bytes per lane), warps striding over keys.
 __global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
-                                    int* __restrict__ status) {
+                                    float* __restrict__ norms, int* __restrict__ status) {
     const int lane = threadIdx.x & 31;
     const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    float kmax = 0.0f;
     bool nan = false;
     for (int64_t j = w0; j < L; j += nw) {
         const uint32_t w = reinterpret_cast<const uint32_t*>(keys + j * DK)[lane];
@@ -123,11 +133,22 @@ __global__ void dsa_key_prep_kernel(const uint8_t* __restrict__ keys, int64_t L,
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        kmax = fmaxf(kmax, __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0)));
+        if (lane == 0) norms[j] = __double2float_ru(__dsqrt_ru((double)sq) * (1.0 / 512.0));
     }
     if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(&status[ST_NAN], 1);
-    if (lane == 0 && kmax > 0.0f)
-        atomicMax(&status[ST_KMAX], __float_as_int(kmax));   // >= 0: int order = float order
+}
+
+// K0c: the sampled keys, j_i = floor(i L / S), as a contiguous [S][128] array
+// for the scoring pass.  One thread per 16 bytes.
+__global__ void dsa_sample_gather_kernel(const uint8_t* __restrict__ keys, int64_t L, int S,
+                                         uint8_t* __restrict__ skeys) {
+    const int64_t n16 = (int64_t)S * (DK / 16);
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n16;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = e >> 3, c = e & 7;
+        const int64_t j = i * L / S;
+        reinterpret_cast<uint4*>(skeys)[e] = __ldg(reinterpret_cast<const uint4*>(keys + j * DK) + c);
+    }
 }
 
 // K0b: the keys' limb rows [L][3][128] (int8), written just before the
@@ -245,22 +266,6 @@ __device__ __forceinline__ uint64_t band_select(const uint64_t* keys, int64_t M,
     return band_select_fn<NT>([keys](int64_t i) { return keys[i]; }, M, k, sm);
 }
 
-struct BandArgs {
-    const float* scores;     // [T][L] approximate scores (tensor-core pass)
-    const uint8_t* q;        // [T][H][128] e4m3
-    const float* w;          // [T][H]
-    int32_t* cand;           // [T][CAP_C] candidate keys
-    int* cand_cnt;           // [T]
-    int* status;
-    int64_t T, L, pos0;
-    int H, k;
-};
-
-__device__ __forceinline__ void band_flag(const BandArgs& a, int64_t t) {
-    const int pos = atomicAdd(&a.status[ST_NFLAG], 1);
-    if (pos < a.T) a.status[ST_FLAGS + pos] = (int)t;
-}
-
 // Largest P = (24-bit prefix << 8) such that at least `need` (>= 1, <= M) of
 // the 32-bit keys key_at(0 .. M-1) are >= P: a floor of the need-th largest
 // key, three 8-bit histogram passes.  NT threads; sm >= 256 + NT/32 + 3.
@@ -296,33 +301,43 @@ __device__ __forceinline__ uint32_t key_floor(KeyAt key_at, int64_t M, int64_t n
     return prefix;
 }
 
-// One block per token.  Bounds: tol = E_t * max_j ||k_j|| (E_t = C_TOL *
-// ||u_t||), which is >= every key's C_TOL * ||u_t|| ||k_j||; lo_j = s~_j - tol,
-// hi_j = s~_j + tol, rounded outwards.
-//   1. tau: a floor of the r1-th largest lo of a strided sample, r1 chosen so
-//      that at least m keys have lo >= tau except with negligible probability
-//   2. one read of the row collects every key with hi >= tau (so every key
-//      with lo >= tau; a miss of the sample only costs the exact-row path)
-//   3. Lambda: a floor of the m-th largest lo among the collected keys (all
-//      keys with lo >= tau are there, at least m of them), so Lambda <= the
-//      exact k-th score
-//   4. candidates: the collected keys with hi_j >= Lambda
-__global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a) {
-    extern __shared__ uint64_t bsm[];
-    uint64_t* col = bsm;                                         // BAND_COLLECT: (s~ bits << 32) | j
-    uint32_t* samp = reinterpret_cast<uint32_t*>(bsm + BAND_COLLECT);   // BAND_SAMPLE lo keys
+struct TokArgs {
+    const uint8_t* q;        // [T][H][128] e4m3
+    const float* w;          // [T][H]
+    const float* norms;      // [L]
+    const float* sscores;    // [T][S] approximate scores of the sampled keys
+    const uint32_t* bitmap;  // [T][W]
+    float* tok_e;            // [T]
+    float* tok_tau;          // [T] the threshold as a float (-inf: every visible key)
+    int32_t* cand;           // [T][CAP_C] candidate keys
+    int* cand_cnt;           // [T]
+    int* status;
+    int64_t T, L, pos0;
+    int H, k, S, W;
+};
+
+__device__ __forceinline__ void band_flag(const TokArgs& a, int64_t t) {
+    const int pos = atomicAdd(&a.status[ST_NFLAG], 1);
+    if (pos < a.T) a.status[ST_FLAGS + pos] = (int)t;
+}
+
+// K2: one block per token: E_t = C_TOL * ||u_t||_2 rounded up, and tau.
+// Tokens that see at most CAP_C keys take all of them (tau = key 0).  The
+// others: the sample holds S_t visible keys; a key of the row reaches the
+// k-th with probability p = m / vis, so the sample holds Binomial(S_t, p)
+// such keys; tau = a floor of the (mean + 5 sd + 8)-th largest lo among them.
+__global__ void __launch_bounds__(BAND_THREADS) dsa_threshold_kernel(const TokArgs a) {
+    __shared__ uint32_t samp[BAND_SAMPLE];
     __shared__ unsigned sm[256 + BAND_THREADS / 32 + 4];
     __shared__ float ured[4][DK];
     __shared__ float nred[BAND_THREADS / 32];
-    __shared__ int cnt, cnt_lo, out_n, nan_seen;
+    __shared__ int nan_seen, st_cnt;
     __shared__ float e_t;
     const int64_t t = blockIdx.x;
     const int64_t vis = max((int64_t)0, min(a.L, a.pos0 + t + 1));
     const int m = (int)min((int64_t)a.k, vis);
-    int32_t* cand = a.cand + t * CAP_C;
-    if (threadIdx.x == 0) { cnt = 0; cnt_lo = 0; out_n = 0; nan_seen = 0; }
-
-    // E_t = C_TOL * ||u_t||_2 rounded up, u_t[d] = sum_h |w_h| |q_hd| (real units)
+    if (threadIdx.x == 0) { nan_seen = 0; st_cnt = 0; }
+    __syncthreads();
     {
         const uint8_t* qt = a.q + t * (int64_t)a.H * DK;
         const float* wt = a.w + t * a.H;
@@ -354,98 +369,80 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
             for (int i = 0; i < BAND_THREADS / 32; ++i) s2 = __fadd_ru(s2, nred[i]);
             e_t = __fmul_ru(__fsqrt_ru(s2), (float)C_TOL * (1.0f + 1.0f / 4096.0f));
             if (nan_seen) atomicOr(&a.status[ST_NAN], 1);
+            a.tok_e[t] = e_t;
         }
         __syncthreads();
     }
+    if (vis <= CAP_C || a.S == 0) {   // every visible key is a candidate
+        if (threadIdx.x == 0) a.tok_tau[t] = -INFINITY;
+        return;
+    }
     const float E = e_t;
+    // the visible sample keys: i with floor(i L / S) < vis, a prefix of the sample
+    const float* srow = a.sscores + t * a.S;
+    for (int i = threadIdx.x; i < a.S; i += BAND_THREADS) {
+        const int64_t j = (int64_t)i * a.L / a.S;
+        if (j < vis) {
+            atomicAdd(&st_cnt, 1);
+            samp[i] = f32_key(__fsub_rd(srow[i], __fmul_ru(E, a.norms[j])));
+        }
+    }
+    __syncthreads();
+    const int St = st_cnt;
+    const double p_k = (double)m / (double)vis;
+    const double mean_k = St * p_k;
+    const int64_t r1 = (int64_t)ceil(mean_k + 5.0 * sqrt(mean_k * (1.0 - p_k)) + 8.0);
+    if (r1 > St) {   // too few sample keys to place tau: take all (the row is then flagged)
+        if (threadIdx.x == 0) a.tok_tau[t] = -INFINITY;
+        return;
+    }
+    const uint32_t* sp = samp;
+    const uint32_t tk = key_floor<BAND_THREADS>([sp](int64_t i) { return sp[i]; }, St, r1, sm);
+    // the key floor as a float (keys at or below that of -inf mean no threshold)
+    if (threadIdx.x == 0) a.tok_tau[t] = tk <= 0x007fffffu ? -INFINITY : key_to_f32(tk);
+}
 
-    if (vis <= CAP_C) {   // short rows: every visible key is a candidate
+// K4: one block per token: the keys marked in the bitmap become its
+// candidates (all visible keys when the token sees at most CAP_C); if they do
+// not fit, the token is flagged for the exact-row path.
+__global__ void __launch_bounds__(BAND_THREADS) dsa_cand_kernel(const TokArgs a) {
+    __shared__ int out_n;
+    const int64_t t = blockIdx.x;
+    const int64_t vis = max((int64_t)0, min(a.L, a.pos0 + t + 1));
+    int32_t* cand = a.cand + t * CAP_C;
+    if (vis <= CAP_C) {
         for (int64_t j = threadIdx.x; j < vis; j += BAND_THREADS) cand[j] = (int32_t)j;
         if (threadIdx.x == 0) a.cand_cnt[t] = (int)vis;
         return;
     }
-    const float* row = a.scores + t * a.L;
-    // one tolerance for every key of the token: E_t * max_j ||k_j|| (>= tol_j)
-    const float tol = __fmul_ru(E, __int_as_float(a.status[ST_KMAX]));
-    auto lo_key = [tol](float s) { return f32_key(__fsub_rd(s, tol)); };
-    auto hi_key = [tol](float s) { return f32_key(__fadd_ru(s, tol)); };
-
-    // 1. tau from the sample: it holds Binomial(S, m / vis) keys whose lo
-    //    reaches the k-th; take the (mean + 5 sd + 8)-th largest
-#pragma unroll 8
-    for (int i = threadIdx.x; i < BAND_SAMPLE; i += BAND_THREADS)
-        samp[i] = lo_key(row[(int64_t)i * vis / BAND_SAMPLE]);
+    if (threadIdx.x == 0) out_n = 0;
     __syncthreads();
-    const double p_k = (double)m / (double)vis;
-    const double mean_k = BAND_SAMPLE * p_k;
-    const int64_t r1 = min((int64_t)BAND_SAMPLE,
-                           (int64_t)ceil(mean_k + 5.0 * sqrt(mean_k * (1.0 - p_k)) + 8.0));
-    const uint32_t tau = key_floor<BAND_THREADS>([samp](int64_t i) { return samp[i]; },
-                                                 BAND_SAMPLE, r1, sm);
-
-    // 2. one read of the row (each lane 4 consecutive scores; warp-uniform loop)
+    const uint32_t* row = a.bitmap + t * a.W;
+    const int nw = (int)((vis + 31) >> 5);
     const int lane = threadIdx.x & 31;
-    auto take = [&](float s, int64_t j, bool valid) {
-        const bool hit = valid && hi_key(s) >= tau;
-        const int pos = warp_append(hit, &cnt);
-        if (pos >= 0 && pos < BAND_COLLECT)
-            col[pos] = ((uint64_t)__float_as_uint(s) << 32) | (uint64_t)j;
-    };
-    if ((a.L & 3) == 0) {
-        const float4* row4 = reinterpret_cast<const float4*>(row);
-        const int64_t n4 = (vis + 3) >> 2;   // the last float4 may hold invisible (-inf) keys
-        // four float4 per lane in flight per step
-        for (int64_t b0 = threadIdx.x & ~31; b0 < n4; b0 += 4 * BAND_THREADS) {
-            float4 v[4];
+    for (int w0 = threadIdx.x & ~31; w0 < nw; w0 += BAND_THREADS) {
+        const int wi = w0 + lane;
+        uint32_t bits = wi < nw ? row[wi] : 0u;
+        if (wi == nw - 1 && (vis & 31)) bits &= (1u << (vis & 31)) - 1u;   // keys past vis
+        const int c = __popc(bits);
+        // one shared atomic per warp for the warp's candidates, in lane order
+        int incl = c;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int64_t i4 = b0 + u * BAND_THREADS + lane;
-                v[u] = i4 < n4 ? __ldg(row4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int64_t i4 = b0 + u * BAND_THREADS + lane;
-                take(v[u].x, 4 * i4 + 0, 4 * i4 + 0 < vis);
-                take(v[u].y, 4 * i4 + 1, 4 * i4 + 1 < vis);
-                take(v[u].z, 4 * i4 + 2, 4 * i4 + 2 < vis);
-                take(v[u].w, 4 * i4 + 3, 4 * i4 + 3 < vis);
-            }
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += u;
         }
-    } else {
-        for (int64_t j0 = threadIdx.x & ~31; j0 < vis; j0 += BAND_THREADS) {
-            const int64_t j = j0 + lane;
-            take(j < vis ? row[j] : 0.0f, j, j < vis);
+        const int tot = __shfl_sync(0xffffffffu, incl, 31);
+        int base = 0;
+        if (lane == 31 && tot) base = atomicAdd(&out_n, tot);
+        base = __shfl_sync(0xffffffffu, base, 31);
+        int pos = base + incl - c;
+        while (bits) {
+            const int b = __ffs(bits) - 1;
+            bits &= bits - 1;
+            if (pos < CAP_C) cand[pos] = wi * 32 + b;
+            ++pos;
         }
-    }
-    __syncthreads();
-    const int C = cnt;
-    if (C <= BAND_COLLECT)
-        for (int i0 = threadIdx.x & ~31; i0 < C; i0 += BAND_THREADS) {
-            const int i = i0 + lane;
-            bool hit = false;
-            if (i < C) hit = lo_key(__uint_as_float((uint32_t)(col[i] >> 32))) >= tau;
-            warp_append(hit, &cnt_lo);
-        }
-    __syncthreads();
-    if (C > BAND_COLLECT || cnt_lo < m) {   // the sample's threshold was off: exact row instead
-        if (threadIdx.x == 0) { band_flag(a, t); a.cand_cnt[t] = 0; }
-        return;
-    }
-    // 3. Lambda
-    const uint32_t lam = key_floor<BAND_THREADS>(
-        [&](int64_t i) { return lo_key(__uint_as_float((uint32_t)(col[i] >> 32))); }, C, m, sm);
-    // 4. the candidates
-    for (int i0 = threadIdx.x & ~31; i0 < C; i0 += BAND_THREADS) {
-        const int i = i0 + lane;
-        bool hit = false;
-        int64_t j = 0;
-        if (i < C) {
-            const uint64_t e = col[i];
-            j = (int64_t)(uint32_t)e;
-            hit = hi_key(__uint_as_float((uint32_t)(e >> 32))) >= lam;
-        }
-        const int pos = warp_append(hit, &out_n);
-        if (pos >= 0 && pos < CAP_C) cand[pos] = (int32_t)j;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -457,8 +454,6 @@ __global__ void __launch_bounds__(BAND_THREADS) dsa_band_kernel(const BandArgs a
         }
     }
 }
-
-constexpr size_t BAND_SMEM = sizeof(uint64_t) * BAND_COLLECT + sizeof(uint32_t) * BAND_SAMPLE;
 
 // ---------------------------------------------------------------------------
 // K3: exact scores of the candidates on the tensor cores.
@@ -899,12 +894,16 @@ __global__ void __launch_bounds__(R_THREADS, 1) dsa_rescore_kernel(const Rescore
 }
 
 // ---------------------------------------------------------------------------
-// K4: exact top-k of each token's candidates, best first, ties to the lowest
-// key; fewer visible keys than k pad with -1 / -inf.
+// K6: exact top-k of each token's candidates, best first, ties to the lowest
+// key; fewer visible keys than k pad with -1 / -inf.  Unless the candidates
+// are all the visible keys, the m-th best of them (m = min(k, visible)) must
+// reach the token's threshold (every other key scores below it); otherwise
+// the token is flagged for the exact-row path, which overwrites its outputs.
 __global__ void __launch_bounds__(SEL_THREADS) dsa_select_kernel(
     const int32_t* __restrict__ cand, const float* __restrict__ exact,
-    const int* __restrict__ cand_cnt, int64_t L, int64_t pos0, int k,
-    int32_t* __restrict__ out_idx, float* __restrict__ out_sc) {
+    const int* __restrict__ cand_cnt, const float* __restrict__ tok_tau, int64_t n_tok, int64_t L,
+    int64_t pos0, int k, int* __restrict__ status, int32_t* __restrict__ out_idx,
+    float* __restrict__ out_sc) {
     extern __shared__ uint64_t ssm[];
     uint64_t* keys = ssm;               // CAP_C
     uint64_t* best = ssm + CAP_C;       // KMAX
@@ -930,6 +929,13 @@ __global__ void __launch_bounds__(SEL_THREADS) dsa_select_kernel(
     }
     __syncthreads();
     block_bitonic_sort_desc(best, kp);
+    if (threadIdx.x == 0 && n < vis) {
+        const int m_req = (int)min((int64_t)k, vis);
+        if (n < m_req || !(cand_score(best[m_req - 1]) >= tok_tau[t])) {
+            const int pos = atomicAdd(&status[ST_NFLAG], 1);
+            if (pos < n_tok) status[ST_FLAGS + pos] = (int)t;
+        }
+    }
     for (int i = threadIdx.x; i < k; i += SEL_THREADS) {
         const uint64_t c = i < m ? best[i] : 0ull;
         out_idx[t * k + i] = c ? (int32_t)cand_row(c) : -1;
@@ -940,14 +946,14 @@ __global__ void __launch_bounds__(SEL_THREADS) dsa_select_kernel(
 constexpr size_t SEL_SMEM = sizeof(uint64_t) * (CAP_C + KMAX);
 
 // ---------------------------------------------------------------------------
-// Fallback: every visible key's exact score of each flagged token (blockIdx.y
-// picks the token from the flagged list), on CUDA cores, in the reference's
-// arithmetic (exact integer dots, fp32 head sum in order), written over the
-// token's row of approximate scores.
+// Fallback: every visible key's exact score of each flagged token of a pass
+// (blockIdx.y picks the token from the pass's part of the flagged list), on
+// CUDA cores, in the reference's arithmetic (exact integer dots, fp32 head
+// sum in order), into row blockIdx.y of `rows` ([FB_ROWS][L]).
 __global__ void dsa_exact_rows_kernel(const uint8_t* __restrict__ q, const float* __restrict__ w,
                                       const uint8_t* __restrict__ keys, int64_t L, int64_t pos0,
                                       int H, const int* __restrict__ flagged,
-                                      float* __restrict__ scores) {
+                                      float* __restrict__ rows) {
     __shared__ int qv[64 * DK];
     __shared__ float ws[64];
     const int64_t t = flagged[blockIdx.y];
@@ -955,7 +961,7 @@ __global__ void dsa_exact_rows_kernel(const uint8_t* __restrict__ q, const float
     for (int i = threadIdx.x; i < H * DK; i += blockDim.x) qv[i] = e4m3_scaled(qt[i]);
     for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = w[t * H + h];
     __syncthreads();
-    float* row = scores + t * L;
+    float* row = rows + (int64_t)blockIdx.y * L;
     const int64_t vis = max((int64_t)0, min(L, pos0 + t + 1));
     for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < vis;
          j += (int64_t)gridDim.x * blockDim.x) {
@@ -975,16 +981,16 @@ __global__ void dsa_exact_rows_kernel(const uint8_t* __restrict__ q, const float
 }
 
 // Fallback: the exact top-k of each flagged token's exact row (one block per
-// flagged token): a block radix select over the visible scores, then the k
-// best sorted, ties to the lowest key.
+// flagged token of the pass, its row in `rows`): a block radix select over
+// the visible scores, then the k best sorted, ties to the lowest key.
 __global__ void __launch_bounds__(SEL_THREADS) dsa_row_select_kernel(
-    const float* __restrict__ scores, int64_t L, int64_t pos0, int k,
+    const float* __restrict__ rows, int64_t L, int64_t pos0, int k,
     const int* __restrict__ flagged, int32_t* __restrict__ out_idx, float* __restrict__ out_sc) {
     extern __shared__ uint64_t fsm[];   // KMAX
     __shared__ unsigned sm[256 + SEL_THREADS / 32 + 4];
     __shared__ int nb;
     const int64_t t = flagged[blockIdx.x];
-    const float* row = scores + t * L;
+    const float* row = rows + (int64_t)blockIdx.x * L;
     const int64_t vis = max((int64_t)0, min(L, pos0 + t + 1));
     const int m = (int)min((int64_t)k, vis);
     auto key_at = [row](int64_t j) { return make_cand(f32_key(row[j]), (uint32_t)j); };
@@ -1013,64 +1019,107 @@ size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 }  // namespace
 
 // Workspace of the exact selection: status words and flagged tokens, key
-// limbs and norms, candidate lists and their exact scores.
+// norms, limbs and the sample, per-token thresholds and bitmaps, candidate
+// lists and their exact scores, and the fallback's exact rows.
 struct DsaExactLayout {
-    size_t status, limbs, cand, cand_cnt, exact, total;
+    size_t status, norms, limbs, skeys, sscores, tok_e, tok_tau, bitmap, cand,
+        cand_cnt, exact, rows, total;
+    int S, W;
 };
 
 static DsaExactLayout dsa_exact_layout(int64_t T, int64_t L) {
     DsaExactLayout d;
+    // the sample only matters for tokens that see more keys than CAP_C
+    d.S = L > CAP_C ? BAND_SAMPLE : 0;
+    d.W = (int)((L + 31) / 32);
     size_t o = 0;
     d.status = o; o += up256(sizeof(int) * (size_t)(ST_FLAGS + T));
+    d.norms = o; o += up256(sizeof(float) * (size_t)L);
     d.limbs = o; o += up256((size_t)L * NLIMB * DK);
+    d.skeys = o; o += up256((size_t)d.S * DK);
+    d.sscores = o; o += up256(sizeof(float) * (size_t)T * d.S);
+    d.tok_e = o; o += up256(sizeof(float) * (size_t)T);
+    d.tok_tau = o; o += up256(sizeof(float) * (size_t)T);
+    d.bitmap = o; o += up256(sizeof(uint32_t) * (size_t)T * d.W);
     d.cand = o; o += up256(sizeof(int32_t) * (size_t)T * CAP_C);
     d.cand_cnt = o; o += up256(sizeof(int) * (size_t)T);
     d.exact = o; o += up256(sizeof(float) * (size_t)T * CAP_C);
+    d.rows = o; o += up256(sizeof(float) * (size_t)FB_ROWS * L);
     d.total = o;
     return d;
 }
 
 size_t dsa_exact_ws_bytes(int64_t T, int64_t L) { return dsa_exact_layout(T, L).total; }
 
-// Clears the status words and prepares the key limbs and norms; runs before
-// the scoring pass so that its timeout flag lands in status[ST_TIMEOUT].
-hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, void* ws,
-                               cudaStream_t st, int** status_out) {
+static TokArgs tok_args(const uint8_t* q, const float* w, int64_t T, int64_t H, int64_t L,
+                        int64_t pos0, int64_t topk, const DsaExactBufs& b, unsigned char* wb,
+                        const DsaExactLayout& d) {
+    TokArgs a;
+    a.q = q; a.w = w; a.norms = b.norms; a.sscores = b.sscores; a.bitmap = b.bitmap;
+    a.tok_e = b.tok_e; a.tok_tau = b.tok_tau;
+    a.cand = reinterpret_cast<int32_t*>(wb + d.cand);
+    a.cand_cnt = reinterpret_cast<int*>(wb + d.cand_cnt);
+    a.status = b.status;
+    a.T = T; a.L = L; a.pos0 = pos0; a.H = (int)H; a.k = (int)topk; a.S = b.S; a.W = b.W;
+    return a;
+}
+
+hmm_status_t dsa_exact_prepare(const uint8_t* keys, int64_t T, int64_t L, int64_t topk,
+                               void* ws, cudaStream_t st, DsaExactBufs* b) {
+    (void)topk;
     const DsaExactLayout d = dsa_exact_layout(T, L);
     unsigned char* w = static_cast<unsigned char*>(ws);
-    int* status = reinterpret_cast<int*>(w + d.status);
-    *status_out = status;
-    HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int) * ST_FLAGS, st));
+    b->status = reinterpret_cast<int*>(w + d.status);
+    b->norms = reinterpret_cast<float*>(w + d.norms);
+    b->skeys = w + d.skeys;
+    b->sscores = reinterpret_cast<float*>(w + d.sscores);
+    b->tok_e = reinterpret_cast<float*>(w + d.tok_e);
+    b->tok_tau = reinterpret_cast<float*>(w + d.tok_tau);
+    b->bitmap = reinterpret_cast<uint32_t*>(w + d.bitmap);
+    b->S = d.S;
+    b->W = d.W;
+    HMM_CUDA_TRY(cudaMemsetAsync(b->status, 0, sizeof(int) * ST_FLAGS, st));
     if (L > 0) {
         const int64_t blocks = std::min<int64_t>((L + 7) / 8, 8 * (int64_t)device_sm_count());
-        dsa_key_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(keys, L, status);
-        return check_launch("dsa_key_prep_kernel");
+        dsa_key_prep_kernel<<<(unsigned)blocks, 256, 0, st>>>(keys, L, b->norms, b->status);
+        hmm_status_t s = check_launch("dsa_key_prep_kernel");
+        if (s != HMM_OK) return s;
+    }
+    if (d.S > 0) {
+        const int64_t n16 = (int64_t)d.S * (DK / 16);
+        dsa_sample_gather_kernel<<<(unsigned)((n16 + 255) / 256), 256, 0, st>>>(keys, L, d.S,
+                                                                                 b->skeys);
+        return check_launch("dsa_sample_gather_kernel");
     }
     return HMM_OK;
 }
 
-// Band, exact rescoring and selection of every token; then the host reads the
-// status words and recomputes flagged tokens from their exact rows.
+hmm_status_t dsa_exact_thresholds(const uint8_t* q, const float* w, int64_t T, int64_t H,
+                                  int64_t L, int64_t pos0, int64_t topk, const DsaExactBufs& b,
+                                  cudaStream_t st) {
+    const DsaExactLayout d = dsa_exact_layout(T, L);
+    unsigned char* wb = reinterpret_cast<unsigned char*>(b.status) - d.status;
+    const TokArgs a = tok_args(q, w, T, H, L, pos0, topk, b, wb, d);
+    dsa_threshold_kernel<<<(unsigned)T, BAND_THREADS, 0, st>>>(a);
+    return check_launch("dsa_threshold_kernel");
+}
+
 hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float* w, int64_t T,
                               int64_t H, int64_t L, int64_t pos0, int64_t topk,
-                              float* scores, int32_t* out_idx, float* out_sc, void* ws,
+                              const DsaExactBufs& b, int32_t* out_idx, float* out_sc, void* ws,
                               cudaStream_t st) {
     const DsaExactLayout d = dsa_exact_layout(T, L);
     unsigned char* wb = static_cast<unsigned char*>(ws);
-    int* status = reinterpret_cast<int*>(wb + d.status);
+    int* status = b.status;
     int32_t* cand = reinterpret_cast<int32_t*>(wb + d.cand);
     int* cand_cnt = reinterpret_cast<int*>(wb + d.cand_cnt);
     float* exact = reinterpret_cast<float*>(wb + d.exact);
+    float* rows = reinterpret_cast<float*>(wb + d.rows);
     hmm_status_t s;
 
-    BandArgs ba;
-    ba.scores = scores; ba.q = q; ba.w = w;
-    ba.cand = cand; ba.cand_cnt = cand_cnt; ba.status = status;
-    ba.T = T; ba.L = L; ba.pos0 = pos0; ba.H = (int)H; ba.k = (int)topk;
-    HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_band_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)BAND_SMEM));
-    dsa_band_kernel<<<(unsigned)T, BAND_THREADS, BAND_SMEM, st>>>(ba);
-    s = check_launch("dsa_band_kernel");
+    const TokArgs ta = tok_args(q, w, T, H, L, pos0, topk, b, wb, d);
+    dsa_cand_kernel<<<(unsigned)T, BAND_THREADS, 0, st>>>(ta);
+    s = check_launch("dsa_cand_kernel");
     if (s != HMM_OK) return s;
 
     // the key limbs, right before the gather that reads them
@@ -1085,7 +1134,6 @@ hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float
     ra.q = q; ra.w = w; ra.klimbs = wb + d.limbs; ra.cand = cand; ra.cand_cnt = cand_cnt;
     ra.exact = exact; ra.status = status; ra.T = T; ra.wait_ns = wait_limit_ns();
     const int grid = std::max(1, (int)std::min<int64_t>(device_sm_count(), T));
-    const ProfileMark pm = profile_begin(st);
     if (H == 64) {
         HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_rescore_kernel<64>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1103,13 +1151,12 @@ hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float
         dsa_rescore_kernel<16><<<grid, R_THREADS, RescoreSmem<16>::BYTES, st>>>(ra);
     }
     s = check_launch("dsa_rescore_kernel");
-    profile_end(pm, st);
     if (s != HMM_OK) return s;
 
     HMM_CUDA_TRY(cudaFuncSetAttribute(dsa_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)SEL_SMEM));
-    dsa_select_kernel<<<(unsigned)T, SEL_THREADS, SEL_SMEM, st>>>(cand, exact, cand_cnt, L, pos0,
-                                                                  (int)topk, out_idx, out_sc);
+    dsa_select_kernel<<<(unsigned)T, SEL_THREADS, SEL_SMEM, st>>>(
+        cand, exact, cand_cnt, b.tok_tau, T, L, pos0, (int)topk, status, out_idx, out_sc);
     s = check_launch("dsa_select_kernel");
     if (s != HMM_OK) return s;
 
@@ -1124,17 +1171,20 @@ hmm_status_t dsa_exact_select(const uint8_t* q, const uint8_t* keys, const float
                          "q or keys hold an e4m3 NaN encoding (0x7f / 0xff), which has no "
                          "exact score");
     const int nflag = (int)std::min<int64_t>(h[ST_NFLAG], T);
-    if (nflag > 0) {   // tokens whose band did not fit: exact rows, then their top-k
-        const int* flagged = status + ST_FLAGS;
-        const int bx = (int)std::max<int64_t>(1, std::min<int64_t>((L + 127) / 128,
-                                                                   2 * device_sm_count()));
-        dsa_exact_rows_kernel<<<dim3(bx, nflag), 128, 0, st>>>(q, w, keys, L, pos0, (int)H,
-                                                              flagged, scores);
+    // tokens whose candidates did not fit: exact rows, then their top-k, FB_ROWS
+    // tokens per pass through the rows buffer
+    const int bx = (int)std::max<int64_t>(1, std::min<int64_t>((L + 127) / 128,
+                                                               2 * device_sm_count()));
+    for (int f0 = 0; f0 < nflag; f0 += FB_ROWS) {
+        const int nf = std::min(FB_ROWS, nflag - f0);
+        const int* flagged = status + ST_FLAGS + f0;
+        dsa_exact_rows_kernel<<<dim3(bx, nf), 128, 0, st>>>(q, w, keys, L, pos0, (int)H, flagged,
+                                                           rows);
         s = check_launch("dsa_exact_rows_kernel");
         if (s != HMM_OK) return s;
         const size_t fsm = sizeof(uint64_t) * KMAX;
-        dsa_row_select_kernel<<<nflag, SEL_THREADS, fsm, st>>>(scores, L, pos0, (int)topk,
-                                                               flagged, out_idx, out_sc);
+        dsa_row_select_kernel<<<nf, SEL_THREADS, fsm, st>>>(rows, L, pos0, (int)topk, flagged,
+                                                           out_idx, out_sc);
         s = check_launch("dsa_row_select_kernel");
         if (s != HMM_OK) return s;
     }
