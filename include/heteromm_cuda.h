@@ -416,14 +416,15 @@ hmm_status_t hmm_seer_threshold_i16(const int16_t* past, int64_t L, const int16_
  *   q [T][H][128] e4m3, keys [L][128] e4m3, w [T][H] fp32 (16-byte aligned),
  *   H in {16, 32, 64}, topk <= 4096, pos0 >= -1.
  *   out_idx [T][topk] int32; out_scores [T][topk] fp32 or NULL;
- *   all_scores [T][L] fp32 or NULL: every score (-inf where not visible),
- *   kept in the caller's buffer instead of the workspace.
- * The q . k products are exact (e4m3 x e4m3 fits fp32); their sum is the
- * tensor core's fp32 accumulation and the head sum is fp32 FMA, so scores
- * match the exact value to within the accumulation rounding, and selections
- * differ from the exact ranking only among keys whose exact scores are that
- * close to the k-th.  Waits for `stream`; HMM_ERR_TIMEOUT if a bounded
- * device wait gave up. */
+ *   all_scores [T][L] fp32 or NULL: the tensor-core pass's approximate score
+ *   of every key (-inf where not visible), for inspection.
+ * The selection and out_scores are the reference's exactly: exact integer
+ * dots, (float) ReLU, fp32 head sum in head order.  Tensor cores score every
+ * key approximately, and the keys whose approximate score could reach a
+ * token's k-th are rescored exactly; a token whose candidates do not settle
+ * its top-k is recomputed from its exact row.  The workspace holds no
+ * [T][L] score matrix.  Waits for `stream`; HMM_ERR_TIMEOUT if a bounded
+ * device wait gave up; HMM_ERR_INVALID for e4m3 NaN encodings in q or keys. */
 size_t hmm_dsa_indexer_fp8_workspace_size(int64_t T, int64_t H, int64_t L, int64_t topk);
 hmm_status_t hmm_dsa_indexer_fp8(const uint8_t* q, const uint8_t* keys, const float* w,
                                  int64_t T, int64_t H, int64_t L, int64_t D, int64_t pos0,
