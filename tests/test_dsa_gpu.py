@@ -111,6 +111,27 @@ def test_dsa_duplicate_keys_take_the_exact_row_path(cuda):
     check_exact(cuda, q, k, w, L - T, topk)
 
 
+def test_dsa_biased_sample_takes_the_exact_row_path(cuda):
+    """Only the sampled keys (j = floor(i L / 4096)) carry the strong component
+    that every query shares: the threshold taken from the sample then sits near
+    the sample's top, fewer than k keys of the row reach it, the check on the
+    rescored candidates fails and every token is recomputed from its exact row
+    (two more launches), still equal to the oracle."""
+    from heteromm_b200 import _abi
+    T, H, L, topk = 8, 64, 20000, 256
+    x = gen.normal_f32(1901, (T, H, 128)) * 60.0
+    x[..., 0] = 448.0
+    y = gen.normal_f32(1902, (L, 128)) * 60.0
+    y[:, 0] = 0.0
+    y[(np.arange(4096) * L) // 4096, 0] = 448.0
+    q, k = gen.e4m3_bits(x), gen.e4m3_bits(y)
+    w = gen.uniform01_f32(1903, (T, H))
+    check_exact(cuda, q, k, w, L - T, topk)        # warm: one-time kernel attributes
+    l0 = _abi.kernel_launches()
+    check_exact(cuda, q, k, w, L - T, topk)
+    assert _abi.kernel_launches() - l0 == 12       # 10 + the exact rows and their top-k
+
+
 def test_dsa_identical_keys(cuda):
     T, H, L, topk = 5, 64, 9000, 64
     q, kd, w = inputs(980, T, H, 1)
