@@ -574,6 +574,125 @@ hmm_status_t prepare_small_kernel() {
     return HMM_OK;
 }
 
+// Few queries (at most NARROW_NQ) over many rows: one CTA per tile of
+// NARROW_NT rows, thread = row.  Columns come into shared memory NARROW_KC at a
+// time by 16-byte cp.async copies, double buffered so that the next chunk's
+// copies are in flight while the current one is summed (rows padded by 16
+// bytes: a quarter-warp's 16-byte reads hit distinct banks).  Each thread
+// extends its row's sum for every query in column order, exactly as the fused
+// kernel does; then the threshold-bitmap words come from warp ballots and one
+// bitonic sort per query gives the tile's best k as candidates for the same
+// merge the fused kernel feeds.  The fused kernel's 16-query register tiles
+// would compute 16 query slots for one query.
+constexpr int NARROW_NQ = 4;
+constexpr int NARROW_NT = 256;
+constexpr int NARROW_KC = 32;   // columns per staged chunk
+
+template <typename T>
+__host__ __device__ constexpr int narrow_ld() { return NARROW_KC + 16 / (int)sizeof(T); }
+
+template <typename In>
+size_t narrow_smem_bytes(int64_t dim) {
+    return sizeof(float) * (size_t)NARROW_NQ * (size_t)((dim + 3) & ~int64_t(3)) +
+           sizeof(uint64_t) * NARROW_NQ * NARROW_NT +
+           2 * sizeof(typename In::T) * NARROW_NT * narrow_ld<typename In::T>();
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <typename In>
+__global__ void __launch_bounds__(NARROW_NT)
+narrow_ip_topk_kernel(const typename In::T* __restrict__ mem, int64_t n, int dim,
+                      const typename In::T* __restrict__ qry, int nq, int k, float thr,
+                      uint32_t* __restrict__ bitmap32, uint64_t* __restrict__ cand, bool vec_ok) {
+    using T = typename In::T;
+    constexpr int LDT = narrow_ld<T>();
+    extern __shared__ __align__(16) unsigned char nsm[];
+    const int dimp = (dim + 3) & ~3;
+    float* sq = reinterpret_cast<float*>(nsm);                                   // [NQ][dimp]
+    uint64_t* keys = reinterpret_cast<uint64_t*>(sq + NARROW_NQ * dimp);         // [NQ][NT]
+    T* buf = reinterpret_cast<T*>(keys + NARROW_NQ * NARROW_NT);                // 2 x [NT][LDT]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int part = blockIdx.x;
+    const int64_t row0 = (int64_t)part * NARROW_NT;
+    const int64_t row = row0 + tid;
+    const int rows = (int)min((int64_t)NARROW_NT, n - row0);
+    for (int i = tid; i < NARROW_NQ * dimp; i += NARROW_NT) {
+        const int q = i / dimp, j = i % dimp;
+        sq[i] = (q < nq && j < dim) ? In::widen1(qry + (int64_t)q * dim + j) : 0.0f;
+    }
+    const int nch = (dim + NARROW_KC - 1) / NARROW_KC;
+    // stage chunk c of the tile's rows into buffer b (rows past the end are
+    // not copied; their sums are never used)
+    auto stage = [&](int c, int b) {
+        const int c0 = c * NARROW_KC, w = min(NARROW_KC, dim - c0);
+        T* dst = buf + b * NARROW_NT * LDT;
+        if (vec_ok) {   // dim % VEC == 0 and 16-byte aligned rows, so w % VEC == 0
+            const int per_row = w / In::VEC;
+            for (int idx = tid; idx < rows * per_row; idx += NARROW_NT) {
+                const int r = idx / per_row, v = (idx - r * per_row) * In::VEC;
+                cp_async16(dst + r * LDT + v, mem + (row0 + r) * dim + c0 + v);
+            }
+        } else {
+            for (int idx = tid; idx < rows * w; idx += NARROW_NT) {
+                const int r = idx / w, j = idx - r * w;
+                dst[r * LDT + j] = mem[(row0 + r) * dim + c0 + j];
+            }
+        }
+        cp_async_commit();
+    };
+    float acc[NARROW_NQ];
+#pragma unroll
+    for (int q = 0; q < NARROW_NQ; ++q) acc[q] = 0.0f;
+    stage(0, 0);
+    for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch) {
+            stage(c + 1, (c + 1) & 1);
+            cp_async_wait_group<1>();   // chunk c has landed (c + 1 may be in flight)
+        } else {
+            cp_async_wait_group<0>();
+        }
+        __syncthreads();
+        const int c0 = c * NARROW_KC, w = min(NARROW_KC, dim - c0);
+        const T* t = buf + (c & 1) * NARROW_NT * LDT + tid * LDT;
+        for (int j = 0; j < w; ++j) {
+            const float a = In::widen1(t + j);
+#pragma unroll
+            for (int q = 0; q < NARROW_NQ; ++q)
+                if (q < nq) acc[q] = In::mac(acc[q], a, sq[q * dimp + c0 + j]);
+        }
+        __syncthreads();   // buffer (c & 1) is restaged by the next iteration but one
+    }
+    const bool valid = row < n;
+    const int64_t words32 = 2 * ((n + 63) / 64);
+#pragma unroll
+    for (int q = 0; q < NARROW_NQ; ++q) {
+        if (q >= nq) break;
+        if (bitmap32) {
+            const unsigned bits = __ballot_sync(0xffffffffu, valid && acc[q] >= thr);
+            const int64_t w32 = (row0 >> 5) + warp;
+            if (lane == 0 && w32 < words32) bitmap32[(int64_t)q * words32 + w32] = bits;
+        }
+        keys[q * NARROW_NT + tid] = valid ? make_cand(f32_key(acc[q]), (uint32_t)row) : 0ull;
+    }
+    const int n_parts = gridDim.x;
+    for (int q = 0; q < nq; ++q) {
+        block_bitonic_sort_desc(keys + q * NARROW_NT, NARROW_NT);   // synchronises before and after
+        uint64_t* dst = cand + ((int64_t)q * n_parts + part) * k;
+        for (int i = tid; i < k; i += NARROW_NT) dst[i] = keys[q * NARROW_NT + i];
+    }
+}
+
+// The narrow kernel applies to few queries over more rows than the small kernel
+// takes, with k within one tile.
+bool narrow_applies(int64_t n, int64_t nq, int64_t k) {
+    return nq >= 1 && nq <= NARROW_NQ && n > SMALL_N && k <= NARROW_NT;
+}
+
 template <typename In, typename IdxT>
 hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const typename In::T* qry,
                        int64_t nq, int64_t k, int64_t row_offset, IdxT* out_idx,
@@ -595,13 +714,25 @@ hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const 
             reinterpret_cast<uint32_t*>(out_bitmap), full_scores, out_idx, out_scores, vec_ok);
         return check_launch("small_ip_topk_kernel");
     }
-    const Plan p = plan_fused(n, nq);
+    Plan p = plan_fused(n, nq);
     uint64_t* cand = static_cast<uint64_t*>(ws);
-    const size_t smem = fused_smem_bytes((int)dim);
-    auto kern = fused_ip_topk_kernel<In>;
-    HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid(p.n_parts, p.n_qgroups);
-    if (n > 0) {
+    if (!full_scores && narrow_applies(n, nq, k)) {
+        p.n_parts = (int)((n + NARROW_NT - 1) / NARROW_NT);
+        const size_t smem = narrow_smem_bytes<In>(dim);
+        auto kern = narrow_ip_topk_kernel<In>;
+        HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+        kern<<<(unsigned)p.n_parts, NARROW_NT, smem, st>>>(
+            mem, n, (int)dim, qry, (int)nq, (int)k, thr, reinterpret_cast<uint32_t*>(out_bitmap),
+            cand, vec_ok);
+        hmm_status_t s = check_launch("narrow_ip_topk_kernel");
+        if (s != HMM_OK) return s;
+    } else if (n > 0) {
+        const size_t smem = fused_smem_bytes((int)dim);
+        auto kern = fused_ip_topk_kernel<In>;
+        HMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+        dim3 grid(p.n_parts, p.n_qgroups);
         kern<<<grid, NT, smem, st>>>(mem, n, (int)dim, qry, (int)nq, (int)k, p.rows_per_part, thr,
                                      reinterpret_cast<uint32_t*>(out_bitmap), full_scores, cand,
                                      vec_ok);
@@ -632,7 +763,9 @@ hmm_status_t run_fused(const typename In::T* mem, int64_t n, int64_t dim, const 
 }
 
 size_t fused_ws_bytes(int64_t n, int64_t nq, int64_t k) {
-    const Plan p = plan_fused(n, nq);
+    Plan p = plan_fused(n, nq);
+    if (narrow_applies(n, nq, k))   // the narrow kernel's tiles are the parts
+        p.n_parts = (int)std::max<int64_t>(p.n_parts, (n + NARROW_NT - 1) / NARROW_NT);
     size_t b = sizeof(uint64_t) * (size_t)nq * (size_t)p.n_parts * (size_t)k;
     if ((int64_t)p.n_parts * k > MERGE_ONE_CTA)   // the first merge level's output
         b += sizeof(uint64_t) * (size_t)nq * (size_t)((p.n_parts + MERGE_GROUP - 1) / MERGE_GROUP) *
