@@ -561,8 +561,10 @@ def run_flat_f32(args, rank, world, local):
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / pk["hbm_gbs"], "traffic": None,
-                         "kernel": "fused_ip_topk_kernel<F32In> + merge_candidates_kernel "
-                                   "(the whole call, timed by events around it)",
+                         "kernel": ("narrow_ip_topk_kernel<F32In>" if nq <= 4 else
+                                    "fused_ip_topk_kernel<F32In>") +
+                                   " + the candidate merge (the whole call, timed by events "
+                                   "around it)",
                          "kernel_ms": ms, "peak_kind": f"{pk_kind} copy bandwidth",
                          "issue": {"achieved_ginstr_s": instr / (ms * 1e-3) / 1e9,
                                    "peak_ginstr_s": issue_peak / 1e9,
