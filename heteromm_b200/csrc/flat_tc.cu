@@ -19,8 +19,13 @@
 // never exceeds the k-th best of the whole memory, so no true top-k row is
 // ever dropped).  A final merge takes the exact top-k of each pool.
 //
-// The threshold is seeded with the exact top-k of the first SEED_ROWS rows
-// (CUDA-core kernel of flat_topk.cu), so the first tiles already filter.
+// The starting threshold comes from a short sample pass of the same kernel
+// over SAMPLE_TPC tiles per cluster spread over the shard: each epilogue
+// thread keeps the SAMPLE_M largest lower bounds s~ - margin of its query, and
+// the k-th largest of them all (distinct rows, each bound <= its row's exact
+// score) is <= the shard's k-th best score.  The scoring pass then covers
+// every row with empty pools, and its first tiles already filter as tightly
+// as the k-th best of the sample allows.
 //
 // The queries are the MMA's M side and the rows its N side, so each epilogue
 // thread owns one query and compares its scores against one threshold held in
@@ -40,7 +45,7 @@
 
 namespace hmm {
 
-// from flat_topk.cu: the exact CUDA-core path (seed sample and small shards)
+// from flat_topk.cu: the exact CUDA-core path (small shards, full pools)
 hmm_status_t flat_bf16_exact(const uint16_t* mem, int64_t n, int64_t dim, const uint16_t* qry,
                              int64_t nq, int64_t k, int64_t row_offset, int64_t* out_idx,
                              float* out_scores, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -71,10 +76,13 @@ constexpr int N_RESCORERS = 4;                  // warps 2, 3, 6 and 7 (warp 3 o
 constexpr int RPR_MAX = 3;                      // rings per rescorer: 8 over 3 or 4 of them
 constexpr int TMEM_COLS = 512;                  // two accumulators of 256 fp32 columns
 constexpr float EPS = 1.0f / 1024.0f;          // >= 25x the worst-case summation gap
-#ifndef HMM_SEED_ROWS
-#define HMM_SEED_ROWS 8192
+constexpr int TC_MIN_ROWS = 8192;              // smaller shards take the exact CUDA-core path
+#ifndef HMM_SAMPLE_TPC
+#define HMM_SAMPLE_TPC 4
 #endif
-constexpr int SEED_ROWS = HMM_SEED_ROWS;
+constexpr int SAMPLE_TPC = HMM_SAMPLE_TPC;      // sample-pass pair tiles per cluster
+constexpr int SAMPLE_M = 4;                     // lower bounds kept per (query, CTA)
+constexpr int MAX_CTAS = 512;                   // grid bound (sample_lb sizing)
 constexpr int POOL_CAP = 8192;
 constexpr int KMAX_TC = 128;
 #ifndef HMM_RAISE_STEP
@@ -119,6 +127,8 @@ struct TcArgs {
     int64_t n_rows;
     int64_t row_begin;
     int n_tiles;             // 256-row pair tiles over [row_begin, n_rows)
+    int sample_tiles;        // sample pass only: tiles spread evenly over the n_tiles
+    uint64_t* sample_lb;     // sample pass only: [nq][gridDim.x * SAMPLE_M] lower-bound keys
     int nq;
     int k;
     int pool_cap;
@@ -163,6 +173,29 @@ __device__ __forceinline__ float exact_dot_rows(const uint16_t* __restrict__ row
         s = fmaf(bf_lo(a.y), bf_lo(b.y), s); s = fmaf(bf_hi(a.y), bf_hi(b.y), s);
         s = fmaf(bf_lo(a.z), bf_lo(b.z), s); s = fmaf(bf_hi(a.z), bf_hi(b.z), s);
         s = fmaf(bf_lo(a.w), bf_lo(b.w), s); s = fmaf(bf_hi(a.w), bf_hi(b.w), s);
+    }
+    return s;
+}
+
+// The same dot product with the query read from the CTA's staged MMA operand
+// (query ql of the CTA: two 64-column boxes of 128 queries, 128-byte rows,
+// 16-byte chunk c of row ql at chunk position c ^ (ql & 7)); only the row
+// comes from global memory, so all of its 16 loads are in flight together.
+__device__ __forceinline__ float exact_dot_staged_q(const uint16_t* __restrict__ row,
+                                                    const unsigned char* Qs, int ql) {
+    uint4 a[16];
+    const uint4* rp = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) a[c] = __ldg(rp + c);
+    float s = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const uint4 b = *reinterpret_cast<const uint4*>(Qs + (c >> 3) * Q_BOX + ql * 128 +
+                                                        (((c & 7) ^ (ql & 7)) << 4));
+        s = fmaf(bf_lo(a[c].x), bf_lo(b.x), s); s = fmaf(bf_hi(a[c].x), bf_hi(b.x), s);
+        s = fmaf(bf_lo(a[c].y), bf_lo(b.y), s); s = fmaf(bf_hi(a[c].y), bf_hi(b.y), s);
+        s = fmaf(bf_lo(a[c].z), bf_lo(b.z), s); s = fmaf(bf_hi(a[c].z), bf_hi(b.z), s);
+        s = fmaf(bf_lo(a[c].w), bf_lo(b.w), s); s = fmaf(bf_hi(a[c].w), bf_hi(b.w), s);
     }
     return s;
 }
@@ -230,18 +263,90 @@ __device__ __forceinline__ void set_abort(Ctrl* ctl, int* status, uint32_t peer)
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 __device__ __forceinline__ void st_volatile(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
 
+// k-th best of M <= RAISE_WINDOW pool keys (one warp), as the radix select of
+// warp_select_threshold but over keys loaded into registers once: all of a
+// lane's loads are in flight together (L2, bypassing L1, so that entries other
+// SMs appended since an earlier read are seen), and the byte passes then touch
+// only registers and the shared histogram.  Slots reserved but not yet
+// written read as 0, below every real key: the result can only be lower, so it
+// stays a lower bound of the window's k-th best.  Returns 0 for k >= M.
+__device__ __forceinline__ uint64_t warp_kth_window(const uint64_t* __restrict__ keys, int M,
+                                                    int k, unsigned* hist) {
+    constexpr int PER_LANE = RAISE_WINDOW / 32;
+    const int lane = threadIdx.x & 31;
+    if (k >= M) return 0ull;
+    uint64_t r[PER_LANE];
+#pragma unroll
+    for (int j = 0; j < PER_LANE; ++j) {
+        const int i = lane + 32 * j;
+        r[j] = i < M ? __ldcg(keys + i) : 0ull;
+    }
+    uint64_t prefix = 0, mask = 0;
+    unsigned need = (unsigned)k;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < PER_LANE; ++j)
+            if ((r[j] & mask) == prefix) atomicAdd(&hist[(r[j] >> shift) & 255], 1u);
+        __syncwarp();
+        // lane l owns bins 255-8l down to 248-8l (descending key order)
+        unsigned c[8], s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * lane - j]; s += c[j]; }
+        unsigned incl = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const unsigned excl = incl - s;
+        const unsigned ball = __ballot_sync(0xffffffffu, excl < need && need <= incl);
+        const int src = __ffs(ball) - 1;
+        unsigned bucket = 0, before = 0, cnt = 0;
+        if (lane == src) {
+            unsigned acc = excl;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (cnt == 0 && acc + c[j] >= need) {
+                    bucket = 255 - 8 * lane - j; before = acc; cnt = c[j];
+                }
+                acc += c[j];
+            }
+        }
+        bucket = __shfl_sync(0xffffffffu, bucket, src);
+        before = __shfl_sync(0xffffffffu, before, src);
+        cnt = __shfl_sync(0xffffffffu, cnt, src);
+        need -= before;
+        prefix |= (uint64_t)bucket << shift;
+        mask |= (uint64_t)0xff << shift;
+        __syncwarp();
+        // every key of this bucket is among the k best: the bucket's prefix
+        // (lower bytes 0) is <= the k-th best and exactly k keys exceed it
+        if (cnt == need) break;
+    }
+    return prefix;
+}
+static_assert(RAISE_WINDOW % 32 == 0 && RAISE_WINDOW <= 1024, "window keys held in registers");
+
 // Rescores one batch of up to 32 queued pairs exactly (lane = pair) and
 // appends the ones that beat their query's threshold to the pools; raises
 // thresholds at fill marks from the newest RAISE_WINDOW pool entries.
+// The pairs are the CTA's own queries (q0 .. q0 + 127), read from its staged
+// query operand Qs.
 __device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned* hist, uint64_t e, bool valid,
-                                           int m, const TcArgs& a) {
+                                           int m, const TcArgs& a, const unsigned char* Qs,
+                                           int q0) {
     const int lane = threadIdx.x & 31;
     if (lane == 0) atomicAdd(&a.status[2], m);
     int q = 0, raise = 0;
     const int64_t row = (int64_t)(e >> 8);
     if (valid && row < a.n_rows && (int)(e & 255u) < a.nq) {
         q = (int)(e & 255u);
-        const float s = exact_dot_rows(a.mem + row * TC_DIM, a.qry + (int64_t)q * TC_DIM);
+        const int ql = q - q0;
+        const float s = (unsigned)ql < (unsigned)PQ
+                            ? exact_dot_staged_q(a.mem + row * TC_DIM, Qs, ql)
+                            : exact_dot_rows(a.mem + row * TC_DIM, a.qry + (int64_t)q * TC_DIM);
         const uint64_t E = make_cand(f32_key(s), (uint32_t)row);
         if (E > ctl->tau[q]) {
             const int pos = atomicAdd(&a.pool_cnt[q], 1);
@@ -261,8 +366,8 @@ __device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned* hist, uint64_t e
         const int W = __shfl_sync(0xffffffffu, raise, src);
         const int qq = __shfl_sync(0xffffffffu, q, src);
         const uint64_t T =
-            warp_select_threshold(a.pool + (int64_t)qq * a.pool_cap + (W > RAISE_WINDOW ? W - RAISE_WINDOW : 0),
-                                  W > RAISE_WINDOW ? RAISE_WINDOW : W, a.k, hist);
+            warp_kth_window(a.pool + (int64_t)qq * a.pool_cap + (W > RAISE_WINDOW ? W - RAISE_WINDOW : 0),
+                            W > RAISE_WINDOW ? RAISE_WINDOW : W, a.k, hist);
         if (lane == 0) atomicAdd(&a.status[3], 1);
         if (lane == 0 && T != 0ull) {
             atomicMax(reinterpret_cast<unsigned long long*>(&a.tau_global[qq]),
@@ -304,6 +409,15 @@ __device__ __noinline__ void rescore_batch(Ctrl* ctl, unsigned* hist, uint64_t e
 // s >= score(t); |s~ - s| <= EPS * max_j|a_rj| * sum_j|b_qj| <= EPS * M_h * L1_q
 // (M_h = max over the tile half's rows), so the epilogue passes every pair
 // with s~ >= score(t) - EPS * M_h * L1_q (rounded down); NaN passes.
+//
+// SAMPLE = true is the sample pass that precedes the scoring pass: the same
+// pipeline over sample_tiles pair tiles spread evenly over the shard, with no
+// rescoring.  Each epilogue thread keeps the SAMPLE_M largest lower bounds
+// s~ - EPS * M_h * L1_q (rounded down) of its query over the rows it sees
+// and writes them to sample_lb; every bound is <= the exact score of a
+// distinct row, so the k-th largest of all of them is <= the k-th best exact
+// score of the shard (sample_tau_kernel turns it into the starting threshold).
+template <bool SAMPLE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
                        const __grid_constant__ CUtensorMap tmQ, const TcArgs a) {
@@ -320,7 +434,14 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
     const uint32_t crank = cluster_ctarank();   // 0: issues the pair's MMAs
     const uint32_t peer = crank ^ 1u;
     const int cl = (int)blockIdx.x >> 1, ncl = (int)gridDim.x >> 1;
-    const int my_tiles = cl < a.n_tiles ? (a.n_tiles - 1 - cl) / ncl + 1 : 0;
+    const int v_tiles = SAMPLE ? a.sample_tiles : a.n_tiles;
+    const int my_tiles = cl < v_tiles ? (v_tiles - 1 - cl) / ncl + 1 : 0;
+    // pair tile of this cluster's i-th iteration (the sample pass spreads its
+    // tiles evenly over the shard)
+    auto tile_of = [&](int i) -> int64_t {
+        const int j = cl + i * ncl;
+        return SAMPLE ? (int64_t)j * a.n_tiles / a.sample_tiles : (int64_t)j;
+    };
     const int q0 = (int)crank * PQ;             // this CTA's first query
     volatile int* abort = &ctl->abort;
 
@@ -376,7 +497,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
                 break;
             }
             if (lane == 0) {
-                const int y = (int)(a.row_begin + ((int64_t)(cl + i * ncl) * 2 + crank) * PR);
+                const int y = (int)(a.row_begin + (tile_of(i) * 2 + crank) * PR);
                 mbar_expect_tx(&ctl->full[s], ROW_STAGE);
                 tma_load_2d(Rs + s * ROW_STAGE, &tmR, &ctl->full[s], 0, y);
                 tma_load_2d(Rs + s * ROW_STAGE + ROW_BOX, &tmR, &ctl->full[s], 64, y);
@@ -517,10 +638,87 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
                     l1 = __fadd_ru(__fadd_ru(l1, fabsf(bf_lo(w[t]))), fabsf(bf_hi(w[t])));
             }
         }
+        if constexpr (SAMPLE) {
+            // the SAMPLE_M largest lower bounds of this query over the rows of
+            // this cluster's sample tiles in row half hh, in descending order
+            float lbs[SAMPLE_M];
+#pragma unroll
+            for (int j = 0; j < SAMPLE_M; ++j) lbs[j] = -INFINITY;
+            for (int i = 0; i < my_tiles; ++i) {
+                const int b = i & 1, e = i % MR_RING;
+                if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort, a.wait_ns)) {
+                    if (lane == 0) set_abort(ctl, a.status, peer);
+                    break;
+                }
+                tc_fence_after();
+                if (ew == 0 && lane == 0) mbar_arrive(&ctl->empty[i % STAGES]);
+                uint64_t v0 = 0, v1 = 0;
+                {
+                    const uint32_t tag = (uint32_t)(i + 1);
+                    const volatile uint64_t* sl = &ctl->mr[e][hh][0];
+                    bool ready = false;
+                    uint64_t t0 = 0;
+                    for (int it = 0;; ++it) {
+                        if (lane == 0) { v0 = sl[0]; v1 = sl[1]; }
+                        v0 = __shfl_sync(0xffffffffu, v0, 0);
+                        v1 = __shfl_sync(0xffffffffu, v1, 0);
+                        if ((uint32_t)(v0 >> 32) == tag && (uint32_t)(v1 >> 32) == tag) { ready = true; break; }
+                        if (it == 0) t0 = globaltimer_ns();
+                        if (*abort || globaltimer_ns() - t0 >= a.wait_ns) break;
+                        __nanosleep(32);
+                    }
+                    if (!ready) {
+                        if (lane == 0) set_abort(ctl, a.status, peer);
+                        break;
+                    }
+                }
+                const float mh = fmaxf(__uint_as_float((uint32_t)v0), __uint_as_float((uint32_t)v1));
+                const float marg = __fmul_ru(EPS, __fmul_ru(mh, l1));
+                // |partial sums| <= M_h * L1_q <= 2^110: neither order overflows,
+                // so the error bound holds (a larger or NaN bound is skipped)
+                const bool use = qvalid && marg <= 0x1p100f;
+                const uint32_t tbase =
+                    tmem + (uint32_t)(b * 2 * PR + hh * PR) + ((uint32_t)(sub * 32) << 16);
+                const int64_t half_row0 = a.row_begin + (tile_of(i) * 2 + hh) * PR;
+#pragma unroll 1
+                for (int c = 0; c < PR / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_x32(tbase + (uint32_t)(c * 32), v);
+                    tmem_wait_ld();
+                    const int64_t rem = a.n_rows - (half_row0 + c * 32);   // rows past the end
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float sv = __uint_as_float(v[j]);
+                        if (use && j < rem && fabsf(sv) <= 3.0e38f) {
+                            const float lb = __fsub_rd(sv, marg);
+                            if (lb > lbs[SAMPLE_M - 1]) {
+                                lbs[SAMPLE_M - 1] = lb;
+#pragma unroll
+                                for (int t = SAMPLE_M - 1; t > 0; --t)
+                                    if (lbs[t] > lbs[t - 1]) {
+                                        const float x = lbs[t]; lbs[t] = lbs[t - 1]; lbs[t - 1] = x;
+                                    }
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&ctl->acc_empty[b]), 0));
+            }
+            // written whatever happened: the bounds of the tiles seen are valid
+            if (qvalid) {
+                uint64_t* out = a.sample_lb + (int64_t)q * (gridDim.x * SAMPLE_M) +
+                                ((int64_t)cl * 2 + hh) * SAMPLE_M;
+#pragma unroll
+                for (int j = 0; j < SAMPLE_M; ++j)
+                    out[j] = lbs[j] > -INFINITY ? (uint64_t)f32_key(lbs[j]) << 32 : 0ull;
+            }
+        }
         int tail = 0;        // pairs this warp has queued in its ring (warp-uniform)
         int published = 0;   // of those, pairs whose tail the rescorers can see
         bool ring_ok = true;
-        for (int i = 0; i < my_tiles; ++i) {
+        for (int i = 0; !SAMPLE && i < my_tiles; ++i) {
             const int b = i & 1, e = i % MR_RING;
             // ---- accumulator ready -> the maxima of the four 32-column chunks
             if (!warp_wait(&ctl->acc_full[b], (i >> 1) & 1, abort, a.wait_ns)) {
@@ -591,7 +789,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
             // rare: re-read the hit chunks into per-chunk bit masks, release the
             // accumulator, and only then queue the (row, query) pairs, so that
             // queueing never holds up the next MMAs
-            const int64_t half_row0 = a.row_begin + ((int64_t)(cl + i * ncl) * 2 + hh) * PR;
+            const int64_t half_row0 = a.row_begin + (tile_of(i) * 2 + hh) * PR;
             uint32_t hb0 = 0, hb1 = 0, hb2 = 0, hb3 = 0;
             for (unsigned hm = hitmask; hm != 0u; hm &= hm - 1u) {
                 const int c = __ffs(hm) - 1;
@@ -666,7 +864,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
             __threadfence_block();
             st_volatile(&ctl->epi_done[ew], 1);   // after its last published pair
         }
-    } else if (warp == 2 || warp == 3 || warp == 6 || warp == 7) {
+    } else if (!SAMPLE && (warp == 2 || warp == 3 || warp == 6 || warp == 7)) {
         // ------------------------------------------------------- rescorers
         // Exact rescoring of the epilogue warps' pairs, off the accumulator
         // path.  The first CTA has three rescorers (warp 3 issues MMAs there),
@@ -681,7 +879,11 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
         for (int e4 = 0; e4 < RPR_MAX; ++e4) head[e4] = 0;
         uint64_t last = globaltimer_ns();
         uint64_t refreshed = 0;
-        for (;;) {
+        // the rescorers read this CTA's queries from Qs: wait for their landing
+        // here (its phase 0 completes once and for all)
+        const bool q_ok = warp_wait(&ctl->q_full, 0, abort, a.wait_ns);
+        if (!q_ok && lane == 0) set_abort(ctl, a.status, peer);
+        for (; q_ok;) {
             // thresholds raised by other clusters (shared through tau_global),
             // copied here every REFRESH_NS: rescorer c refreshes the CTA's query
             // blocks of 32 numbered c, c + nres, ...
@@ -740,7 +942,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
                         }
                     }
                 }
-                rescore_batch(ctl, ctl->hist[c], entry, valid, m, a);
+                rescore_batch(ctl, ctl->hist[c], entry, valid, m, a, Qs, q0);
                 progress = true;
             }
             if (progress) {
@@ -777,28 +979,21 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
 }
 
 
-// Seeds each query's pool with the exact top-k of the sample rows and sets
-// its starting threshold to the k-th of them.
-__global__ void seed_pool_kernel(const int64_t* __restrict__ seed_idx,
-                                 const float* __restrict__ seed_sc, int nq, int k,
-                                 uint64_t* __restrict__ pool, int pool_cap, int* __restrict__ cnt,
-                                 uint64_t* __restrict__ tau) {
+// Starting threshold of each query from the sample pass's lower bounds
+// (keys << 32, 0 = none): the k-th largest x of them bounds the shard's k-th
+// best exact score from below, and (key(x) << 32) is below the composite of
+// every row scoring >= x, so at least k composites exceed it.  Empties the
+// query's pool.  One block of 256 threads per query.
+__global__ void __launch_bounds__(256) sample_tau_kernel(const uint64_t* __restrict__ lb,
+                                                         int n_lb, int k,
+                                                         uint64_t* __restrict__ tau,
+                                                         int* __restrict__ cnt) {
+    __shared__ unsigned sm[300];
     const int q = blockIdx.x;
-    __shared__ int m;
-    if (threadIdx.x == 0) m = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < k; i += blockDim.x) {
-        const int64_t r = seed_idx[(int64_t)q * k + i];
-        if (r >= 0) {
-            pool[(int64_t)q * pool_cap + i] = make_cand(f32_key(seed_sc[(int64_t)q * k + i]),
-                                                        (uint32_t)r);
-            atomicAdd(&m, 1);
-        }
-    }
-    __syncthreads();
+    const uint64_t T = block_select_threshold(lb + (int64_t)q * n_lb, n_lb, k, sm);
     if (threadIdx.x == 0) {
-        cnt[q] = m;
-        tau[q] = m == k ? pool[(int64_t)q * pool_cap + k - 1] : 0ull;
+        tau[q] = T & 0xffffffff00000000ull;
+        cnt[q] = 0;
     }
 }
 
@@ -848,10 +1043,10 @@ hmm_status_t make_tmap_bf16(CUtensorMap* m, const void* base, int64_t rows, int 
 }
 
 struct TcLayout {
-    size_t pool, cnt, tau, status, seed_idx, seed_sc, seed_ws, total;
+    size_t pool, cnt, tau, status, sample_lb, total;
 };
 
-TcLayout tc_layout(int64_t n, int64_t nq_pass, int64_t k) {
+TcLayout tc_layout(int64_t nq_pass) {
     TcLayout L;
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
     size_t o = 0;
@@ -859,9 +1054,7 @@ TcLayout tc_layout(int64_t n, int64_t nq_pass, int64_t k) {
     L.cnt = o; o += up(sizeof(int) * nq_pass);
     L.tau = o; o += up(sizeof(uint64_t) * nq_pass);
     L.status = o; o += up(sizeof(int) * 4);
-    L.seed_idx = o; o += up(sizeof(int64_t) * nq_pass * k);
-    L.seed_sc = o; o += up(sizeof(float) * nq_pass * k);
-    L.seed_ws = o; o += up(flat_bf16_exact_ws_bytes(std::min<int64_t>(n, SEED_ROWS), nq_pass, k));
+    L.sample_lb = o; o += up(sizeof(uint64_t) * nq_pass * MAX_CTAS * SAMPLE_M);
     L.total = o;
     return L;
 }
@@ -870,13 +1063,14 @@ TcLayout tc_layout(int64_t n, int64_t nq_pass, int64_t k) {
 
 bool tc_path_applies(int64_t n, int64_t dim, int64_t nq, int64_t k, const void* mem,
                      const void* qry) {
-    return dim == TC_DIM && k >= 1 && k <= KMAX_TC && nq >= 1 && n > SEED_ROWS &&
+    return dim == TC_DIM && k >= 1 && k <= KMAX_TC && nq >= 1 && n > TC_MIN_ROWS &&
            (reinterpret_cast<uintptr_t>(mem) % 16) == 0 &&
            (reinterpret_cast<uintptr_t>(qry) % 16) == 0;
 }
 
 size_t tc_ws_bytes(int64_t n, int64_t nq, int64_t k) {
-    return tc_layout(n, std::min<int64_t>(nq, TC_NMAX), k).total + 256;
+    (void)n; (void)k;
+    return tc_layout(std::min<int64_t>(nq, TC_NMAX)).total + 256;
 }
 
 // Scores one shard on tensor cores and returns its exact top-k (int64 rows
@@ -890,16 +1084,17 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
                           void* ws, size_t ws_bytes, cudaStream_t st, int32_t* dev_status) {
     // tile coordinates (up to n + 255) stay int32
     HMM_REQUIRE(n < (int64_t(1) << 31) - 512, "n_rows must be < 2^31 - 512");
-    HMM_CUDA_TRY(cudaFuncSetAttribute(tc_score_select_kernel,
+    HMM_CUDA_TRY(cudaFuncSetAttribute(tc_score_select_kernel<false>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
-    const int64_t seed = std::min<int64_t>(n, SEED_ROWS);
+    HMM_CUDA_TRY(cudaFuncSetAttribute(tc_score_select_kernel<true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM));
     CUtensorMap tmR;
     hmm_status_t s = make_tmap_bf16(&tmR, mem, n, PR);
     if (s != HMM_OK) return s;
     const int sms = device_sm_count();
     for (int64_t q0 = 0; q0 < nq; q0 += TC_NMAX) {
         const int nqp_pass = (int)std::min<int64_t>(TC_NMAX, nq - q0);
-        const TcLayout L = tc_layout(n, nqp_pass, k);
+        const TcLayout L = tc_layout(nqp_pass);
         if (ws_bytes < L.total)
             return set_error(HMM_ERR_OOM, "workspace too small: %zu < %zu", ws_bytes, L.total);
         unsigned char* w = static_cast<unsigned char*>(ws);
@@ -907,33 +1102,23 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
         int* cnt = reinterpret_cast<int*>(w + L.cnt);
         uint64_t* tau = reinterpret_cast<uint64_t*>(w + L.tau);
         int* status = reinterpret_cast<int*>(w + L.status);
-        int64_t* seed_idx = reinterpret_cast<int64_t*>(w + L.seed_idx);
-        float* seed_sc = reinterpret_cast<float*>(w + L.seed_sc);
+        uint64_t* sample_lb = reinterpret_cast<uint64_t*>(w + L.sample_lb);
         const uint16_t* qp = qry + q0 * TC_DIM;
 
+        // empty pool slots read as 0 (below every key) in threshold raises
         HMM_CUDA_TRY(cudaMemsetAsync(pool, 0, sizeof(uint64_t) * nqp_pass * POOL_CAP, st));
         HMM_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int) * 4, st));
-        s = flat_bf16_exact(mem, seed, TC_DIM, qp, nqp_pass, k, 0, seed_idx, seed_sc,
-                            w + L.seed_ws, L.total - L.seed_ws, st);
-        if (s != HMM_OK) return s;
-        seed_pool_kernel<<<nqp_pass, 128, 0, st>>>(seed_idx, seed_sc, nqp_pass, (int)k, pool,
-                                                    POOL_CAP, cnt, tau);
-        s = check_launch("seed_pool_kernel");
-        if (s != HMM_OK) return s;
 
         CUtensorMap tmQ;
         s = make_tmap_bf16(&tmQ, qp, nqp_pass, PQ);
         if (s != HMM_OK) return s;
-        // One tensor-core pass over rows [seed, n), appending to the pools.  The
-        // pools start from the seed's exact top-k, and the rescorers refresh the
-        // shared threshold as candidates arrive, so one pass keeps hits sparse;
-        // passes over growing row prefixes, each reseeded from the exact top-k
-        // of the last, measured no faster at 8Mi-64Mi rows (slower below 32Mi).
         {
             TcArgs a;
             a.n_rows = n;
-            a.row_begin = seed;
-            a.n_tiles = (int)((n - seed + 2 * PR - 1) / (2 * PR));
+            a.row_begin = 0;
+            a.n_tiles = (int)((n + 2 * PR - 1) / (2 * PR));
+            a.sample_tiles = 0;
+            a.sample_lb = sample_lb;
             a.nq = nqp_pass;
             a.k = (int)k;
             a.pool_cap = POOL_CAP;
@@ -946,9 +1131,27 @@ hmm_status_t flat_bf16_tc(const uint16_t* mem, int64_t n, const uint16_t* qry, i
             a.status = status;
             a.wait_ns = wait_limit_ns();
             // clusters of two CTAs, one per pair of SMs
-            const int grid = 2 * std::max(1, std::min(sms / 2, a.n_tiles));
+            const int ncl_max = std::max(1, std::min(sms, MAX_CTAS) / 2);
+
+            // 1. sample pass: SAMPLE_TPC tiles per cluster spread over the shard
+            //    (all of them for small shards) -> lower bounds -> starting
+            //    thresholds, pools emptied
+            a.sample_tiles = std::min(a.n_tiles, SAMPLE_TPC * ncl_max);
+            const int grid_s = 2 * std::min(ncl_max, a.sample_tiles);
+            tc_score_select_kernel<true><<<grid_s, NTHREADS, TC_SMEM, st>>>(tmR, tmQ, a);
+            s = check_launch("tc_score_select_kernel<sample>");
+            if (s != HMM_OK) return s;
+            sample_tau_kernel<<<nqp_pass, 256, 0, st>>>(sample_lb, grid_s * SAMPLE_M, (int)k, tau,
+                                                        cnt);
+            s = check_launch("sample_tau_kernel");
+            if (s != HMM_OK) return s;
+
+            // 2. one scoring pass over every row, appending to the pools; the
+            //    rescorers raise and share the thresholds as candidates arrive
+            a.sample_tiles = 0;
+            const int grid = 2 * std::min(ncl_max, a.n_tiles);
             const ProfileMark pm = profile_begin(st);
-            tc_score_select_kernel<<<grid, NTHREADS, TC_SMEM, st>>>(tmR, tmQ, a);
+            tc_score_select_kernel<false><<<grid, NTHREADS, TC_SMEM, st>>>(tmR, tmQ, a);
             s = check_launch("tc_score_select_kernel");
             profile_end(pm, st);
             if (s != HMM_OK) return s;
