@@ -277,7 +277,8 @@ def run_ours(args, rank, world, local):
     if rank == 0:
         pk, pk_kind = peaks()
         # algorithmic work of one scoring-kernel launch: 2 x rows x dim FLOP per
-        # query over this rank's shard (the 8,192 seed rows included)
+        # query over this rank's shard (the scoring pass reads every row once;
+        # the short sample pass before it is not counted as algorithmic work)
         flop = 2.0 * per * DIM * N_QUERIES
         achieved = flop / (kern_ms * 1e-3) / 1e12
         peak_t = pk["bf16_tflops"]

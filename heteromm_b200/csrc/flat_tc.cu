@@ -97,6 +97,7 @@ constexpr int MR_RING = 8;                      // tiles of row bounds in flight
 static_assert(MR_RING >= STAGES + 2, "a row-bound slot is rewritten only after both epilogues read it");
 static_assert(N_RB_WARPS == 2, "the epilogue reads two row-bound slots per half");
 constexpr uint64_t REFRESH_NS = 2000;          // cadence of the rescorers' shared-threshold refresh
+constexpr uint64_t DRAIN_NS = 1000000;         // abort path: all of a producer's stage drains together
 
 struct __align__(8) Ctrl {
     uint64_t full[STAGES];          // this CTA's rows of tile i landed (TMA tx); in the first
@@ -515,10 +516,19 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
                 }
         }
         if (*abort) {
-            // drain: the latest arming of each stage must land before exit
+            // drain: the latest arming of each stage must land before exit.  In
+            // the first CTA a stage's phase also counts the peer's forwarded
+            // landing, which a forwarder that gave up never sends, so all the
+            // stages share one budget (a copy lands within microseconds; the
+            // budget is a thousand times that) instead of one each
+            const uint64_t t_end = globaltimer_ns() + DRAIN_NS;
+            auto left = [&]() -> uint64_t {
+                const uint64_t now = globaltimer_ns();
+                return now < t_end ? t_end - now : 0ull;
+            };
             for (int i = max(0, issued - STAGES); i < issued; ++i)
-                mbar_wait_drain(&ctl->full[i % STAGES], (i / STAGES) & 1);
-            mbar_wait_drain(&ctl->q_full, 0);
+                mbar_wait_drain(&ctl->full[i % STAGES], (i / STAGES) & 1, left());
+            mbar_wait_drain(&ctl->q_full, 0, left());
             // the pair MMAs already issued commit to this CTA's barriers after
             // they complete; their arrivals land well within this pause, before
             // the CTA can exit
