@@ -7,11 +7,12 @@
 // Tensor cores sum in their own order, so their scores are approximations.
 // The kernel uses them only to decide which (row, query) pairs can matter:
 //   s~ = tensor-core score of row r for query q (fp32 accumulate in TMEM)
-//   |s~ - s| <= EPS * max_j|a_rj| * sum_j|b_qj|   (s = the reference's score)
-// A pair is rescored exactly - fp32 multiply-add in ascending j over the row
-// (read back from L2, where it was just streamed), which rounds exactly as the
-// reference's separate multiply and add because bf16 products are exact in
-// fp32 - only when its upper bound s~ + margin reaches the query's current
+//   |s~ - s| <= EPS * max_j|a_rj| * sum_j|b_qj| + 2^-118   (s = the reference's
+//   score; the 2^-118 covers products below fp32's normal range, and a bound
+//   past 2^100, where partial sums may overflow, lets every pair through)
+// A pair is rescored exactly - the reference's separate fp32 multiply and add
+// in ascending j over the row (read back from L2, where it was just streamed)
+// - only when its upper bound s~ + margin reaches the query's current
 // threshold.  Exact (score, row) composites that beat the threshold enter a
 // per-query candidate pool in global memory; each time a pool reaches a
 // power-of-two fill mark, the warp that filled it computes the pool's k-th
@@ -144,6 +145,13 @@ struct TcArgs {
     uint64_t wait_ns;        // limit of every bounded wait (wait_limit_ns())
 };
 
+// EPS * M_h * L1_q (rounded up) plus 2^-118: products and partial sums below
+// fp32's normal range may be flushed or rounded differently by the tensor core,
+// at most 2^-126 each over 128 of them.
+__device__ __forceinline__ float tc_margin(float mh, float l1) {
+    return __fadd_ru(__fmul_ru(EPS, __fmul_ru(mh, l1)), 0x1p-118f);
+}
+
 __device__ __forceinline__ float tau_score(uint64_t t) {
     return t == 0ull ? -INFINITY : cand_score(t);
 }
@@ -155,12 +163,19 @@ __device__ __forceinline__ float max3_nan(float a, float b, float c) {
     return d;
 }
 
+// s + a * b with the product rounded first (no contraction into an FMA).
+__device__ __forceinline__ float mac_rn(float s, float a, float b) {
+    return __fadd_rn(s, __fmul_rn(a, b));
+}
+
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
 // The reference's fp32 dot product of a memory row and a query, j
-// ascending, both read from global memory (the row was just streamed and is
-// in L2; the queries are small and stay cached).
+// ascending, each product rounded before it is added (a fused multiply-add
+// would differ where a bf16 x bf16 product overflows fp32 or falls below its
+// normal range), both read from global memory (the row was just streamed and
+// is in L2; the queries are small and stay cached).
 __device__ __forceinline__ float exact_dot_rows(const uint16_t* __restrict__ row,
                                                 const uint16_t* __restrict__ qrow) {
     float s = 0.0f;
@@ -170,10 +185,10 @@ __device__ __forceinline__ float exact_dot_rows(const uint16_t* __restrict__ row
     for (int c = 0; c < 16; ++c) {
         const uint4 a = __ldg(rp + c);
         const uint4 b = __ldg(qp + c);
-        s = fmaf(bf_lo(a.x), bf_lo(b.x), s); s = fmaf(bf_hi(a.x), bf_hi(b.x), s);
-        s = fmaf(bf_lo(a.y), bf_lo(b.y), s); s = fmaf(bf_hi(a.y), bf_hi(b.y), s);
-        s = fmaf(bf_lo(a.z), bf_lo(b.z), s); s = fmaf(bf_hi(a.z), bf_hi(b.z), s);
-        s = fmaf(bf_lo(a.w), bf_lo(b.w), s); s = fmaf(bf_hi(a.w), bf_hi(b.w), s);
+        s = mac_rn(s, bf_lo(a.x), bf_lo(b.x)); s = mac_rn(s, bf_hi(a.x), bf_hi(b.x));
+        s = mac_rn(s, bf_lo(a.y), bf_lo(b.y)); s = mac_rn(s, bf_hi(a.y), bf_hi(b.y));
+        s = mac_rn(s, bf_lo(a.z), bf_lo(b.z)); s = mac_rn(s, bf_hi(a.z), bf_hi(b.z));
+        s = mac_rn(s, bf_lo(a.w), bf_lo(b.w)); s = mac_rn(s, bf_hi(a.w), bf_hi(b.w));
     }
     return s;
 }
@@ -193,10 +208,10 @@ __device__ __forceinline__ float exact_dot_staged_q(const uint16_t* __restrict__
     for (int c = 0; c < 16; ++c) {
         const uint4 b = *reinterpret_cast<const uint4*>(Qs + (c >> 3) * Q_BOX + ql * 128 +
                                                         (((c & 7) ^ (ql & 7)) << 4));
-        s = fmaf(bf_lo(a[c].x), bf_lo(b.x), s); s = fmaf(bf_hi(a[c].x), bf_hi(b.x), s);
-        s = fmaf(bf_lo(a[c].y), bf_lo(b.y), s); s = fmaf(bf_hi(a[c].y), bf_hi(b.y), s);
-        s = fmaf(bf_lo(a[c].z), bf_lo(b.z), s); s = fmaf(bf_hi(a[c].z), bf_hi(b.z), s);
-        s = fmaf(bf_lo(a[c].w), bf_lo(b.w), s); s = fmaf(bf_hi(a[c].w), bf_hi(b.w), s);
+        s = mac_rn(s, bf_lo(a[c].x), bf_lo(b.x)); s = mac_rn(s, bf_hi(a[c].x), bf_hi(b.x));
+        s = mac_rn(s, bf_lo(a[c].y), bf_lo(b.y)); s = mac_rn(s, bf_hi(a[c].y), bf_hi(b.y));
+        s = mac_rn(s, bf_lo(a[c].z), bf_lo(b.z)); s = mac_rn(s, bf_hi(a[c].z), bf_hi(b.z));
+        s = mac_rn(s, bf_lo(a[c].w), bf_lo(b.w)); s = mac_rn(s, bf_hi(a[c].w), bf_hi(b.w));
     }
     return s;
 }
@@ -683,7 +698,7 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
                     }
                 }
                 const float mh = fmaxf(__uint_as_float((uint32_t)v0), __uint_as_float((uint32_t)v1));
-                const float marg = __fmul_ru(EPS, __fmul_ru(mh, l1));
+                const float marg = tc_margin(mh, l1);
                 // |partial sums| <= M_h * L1_q <= 2^110: neither order overflows,
                 // so the error bound holds (a larger or NaN bound is skipped)
                 const bool use = qvalid && marg <= 0x1p100f;
@@ -789,8 +804,11 @@ tc_score_select_kernel(const __grid_constant__ CUtensorMap tmR,
             }
             const float mh = fmaxf(__uint_as_float((uint32_t)v0), __uint_as_float((uint32_t)v1));
             const float ts = tau_score(*reinterpret_cast<volatile uint64_t*>(&ctl->tau[q]));
+            const float marg = tc_margin(mh, l1);
+            // a margin past 2^100 means partial sums may overflow, where the
+            // bound does not hold: then every pair passes (-inf included)
             const float theta =
-                qvalid ? __fsub_rd(ts, __fmul_ru(EPS, __fmul_ru(mh, l1))) : INFINITY;
+                !qvalid ? INFINITY : (marg <= 0x1p100f ? __fsub_rd(ts, marg) : -INFINITY);
             // warp-uniform: chunks where some pair reaches theta (NaN passes)
             unsigned hitmask = (__any_sync(0xffffffffu, !(cm0 < theta)) ? 1u : 0u) |
                                (__any_sync(0xffffffffu, !(cm1 < theta)) ? 2u : 0u) |

@@ -45,8 +45,10 @@ struct BF16In {
     using T = uint16_t;
     static constexpr int VEC = 8;
     __device__ static float widen1(const uint16_t* p) { return bf16_bits_to_f32(*p); }
-    // bf16 x bf16 products are exact in fp32: fma rounds exactly as mul+add.
-    __device__ static float mac(float acc, float a, float b) { return fmaf(a, b, acc); }
+    // the product rounded before it is added, as the reference does: a bf16 x bf16
+    // product is exact in fp32 only inside its normal range, so a fused
+    // multiply-add would differ where a product overflows or underflows
+    __device__ static float mac(float acc, float a, float b) { return __fadd_rn(acc, __fmul_rn(a, b)); }
 };
 
 size_t fused_smem_bytes(int dim) {

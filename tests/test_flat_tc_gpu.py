@@ -62,6 +62,60 @@ def test_tc_large_magnitudes_and_zero_rows(cuda):
     assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
 
 
+def _nonfinite_rows(n):
+    """N(0,1) rows with a few +-inf rows, rows whose products overflow fp32,
+    NaN rows and +-0 rows."""
+    x = gen.normal_f32(101, (n, 128))
+    i = np.arange(n)
+    x[i % 997 == 3, 7] = np.nan
+    x[i % 20011 == 5, 11] = np.inf
+    x[i % 20021 == 6, 13] = -np.inf
+    x[i % 7919 == 7] *= np.float32(1e37)     # |products| past 3.4e38
+    x[i % 1031 == 9] = 0.0
+    x[i % 1033 == 10] = -0.0
+    return gen.bf16_bits(x)
+
+
+def test_tc_nonfinite_and_overflowing_rows(cuda):
+    """NaN rows (rank last), +-inf rows, rows whose bf16 x bf16 products
+    overflow fp32 (the reference rounds each product before adding it, so
+    inf - huge stays inf where a fused multiply-add would not) and +-0 rows,
+    on a shard larger than the sample pass covers, so that both passes meet
+    them; each query's top-100 holds infinite and finite scores."""
+    n, nq, k = 200_000, 16, 100
+    mem = _nonfinite_rows(n)
+    qry = gen.bf16_bits(gen.normal_f32(102, (nq, 128)) * np.float32(4.0))
+    idx, sc = run(cuda, mem, qry, k)
+    oidx, osc = O.ip_topk_bf16(mem, qry, k)
+    assert np.isinf(osc).any() and np.isfinite(osc).all(axis=1).sum() < nq
+    assert np.isfinite(osc[:, -1]).all()
+    assert np.array_equal(idx, oidx)
+    assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
+
+
+def test_product_overflow_against_a_large_partial_sum(cuda):
+    """Rows whose second product overflows fp32 while the partial sum before it
+    is large and of the other sign: -3e38 + (3e38 * 2).  The reference rounds
+    the product to +inf before adding it, so the score is +inf; a fused
+    multiply-add would keep it finite (3e38).  The tensor-core path (60,000
+    rows) and the CUDA-core path (8,192 rows) must both give the oracle's bits."""
+    k = 50
+    for n in (60_000, 8192):
+        x = gen.normal_f32(105, (n, 128))
+        rows = np.arange(16) * (n // 16) + 7
+        x[rows, 0] = -3.0e38
+        x[rows, 1] = 3.0e38
+        mem = gen.bf16_bits(x)
+        q = gen.normal_f32(106, (4, 128))
+        q[0, 0], q[0, 1] = 1.0, 2.0
+        qry = gen.bf16_bits(q)
+        idx, sc = run(cuda, mem, qry, k)
+        oidx, osc = O.ip_topk_bf16(mem, qry, k)
+        assert np.isposinf(osc[0, :16]).all() and np.array_equal(oidx[0, :16], rows)
+        assert np.array_equal(idx, oidx)
+        assert np.array_equal(sc.view(np.uint32), osc.view(np.uint32))
+
+
 def test_tc_sharded_merge(cuda):
     n, nq, k, shards = 80000, 32, 100, 4
     mem = gen.bf16_bits(gen.normal_f32(71, (n, 128)))
