@@ -309,7 +309,8 @@ def run_ours(args, rank, world, local):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t,
                          "unit": "TFLOP/s", "frac": achieved / peak_t,
                          "traffic": traffic_per_launch("tc_score_select_kernel", per),
-                         "kernel": "tc_score_select_kernel", "kernel_ms": kern_ms,
+                         "kernel": "tc_score_select_kernel<0> (the scoring pass)",
+                         "kernel_ms": kern_ms,
                          "kernel_launches_per_step": k_n / args.steps,
                          "peak_kind": f"{pk_kind} bf16 burst (cuBLAS 8192^3, best of 10): the "
                                       f"timed region is {ms * args.steps:.0f} ms",
