@@ -97,7 +97,9 @@ hmm_status_t hmm_ip_topk_f32(const float* mem, int64_t n_rows, int64_t dim,
  * accumulate: one shard of a row-sharded memory.  Row i of this shard has
  * global index row_offset + i; out_idx [n_queries][k] int64 global indices,
  * out_scores [n_queries][k] fp32 (required: the shard merge needs them).
- * Scores equal the reference's fp32 inner product of the widened values.
+ * Scores equal the reference's fp32 inner product of the widened values
+ * (j ascending, each product rounded before it is added, as its g++ build
+ * without FMA contraction does).
  * For dim == 128, k <= 128, n_rows > 8192 and 16-byte aligned pointers the
  * rows are scored on the tensor cores (tcgen05) and the candidates rescored
  * exactly; that path waits for `stream` before returning (it reads back the
