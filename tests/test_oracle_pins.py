@@ -135,6 +135,22 @@ def test_bm25_golden():
                    abs(sc[q][i] - sc[q][max(i - 1, 0)]) <= 1e-12 * abs(sc[q][i])
 
 
+def test_bf16_score_rounds_each_product():
+    """The oracle's bf16 score is the reference's loop `s += a * b` in fp32 with
+    no contraction: a product that overflows becomes +inf before it is added,
+    so -3e38 + 3e38 * 2 scores +inf (a fused multiply-add would give 3e38), and
+    an ordinary row keeps its plain sequential sum."""
+    mem = np.zeros((3, 128), np.float32)
+    mem[0, 0], mem[0, 1] = -3.0e38, 3.0e38
+    mem[1, :4] = [1.5, -2.0, 0.25, 8.0]
+    mem[2, 0], mem[2, 1] = 3.0e38, -3.0e38
+    q = np.zeros((1, 128), np.float32)
+    q[0, :4] = [1.0, 2.0, 4.0, 0.5]
+    idx, sc = O.ip_topk_bf16(gen.bf16_bits(mem), gen.bf16_bits(q), 3)
+    assert idx[0].tolist() == [0, 1, 2]
+    assert np.isposinf(sc[0, 0]) and sc[0, 1] == np.float32(2.5) and np.isneginf(sc[0, 2])
+
+
 def test_e4m3_decode_table():
     vals = O.e4m3_to_f32(np.arange(256, dtype=np.uint8))
     assert vals[0x38] == 1.0 and vals[0x7E] == 448.0 and vals[0xFE] == -448.0
