@@ -1,5 +1,5 @@
 """The multi-rank exchange of the sharded flat retrieval (heteromm_b200.shard)
-on gloo CPU ranks (world sizes 2 and 4): each rank takes its row range, computes its
+on gloo CPU ranks (world sizes 2, 4 and 8): each rank takes its row range, computes its
 local top-k with global indices (the oracle stands in for the GPU kernel),
 all-gathers and merges (the oracle's merge); every rank must hold the
 unsharded top-k."""
@@ -41,7 +41,8 @@ def _rank_main(rank, world, port, n, nq, k, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,n,nq,k", [(2, 20011, 8, 50), (2, 300, 3, 100), (4, 9001, 5, 64)])
+@pytest.mark.parametrize("world,n,nq,k", [(2, 20011, 8, 50), (2, 300, 3, 100), (4, 9001, 5, 64),
+                                         (8, 16007, 4, 100)])
 def test_sharded_topk_equals_unsharded(tmp_path, world, n, nq, k):
     sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
     import gen
