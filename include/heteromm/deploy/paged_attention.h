@@ -126,36 +126,41 @@ private:
     size_t top_k_ = 8;
 };
 
-// Fluent construction (reference paged_attention.h:198-260).
+// Fluent construction (reference paged_attention.h:198-260): the settings
+// collect in one struct, each with_* call overwrites one field, and build()
+// hands them all to the PagedAttention constructor.
 class PagedAttentionBuilder {
 public:
     PagedAttentionBuilder() = default;
     PagedAttentionBuilder& with_schedule_path(const std::string& path) {
-        schedule_path_ = path;
-        return *this;
+        return assign(&Settings::schedule_path, path);
     }
     PagedAttentionBuilder& with_projection_weight(const std::vector<std::vector<float>>& weight) {
-        projection_weight_ = weight;
-        return *this;
+        return assign(&Settings::projection_weight, weight);
     }
     PagedAttentionBuilder& with_page_size(size_t page_size) {
-        page_size_ = page_size;
-        return *this;
+        return assign(&Settings::page_size, page_size);
     }
-    PagedAttentionBuilder& with_top_k(size_t top_k) {
-        top_k_ = top_k;
-        return *this;
-    }
+    PagedAttentionBuilder& with_top_k(size_t top_k) { return assign(&Settings::top_k, top_k); }
     std::shared_ptr<PagedAttention> build() {
-        return std::make_shared<PagedAttention>(schedule_path_, projection_weight_, page_size_,
-                                                top_k_);
+        const Settings& c = settings_;
+        return std::make_shared<PagedAttention>(c.schedule_path, c.projection_weight, c.page_size,
+                                                c.top_k);
     }
 
 private:
-    std::string schedule_path_;
-    std::vector<std::vector<float>> projection_weight_;
-    size_t page_size_ = 16;
-    size_t top_k_ = 8;
+    struct Settings {
+        std::string schedule_path;
+        std::vector<std::vector<float>> projection_weight;
+        size_t page_size = 16;   // the reference's defaults
+        size_t top_k = 8;
+    };
+    template <typename Field, typename Value>
+    PagedAttentionBuilder& assign(Field Settings::*field, const Value& value) {
+        settings_.*field = value;
+        return *this;
+    }
+    Settings settings_;
 };
 
 inline PagedAttentionBuilder create_paged_attention() { return PagedAttentionBuilder(); }
